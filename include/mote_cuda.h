@@ -1,0 +1,191 @@
+/*
+ * mote_cuda.h -- C ABI of libmote_cuda.so, the B200 (sm_100a) CUDA data plane
+ * for Mote's Q4_0 linear and per-token layer kernels.
+ *
+ * This is the surface the empty `mote-backend-cuda` crate of RiversJin/mote
+ * (crates/mote-backend-cuda/src/lib.rs:1-3) binds.  It mirrors the extern "C"
+ * surface of the HIP backend (crates/mote-backend-hip/src/ffi.rs) name for
+ * name with the `mote_hip_` prefix replaced by `mote_cuda_`, with identical
+ * argument order, types and status conventions:
+ *
+ *   - every function returns an int status, 0 on success;
+ *   - runtime functions return the raw cudaError_t;
+ *   - kernel launchers validate their arguments before enqueueing anything
+ *     and return the same codes as the HIP shim they replace (1 = invalid
+ *     value, 9 = invalid configuration, -1 = the norm/RoPE shims' private
+ *     kInternalError), fully validated empty sizes return 0 without a launch,
+ *     and after a launch they return cudaGetLastError();
+ *   - pointers are untyped device pointers from mote_cuda_malloc (or any
+ *     cudaMalloc'd memory), streams are opaque cudaStream_t handles and every
+ *     kernel runs asynchronously on the stream it is given.
+ *
+ * Data formats: f16 is IEEE binary16 (uint16 bits), Q4_0 is the ggml block
+ * layout (per 32 elements: little-endian f16 scale d, then 16 bytes where
+ * byte j holds element j in its low nibble and element j+16 in its high
+ * nibble; value = (q - 8) * d), rows contiguous, K/32*18 bytes per row.
+ */
+#ifndef MOTE_CUDA_H
+#define MOTE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------- */
+/* Runtime shim: crates/mote-backend-hip/src/ffi.rs:42-61                   */
+/* ---------------------------------------------------------------------- */
+
+/* mote_hip_get_device_count (ffi.rs:43) */
+int mote_cuda_get_device_count(int* count);
+/* mote_hip_set_device (ffi.rs:44) */
+int mote_cuda_set_device(int ordinal);
+/* mote_hip_malloc (ffi.rs:45); allocations are 256-byte aligned */
+int mote_cuda_malloc(void** pointer, size_t bytes);
+/* mote_hip_free (ffi.rs:46) */
+int mote_cuda_free(void* pointer);
+/* mote_hip_memcpy_host_to_device (ffi.rs:47-51), synchronous */
+int mote_cuda_memcpy_host_to_device(void* destination, const void* source, size_t bytes);
+/* mote_hip_memcpy_device_to_host (ffi.rs:52-56), synchronous */
+int mote_cuda_memcpy_device_to_host(void* destination, const void* source, size_t bytes);
+/* mote_hip_stream_create (ffi.rs:57); non-blocking stream on the current device */
+int mote_cuda_stream_create(void** stream);
+/* mote_hip_stream_destroy (ffi.rs:58) */
+int mote_cuda_stream_destroy(void* stream);
+/* mote_hip_stream_synchronize (ffi.rs:59) */
+int mote_cuda_stream_synchronize(void* stream);
+/* mote_hip_mem_get_info (ffi.rs:60) */
+int mote_cuda_mem_get_info(size_t* free_bytes, size_t* total_bytes);
+
+/* Additions without a HIP counterpart: asynchronous copies, pinned host
+ * memory, events, the device status word and error strings. */
+int mote_cuda_memcpy_host_to_device_async(void* destination, const void* source, size_t bytes,
+                                          void* stream);
+int mote_cuda_memcpy_device_to_host_async(void* destination, const void* source, size_t bytes,
+                                          void* stream);
+int mote_cuda_memset_async(void* destination, int value, size_t bytes, void* stream);
+int mote_cuda_host_alloc(void** pointer, size_t bytes);
+int mote_cuda_host_free(void* pointer);
+int mote_cuda_event_create(void** event);
+int mote_cuda_event_destroy(void* event);
+int mote_cuda_event_record(void* event, void* stream);
+int mote_cuda_event_elapsed_ms(float* ms, void* start, void* end);
+/* Reads (clear != 0: and clears) the current device's status word.  Bit 0:
+ * a bounded device-side wait expired; bit 1: an index was out of range. */
+int mote_cuda_device_status(unsigned* status, int clear);
+const char* mote_cuda_status_string(int status);
+int mote_cuda_abi_version(void);
+
+/* ---------------------------------------------------------------------- */
+/* Q4_0 weight-only linear                                                 */
+/* ---------------------------------------------------------------------- */
+
+/* Replaces mote_hip_quantized_linear_q4_0_f16
+ * (crates/mote-backend-hip/src/quantized_linear.hip:56-91, bound at
+ * crates/mote-backend-hip/src/ffi.rs:294-302).
+ * output[rows, N] (f16) = input[rows, K] (f16) * weights[N, K] (Q4_0)^T with
+ * f32 accumulation.  Errors: any null pointer (stream included) or K % 32 != 0
+ * -> 1; rows*N beyond 32 bits -> 9; rows == 0 or N == 0 -> 0, no launch;
+ * K == 0 writes zeros. */
+int mote_cuda_quantized_linear_q4_0_f16(const void* input, const void* weights, void* output,
+                                        uint64_t rows, uint64_t output_features,
+                                        uint64_t input_features, void* stream);
+
+/* Same contract, f16 input and f32 output (the f32 accumulator unrounded).
+ * No HIP counterpart; same argument rules as the f16 entry point. */
+int mote_cuda_quantized_linear_q4_0_f16_f32out(const void* input, const void* weights,
+                                               void* output, uint64_t rows,
+                                               uint64_t output_features, uint64_t input_features,
+                                               void* stream);
+
+/* f32 input and f32 output: the device counterpart of mote-reference's
+ * quantized_linear_f32 (crates/mote-reference/src/quantized.rs:89-144) for
+ * Q4_0.  Same argument rules as the f16 entry point. */
+int mote_cuda_quantized_linear_q4_0_f32(const void* input, const void* weights, void* output,
+                                        uint64_t rows, uint64_t output_features,
+                                        uint64_t input_features, void* stream);
+
+/* Fused FFN gate/up projection with SwiGLU epilogue:
+ * output[rows, F] (f16) = silu(input * gate^T) * (input * up^T), with gate and
+ * up both Q4_0 [F, K].  No reference counterpart (SwiGLU is named only in
+ * docs/architecture.md:191); argument rules as the linear entry points. */
+int mote_cuda_q4_0_gate_up_swiglu_f16(const void* input, const void* gate_weights,
+                                      const void* up_weights, void* output, uint64_t rows,
+                                      uint64_t ffn_features, uint64_t input_features,
+                                      void* stream);
+
+/* Decodes Q4_0 [rows, K] to f32, bit-identical to mote-reference's
+ * dequantize_quantized_row (crates/mote-reference/src/quantized.rs:58-74). */
+int mote_cuda_q4_0_decode_f32(const void* weights, void* output, uint64_t rows,
+                              uint64_t input_features, void* stream);
+
+/* Encodes f32 [rows, K] (16-byte aligned) to Q4_0 with ggml's reference
+ * quantizer rule (d = signed absmax / -8, q = min(15, trunc(x/d + 8.5))).
+ * No reference counterpart: the reference builds blocks by hand
+ * (crates/mote-reference/tests/quantized_rows.rs:4-8). */
+int mote_cuda_q4_0_encode_f32(const void* input, void* weights, uint64_t rows,
+                              uint64_t input_features, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Per-token layer kernels                                                 */
+/* ---------------------------------------------------------------------- */
+
+/* Replaces mote_hip_rms_norm_f16 (crates/mote-backend-hip/src/rms_norm.hip:68-98,
+ * ffi.rs:126-134).  Row RMSNorm, f16 in/weight/out, f32 math.  Null -> -1;
+ * rows or hidden 0 -> 0; rows > 2^32-1 -> -1.  input may equal output. */
+int mote_cuda_rms_norm_f16(const void* input, const void* weight, void* output, uint64_t rows,
+                           uint64_t hidden_size, float epsilon, void* stream);
+
+/* Replaces mote_hip_fused_add_rms_norm_f16
+ * (crates/mote-backend-hip/src/fused_add_rms_norm.hip:99-138, ffi.rs:176-185).
+ * sum = input + residual (f32); output = norm(sum) * weight; residual <- f16(sum).
+ * Null, non-finite or negative epsilon, or output == residual -> -1. */
+int mote_cuda_fused_add_rms_norm_f16(const void* input, void* residual, const void* weight,
+                                     void* output, uint64_t rows, uint64_t hidden_size,
+                                     float epsilon, void* stream);
+
+/* Replaces mote_hip_rope_f16 (crates/mote-backend-hip/src/rope.hip:99-150,
+ * ffi.rs:230-241).  input/output [tokens, heads, head_dim] f16 (may alias),
+ * cos/sin [tokens, rotary_dim/2] f32; layout 0 = half-split, 1 = interleaved;
+ * the tail after rotary_dim is copied. */
+int mote_cuda_rope_f16(const void* input, const void* cos, const void* sin, void* output,
+                       uint64_t tokens, uint64_t heads, uint64_t head_dim, uint64_t rotary_dim,
+                       uint32_t layout, void* stream);
+
+/* Fused per-token layer kernel (no reference counterpart; composes the two
+ * entry points above): x_out = rms_norm(x) * gamma over [tokens, hidden], and
+ * q_out / k_out = RoPE of q [tokens, q_heads, head_dim] and
+ * k [tokens, kv_heads, head_dim] with rotary_dim == head_dim, in one launch. */
+int mote_cuda_rms_norm_rope_f16(const void* x, const void* gamma, void* x_out, const void* q,
+                                void* q_out, const void* k, void* k_out, const void* cos,
+                                const void* sin, uint64_t tokens, uint64_t hidden,
+                                uint64_t q_heads, uint64_t kv_heads, uint64_t head_dim,
+                                uint32_t layout, float epsilon, void* stream);
+
+/* out = silu(gate) * up, f16, silu(g) = g / (1 + exp(-g)) in f32.  No
+ * reference counterpart (docs/architecture.md:191 names the op). */
+int mote_cuda_swiglu_f16(const void* gate, const void* up, void* output, uint64_t n,
+                         void* stream);
+
+/* out[t, :] = table[ids[t], :] (f16, bit-exact); ids are int32.  Ids outside
+ * [0, vocab) produce a zero row and OR 2 into *error_flag (a device uint32 the
+ * caller zeroes and reads).  No reference counterpart. */
+int mote_cuda_embedding_gather_f16(const void* table, const void* ids, void* output,
+                                   uint64_t tokens, uint64_t vocab, uint64_t hidden,
+                                   void* error_flag, void* stream);
+
+/* cos/sin tables [tokens, rotary_dim/2] f32 for RoPE:
+ * angle = positions[t] * theta^(-2j/rotary_dim) in f64, rounded once.  The
+ * reference takes these tables as inputs (crates/mote-backend-hip/src/rope.rs:66-82)
+ * and has no generator. */
+int mote_cuda_rope_cos_sin_f32(const void* positions, void* cos_out, void* sin_out,
+                               uint64_t tokens, uint64_t rotary_dim, double theta,
+                               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOTE_CUDA_H */

@@ -1,0 +1,270 @@
+"""Device context, storage and tensors of the CUDA backend.
+
+Mirrors ``HipContext`` / ``HipStorage`` (crates/mote-backend-hip/src/
+context.rs:13-206, storage.rs:8-96) and ``mote_core::Tensor``
+(crates/mote-core/src/tensor.rs:5-117): a context owns one stream on one
+device plus every allocation made through it; tensors are a descriptor, a
+shared storage handle and a byte offset; the typed ops accept only
+contiguous, zero-offset tensors whose storage belongs to the context they
+are given.
+"""
+from __future__ import annotations
+
+import ctypes
+import itertools
+import threading
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import errors
+from ._native import lib
+from .types import TensorDesc
+
+STORAGE_ALIGNMENT = 256  # cudaMalloc guarantees 256-byte alignment (storage.rs:89-91)
+
+
+@dataclass(frozen=True)
+class Device:
+    """``mote_types::Device`` (crates/mote-types/src/device.rs:9-31)."""
+
+    backend: str
+    ordinal: int
+
+
+@dataclass(frozen=True)
+class MemoryInfo:
+    free_bytes: int
+    total_bytes: int
+
+
+class _ContextInner:
+    def __init__(self, ordinal: int):
+        self.ordinal = ordinal
+        self.device = Device("cuda", ordinal)
+        stream = ctypes.c_void_p()
+        errors.check(lib().mote_cuda_set_device(ordinal), "select device")
+        errors.check(lib().mote_cuda_stream_create(ctypes.byref(stream)), "create stream")
+        self.stream = stream.value
+        self._lock = threading.Lock()
+
+    def select(self) -> None:
+        errors.check(lib().mote_cuda_set_device(self.ordinal), "select device")
+
+    def close(self) -> None:
+        if self.stream:
+            lib().mote_cuda_set_device(self.ordinal)
+            lib().mote_cuda_stream_synchronize(self.stream)
+            lib().mote_cuda_stream_destroy(self.stream)
+            self.stream = None
+
+    def __del__(self):  # pragma: no cover - best effort at interpreter exit
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_storage_ids = itertools.count(1)
+
+
+class CudaStorage:
+    """One device allocation owned by a context (``HipStorage``)."""
+
+    def __init__(self, context: "_ContextInner", size_bytes: int, initial: bytes | None = None):
+        self.context = context
+        self.size_bytes = int(size_bytes)
+        self.id = next(_storage_ids)
+        self.alignment = STORAGE_ALIGNMENT
+        context.select()
+        ptr = ctypes.c_void_p()
+        errors.check(lib().mote_cuda_malloc(ctypes.byref(ptr), max(self.size_bytes, 1)),
+                     "allocate device storage")
+        self.pointer = ptr.value
+        if initial is not None and len(initial):
+            buf = np.frombuffer(initial, np.uint8) if not isinstance(initial, np.ndarray) \
+                else np.ascontiguousarray(initial).view(np.uint8).reshape(-1)
+            st = lib().mote_cuda_memcpy_host_to_device(self.pointer, buf.ctypes.data, buf.nbytes)
+            if st != 0:
+                lib().mote_cuda_free(self.pointer)
+                self.pointer = None
+                errors.check(st, "upload device storage")
+
+    def read_bytes(self) -> bytes:
+        if self.size_bytes == 0:
+            return b""
+        self.context.select()
+        errors.check(lib().mote_cuda_stream_synchronize(self.context.stream),
+                     "synchronize before readback")
+        out = np.empty(self.size_bytes, np.uint8)
+        errors.check(lib().mote_cuda_memcpy_device_to_host(out.ctypes.data, self.pointer,
+                                                           self.size_bytes), "read device storage")
+        return out.tobytes()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            if self.pointer:
+                lib().mote_cuda_set_device(self.context.ordinal)
+                lib().mote_cuda_free(self.pointer)
+                self.pointer = None
+        except Exception:
+            pass
+
+
+class TensorError(ValueError):
+    pass
+
+
+class Tensor:
+    """``mote_core::Tensor``: descriptor + shared storage + byte offset."""
+
+    def __init__(self, desc: TensorDesc, storage: CudaStorage, byte_offset: int = 0):
+        span = desc.required_span_bytes
+        if byte_offset > storage.size_bytes:
+            raise TensorError(f"OffsetOutOfBounds {byte_offset} > {storage.size_bytes}")
+        if byte_offset + span > storage.size_bytes:
+            raise TensorError(f"StorageTooSmall [{byte_offset}, {byte_offset + span}) > "
+                              f"{storage.size_bytes}")
+        if span and (storage.alignment < desc.required_alignment or
+                     byte_offset % desc.required_alignment):
+            raise TensorError("Misaligned")
+        self.desc = desc
+        self.storage = storage
+        self.byte_offset = int(byte_offset)
+
+    @property
+    def device(self) -> Device:
+        return self.storage.context.device
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        return self.desc.shape
+
+    @property
+    def pointer(self) -> int:
+        return self.storage.pointer + self.byte_offset
+
+    def shares_storage_with(self, other: "Tensor") -> bool:
+        return self.storage is other.storage
+
+    def __repr__(self) -> str:
+        return f"Tensor({self.desc.shape}, {self.desc.encoding!r}, storage={self.storage.id})"
+
+
+class CudaContext:
+    """``HipContext``: one device, one stream, owned allocations."""
+
+    def __init__(self, ordinal: int = 0):
+        if ordinal < 0 or ordinal > 0x7FFFFFFF:
+            raise errors.DeviceOrdinalTooLarge(ordinal=ordinal)
+        count = ctypes.c_int(0)
+        errors.check(lib().mote_cuda_get_device_count(ctypes.byref(count)), "enumerate devices")
+        if ordinal >= count.value:
+            raise errors.DeviceUnavailable(ordinal=ordinal, available=count.value)
+        self.inner = _ContextInner(ordinal)
+
+    # -- identity ---------------------------------------------------------
+    @property
+    def device(self) -> Device:
+        return self.inner.device
+
+    @property
+    def stream(self) -> int:
+        """The raw cudaStream_t handle every op of this context runs on."""
+        return self.inner.stream
+
+    # -- allocation -------------------------------------------------------
+    def _validate_desc(self, desc: TensorDesc) -> None:
+        if not desc.is_contiguous:
+            raise errors.UnsupportedLayout(actual=desc.layout)
+
+    def empty(self, desc: TensorDesc) -> Tensor:
+        self._validate_desc(desc)
+        return Tensor(desc, CudaStorage(self.inner, desc.required_span_bytes), 0)
+
+    def from_bytes(self, desc: TensorDesc, data) -> Tensor:
+        self._validate_desc(desc)
+        buf = np.ascontiguousarray(data).view(np.uint8).reshape(-1) \
+            if isinstance(data, np.ndarray) else np.frombuffer(bytes(data), np.uint8)
+        expected = desc.required_span_bytes
+        if buf.nbytes != expected:
+            raise errors.ByteLengthMismatch(expected=expected, actual=buf.nbytes)
+        return Tensor(desc, CudaStorage(self.inner, expected, buf), 0)
+
+    def from_numpy(self, desc: TensorDesc, array: np.ndarray) -> Tensor:
+        return self.from_bytes(desc, np.ascontiguousarray(array))
+
+    def read_bytes(self, tensor: Tensor) -> bytes:
+        storage = self.storage(tensor)
+        return storage.read_bytes()[: tensor.desc.required_span_bytes]
+
+    def read_numpy(self, tensor: Tensor, dtype) -> np.ndarray:
+        return np.frombuffer(self.read_bytes(tensor), dtype=dtype).reshape(tensor.shape) \
+            if tensor.desc.encoding.plain is not None else np.frombuffer(self.read_bytes(tensor),
+                                                                          np.uint8)
+
+    def sync(self) -> None:
+        self.inner.select()
+        errors.check(lib().mote_cuda_stream_synchronize(self.stream), "synchronize stream")
+
+    def memory_info(self) -> MemoryInfo:
+        self.inner.select()
+        free, total = ctypes.c_size_t(), ctypes.c_size_t()
+        errors.check(lib().mote_cuda_mem_get_info(ctypes.byref(free), ctypes.byref(total)),
+                     "query device memory info")
+        return MemoryInfo(free.value, total.value)
+
+    def device_status(self, clear: bool = True) -> int:
+        """Reads the device status word (bounded-wait timeouts, bad indices)."""
+        self.inner.select()
+        st = ctypes.c_uint(0)
+        errors.check(lib().mote_cuda_device_status(ctypes.byref(st), int(clear)),
+                     "read device status")
+        return st.value
+
+    # -- host transfers on the context stream -----------------------------
+    def upload_async(self, tensor: Tensor, host: "PinnedBuffer", nbytes: int | None = None):
+        n = tensor.desc.required_span_bytes if nbytes is None else nbytes
+        errors.check(lib().mote_cuda_memcpy_host_to_device_async(
+            tensor.pointer, host.pointer, n, self.stream), "upload (async)")
+
+    def download_async(self, host: "PinnedBuffer", tensor: Tensor, nbytes: int | None = None):
+        n = tensor.desc.required_span_bytes if nbytes is None else nbytes
+        errors.check(lib().mote_cuda_memcpy_device_to_host_async(
+            host.pointer, tensor.pointer, n, self.stream), "download (async)")
+
+    # -- ownership check used by every op (context.rs:150-176) --------------
+    def storage(self, tensor: Tensor) -> CudaStorage:
+        if tensor.device != self.device:
+            raise errors.DeviceMismatch(expected=self.device, actual=tensor.device)
+        if tensor.byte_offset != 0:
+            raise errors.UnsupportedByteOffset(byte_offset=tensor.byte_offset)
+        if not tensor.desc.is_contiguous:
+            raise errors.UnsupportedLayout(actual=tensor.desc.layout)
+        if not isinstance(tensor.storage, CudaStorage) or tensor.storage.context is not self.inner:
+            raise errors.WrongStorage()
+        return tensor.storage
+
+
+class PinnedBuffer:
+    """Page-locked host memory (cudaHostAlloc) viewed as a numpy array."""
+
+    def __init__(self, nbytes: int):
+        ptr = ctypes.c_void_p()
+        errors.check(lib().mote_cuda_host_alloc(ctypes.byref(ptr), max(int(nbytes), 1)),
+                     "allocate pinned host memory")
+        self.pointer = ptr.value
+        self.nbytes = int(nbytes)
+        raw = (ctypes.c_uint8 * max(self.nbytes, 1)).from_address(self.pointer)
+        self.array = np.frombuffer(raw, np.uint8)[: self.nbytes]
+
+    def view(self, dtype) -> np.ndarray:
+        return self.array.view(dtype)
+
+    def __del__(self):  # pragma: no cover
+        try:
+            if self.pointer:
+                lib().mote_cuda_host_free(self.pointer)
+                self.pointer = None
+        except Exception:
+            pass

@@ -1,0 +1,7 @@
+// Single translation unit of libmote_cuda.so.  The components are separate
+// files for reading; compiling them as one unit lets them share the
+// per-device status word without relocatable device code.
+#include "runtime.cu"
+#include "q4_0_linear.cu"
+#include "layer_ops.cu"
+#include "q4_0_codec.cu"

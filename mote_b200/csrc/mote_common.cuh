@@ -1,0 +1,154 @@
+// Shared device helpers for the Mote CUDA data plane (sm_100a).
+//
+// Inline PTX wrappers for the Blackwell/Hopper asynchronous machinery the
+// kernels use: mbarriers, 1-D bulk copies (global -> shared, no multicast),
+// warp-level mma.sync, and bounded waits.  Every wait in this library has an
+// iteration/time limit; on expiry it records an error code in a per-device
+// status word that the host reads with mote_cuda_device_status(), and the
+// kernel returns instead of spinning forever.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mote {
+
+// Status codes shared by every entry point.  Success is 0; the reference HIP
+// shims return hipErrorInvalidValue (1), hipErrorInvalidConfiguration (9) or
+// a private -1 ("kInternalError"), and the CUDA runtime uses the same numeric
+// values for cudaErrorInvalidValue / cudaErrorInvalidConfiguration.
+constexpr int kSuccess = 0;
+constexpr int kInternalError = -1;
+constexpr int kInvalidValue = static_cast<int>(cudaErrorInvalidValue);                    // 1
+constexpr int kInvalidConfiguration = static_cast<int>(cudaErrorInvalidConfiguration);    // 9
+
+// Device-side error codes recorded in g_device_status.
+constexpr unsigned kDevWaitTimeout = 1u;
+constexpr unsigned kDevIndexOutOfRange = 2u;
+
+constexpr std::uint64_t kMaxGridX = 0xffffffffULL;
+
+// Cycle budget for one bounded wait (~1 s at 2 GHz).
+constexpr long long kWaitCycles = 2000000000LL;
+
+__device__ __forceinline__ std::uint32_t smem_u32(const void* p) {
+    return static_cast<std::uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier -------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(std::uint64_t* bar, std::uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t parity) {
+    std::uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete.  Returns false (and
+// records kDevWaitTimeout in *status) if it has not completed within
+// kWaitCycles.
+__device__ __forceinline__ bool mbar_wait_bounded(std::uint64_t* bar, std::uint32_t parity,
+                                                  unsigned* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - start > kWaitCycles) {
+            if (status) atomicOr(status, kDevWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---- bulk copy (TMA engine, untiled, no multicast) -------------------------
+// Copies `bytes` (multiple of 16) from 16-byte aligned global memory to
+// 16-byte aligned shared memory and signals completion on `bar` via
+// complete_tx.  The L2 policy marks the streamed bytes evict-first so a
+// stream of weights does not push activations out of L2.
+__device__ __forceinline__ std::uint64_t l2_evict_first_policy() {
+    std::uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gmem,
+                                              std::uint32_t bytes, std::uint64_t* bar,
+                                              std::uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// ---- warp MMA --------------------------------------------------------------
+// D = A(16x16, f16, row) * B(16x8, f16, col) + C, f32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], std::uint32_t a0, std::uint32_t a1,
+                                          std::uint32_t a2, std::uint32_t a3, std::uint32_t b0,
+                                          std::uint32_t b1, const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+          "f"(c[2]), "f"(c[3]));
+}
+
+// (a & b) | c in one LOP3.
+__device__ __forceinline__ std::uint32_t and_or(std::uint32_t a, std::uint32_t b,
+                                                std::uint32_t c) {
+    std::uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ std::uint32_t prmt(std::uint32_t a, std::uint32_t b,
+                                              std::uint32_t sel) {
+    std::uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ std::uint32_t hsub2_u32(std::uint32_t a, std::uint32_t b) {
+    std::uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ float half_bits_to_float(std::uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+
+// Per-device status word (error codes from bounded waits / index checks).
+// The library is compiled as one translation unit (libmote_cuda.cu includes
+// every component), so this definition is unique.
+__device__ unsigned g_device_status = 0;
+
+}  // namespace mote
+
+#define MOTE_RETURN_IF_LAUNCH_FAILED() return static_cast<int>(cudaGetLastError())

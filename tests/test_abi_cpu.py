@@ -1,0 +1,136 @@
+"""C ABI checks that need no GPU.
+
+* the library loads and exports every function ``include/mote_cuda.h``
+  declares, and the Python binding declares the same set;
+* every launcher rejects invalid arguments with the reference shim's status
+  code before touching the device, and returns 0 for validated empty sizes
+  (these paths never reach the CUDA runtime, so they run on CPU hosts).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from mote_b200 import _native
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "mote_cuda.h"
+FAKE = 0x1000  # never dereferenced: every call below returns before launching
+STREAM = 0x2000
+
+
+def declared_symbols() -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return set(re.findall(r"\b(mote_cuda_\w+)\s*\(", text))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _native.lib()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    symbols = declared_symbols()
+    assert len(symbols) >= 30
+    for name in sorted(symbols):
+        assert hasattr(lib, name), name
+
+
+def test_python_binding_matches_header():
+    assert declared_symbols() == set(_native.SIGNATURES)
+
+
+def test_abi_version(lib):
+    assert lib.mote_cuda_abi_version() == 1
+
+
+LINEARS = ["mote_cuda_quantized_linear_q4_0_f16", "mote_cuda_quantized_linear_q4_0_f16_f32out",
+           "mote_cuda_quantized_linear_q4_0_f32"]
+
+
+@pytest.mark.parametrize("name", LINEARS)
+def test_linear_argument_rules(lib, name):
+    fn = getattr(lib, name)
+    # quantized_linear.hip:64-76: null pointers, stream included -> 1
+    assert fn(None, FAKE, FAKE, 1, 1, 32, STREAM) == 1
+    assert fn(FAKE, None, FAKE, 1, 1, 32, STREAM) == 1
+    assert fn(FAKE, FAKE, None, 1, 1, 32, STREAM) == 1
+    assert fn(FAKE, FAKE, FAKE, 1, 1, 32, None) == 1
+    # K not a multiple of 32 -> 1
+    assert fn(FAKE, FAKE, FAKE, 1, 1, 33, STREAM) == 1
+    # empty outputs -> 0 without a launch
+    assert fn(FAKE, FAKE, FAKE, 0, 5, 64, STREAM) == 0
+    assert fn(FAKE, FAKE, FAKE, 3, 0, 64, STREAM) == 0
+    # rows * N beyond 32 bits -> 9 (cudaErrorInvalidConfiguration)
+    assert fn(FAKE, FAKE, FAKE, 1 << 32, 1, 32, STREAM) == 9
+    assert fn(FAKE, FAKE, FAKE, 1 << 17, 1 << 17, 32, STREAM) == 9
+
+
+def test_gate_up_argument_rules(lib):
+    fn = lib.mote_cuda_q4_0_gate_up_swiglu_f16
+    assert fn(FAKE, FAKE, None, FAKE, 1, 8, 32, STREAM) == 1
+    assert fn(FAKE, FAKE, FAKE, FAKE, 1, 8, 33, STREAM) == 1
+    assert fn(FAKE, FAKE, FAKE, FAKE, 0, 8, 32, STREAM) == 0
+
+
+def test_rms_norm_argument_rules(lib):
+    fn = lib.mote_cuda_rms_norm_f16
+    eps = ctypes.c_float(1e-6)
+    # rms_norm.hip:166-174
+    assert fn(None, FAKE, FAKE, 1, 8, eps, STREAM) == -1
+    assert fn(FAKE, FAKE, FAKE, 1, 8, eps, None) == -1
+    assert fn(FAKE, FAKE, FAKE, 0, 8, eps, STREAM) == 0
+    assert fn(FAKE, FAKE, FAKE, 3, 0, eps, STREAM) == 0
+    assert fn(FAKE, FAKE, FAKE, 1 << 32, 8, eps, STREAM) == -1
+
+
+def test_fused_add_rms_norm_argument_rules(lib):
+    fn = lib.mote_cuda_fused_add_rms_norm_f16
+    # fused_add_rms_norm.hip:296-312
+    assert fn(FAKE, None, FAKE, FAKE, 1, 8, ctypes.c_float(1e-6), STREAM) == -1
+    for bad in (float("nan"), float("inf"), -1e-6):
+        assert fn(FAKE, 0x3000, FAKE, FAKE, 1, 8, ctypes.c_float(bad), STREAM) == -1
+    assert fn(FAKE, 0x3000, FAKE, 0x3000, 1, 8, ctypes.c_float(1e-6), STREAM) == -1
+    assert fn(FAKE, 0x3000, FAKE, FAKE, 0, 8, ctypes.c_float(1e-6), STREAM) == 0
+
+
+def test_rope_argument_rules(lib):
+    fn = lib.mote_cuda_rope_f16
+    # rope.hip:436-457
+    assert fn(None, FAKE, FAKE, FAKE, 1, 1, 4, 4, 0, STREAM) == -1
+    assert fn(FAKE, None, FAKE, FAKE, 1, 1, 4, 4, 0, STREAM) == -1
+    assert fn(FAKE, FAKE, FAKE, FAKE, 1, 1, 4, 4, 2, STREAM) == -1  # unknown layout
+    assert fn(FAKE, FAKE, FAKE, FAKE, 1, 1, 4, 3, 0, STREAM) == -1  # odd rotary_dim
+    assert fn(FAKE, FAKE, FAKE, FAKE, 1, 1, 4, 6, 0, STREAM) == -1  # rotary_dim > head_dim
+    assert fn(FAKE, FAKE, FAKE, FAKE, 0, 3, 8, 8, 0, STREAM) == 0
+    assert fn(FAKE, FAKE, FAKE, FAKE, 2, 0, 8, 8, 0, STREAM) == 0
+    assert fn(FAKE, FAKE, FAKE, FAKE, 1 << 31, 4, 8, 8, 0, STREAM) == -1
+
+
+def test_rope_zero_rotary_dim_accepts_null_tables(lib):
+    # rotary_dim == 0 is a pure copy; null tables are tolerated (rope.hip:439-444)
+    # but we still must not launch here: zero tokens.
+    assert lib.mote_cuda_rope_f16(FAKE, None, None, FAKE, 0, 1, 4, 0, 0, STREAM) == 0
+
+
+def test_new_op_argument_rules(lib):
+    assert lib.mote_cuda_swiglu_f16(None, FAKE, FAKE, 8, STREAM) == -1
+    assert lib.mote_cuda_swiglu_f16(FAKE, FAKE, FAKE, 0, STREAM) == 0
+    assert lib.mote_cuda_embedding_gather_f16(FAKE, FAKE, FAKE, 1, 8, 8, None, STREAM) == -1
+    assert lib.mote_cuda_embedding_gather_f16(FAKE, FAKE, FAKE, 0, 8, 8, FAKE, STREAM) == 0
+    assert lib.mote_cuda_q4_0_decode_f32(FAKE, FAKE, 1, 33, STREAM) == 1
+    assert lib.mote_cuda_q4_0_encode_f32(FAKE + 4, FAKE, 1, 32, STREAM) == 1  # unaligned input
+    assert lib.mote_cuda_rope_cos_sin_f32(FAKE, FAKE, FAKE, 1, 3, ctypes.c_double(1e4),
+                                          STREAM) == -1
+    eps = ctypes.c_float(1e-6)
+    assert lib.mote_cuda_rms_norm_rope_f16(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE,
+                                           0, 64, 1, 1, 64, 0, eps, STREAM) == 0
+    assert lib.mote_cuda_rms_norm_rope_f16(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE,
+                                           1, 64, 1, 1, 64, 5, eps, STREAM) == -1
+
+
+def test_status_strings(lib):
+    assert b"invalid" in lib.mote_cuda_status_string(-1).lower()
+    assert lib.mote_cuda_status_string(1)

@@ -1,0 +1,223 @@
+"""GPU parity of the Q4_0 linear against the CPU oracle (mote-reference restated).
+
+Mirrors crates/mote-backend-hip/tests/quantized_linear.rs (fixtures,
+tolerance abs 0.01 / rel 0.002 against the f16-rounded f32 oracle, empty
+outputs, K == 0, aliasing and encoding validation) and adds the BASELINE
+shapes with seeded N(0, 0.02) Q4_0 weights and N(0, 1) activations.
+
+Bounds asserted, with ``checker`` metrics against a float64 accumulation of
+the decoded weights:
+* f16 outputs: element-wise relative error (floor rms) <= 1e-3 -- the f16
+  output rounding alone contributes up to 4.9e-4;
+* f32 outputs: element-wise relative error (floor rms) <= 1e-5.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import checker
+from tests import _fixtures as fx
+
+pytestmark = pytest.mark.gpu
+
+from mote_b200 import errors, ops  # noqa: E402
+from mote_b200.context import CudaContext  # noqa: E402
+from mote_b200.types import DType, QuantFormat, plain, quantized  # noqa: E402
+
+F16_BOUND = 1e-3
+F32_BOUND = 1e-5
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    return CudaContext(0)
+
+
+def run_linear(ctx, x, w_bytes, m, n, k, in_dtype=DType.F16, out_dtype=DType.F16):
+    np_in = np.float16 if in_dtype is DType.F16 else np.float32
+    np_out = np.float16 if out_dtype is DType.F16 else np.float32
+    xt = ctx.from_bytes(plain((m, k), in_dtype), np.asarray(x, np_in))
+    wt = ctx.from_bytes(quantized((n, k)), np.asarray(w_bytes, np.uint8))
+    yt = ctx.empty(plain((m, n), out_dtype))
+    ops.quantized_linear_q4_0(ctx, xt, wt, yt, in_dtype, out_dtype)
+    out = np.frombuffer(ctx.read_bytes(yt), np_out).astype(np.float32).reshape(m, n)
+    assert ctx.device_status() == 0
+    return out
+
+
+def oracle_linear(oracle_ref, x_f32, w_bytes, m, n, k):
+    threads = min(8, max(1, oracle_ref.host_threads()))
+    return oracle_ref.quantized_linear_f32(x_f32, w_bytes, oracle_ref.Q4_0, m, n, k,
+                                           threads=threads).reshape(m, n)
+
+
+def test_reference_fixture_3x5x64(ctx, oracle_lib):
+    """quantized_linear.rs:13-62, verbatim fixture and tolerance (generic path)."""
+    rows, n, k = 3, 5, 64
+    x = fx.hip_linear_input(rows, k)
+    w = fx.hip_linear_weights(n, k)
+    wt = ctx.from_bytes(quantized((n, k)), w)
+    assert ctx.read_bytes(wt) == w.tobytes()  # bytes stay as uploaded
+    got = run_linear(ctx, x, w, rows, n, k)
+    want = checker.f16_round(oracle_linear(oracle_lib, x.astype(np.float32), w, rows, n, k))
+    ok, bad = checker.within_reference_tolerance(got, want, 0.01, 0.002)
+    assert ok, (bad, got.reshape(-1)[bad], want.reshape(-1)[bad])
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9, 16, 17, 33, 64, 70])
+@pytest.mark.parametrize("n,k", [(40, 256), (2048, 2048), (96, 1280)])
+def test_fast_path_matches_oracle(ctx, oracle_lib, m, n, k):
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=1000 + n + k)
+    x = fx.activations(m, k, seed=7 + m).astype(np.float16)
+    got = run_linear(ctx, x, w, m, n, k)
+    x32 = x.astype(np.float32)
+    want32 = oracle_linear(oracle_lib, x32, w, m, n, k)
+    ok, bad = checker.within_reference_tolerance(got, checker.f16_round(want32), 0.01, 0.002)
+    assert ok, bad
+    ref64 = checker.linear_f64(x32, checker.q4_0_dequant_np(w, n, k))
+    assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND
+    assert checker.rel_err_normwise(got, ref64) <= F16_BOUND
+
+
+@pytest.mark.parametrize("m", [1, 3, 4, 5, 16])
+def test_f32_activations_keep_full_precision(ctx, oracle_lib, m):
+    """Config 1 (M=1, K=N=2048) and neighbours: f32 in, f32 out."""
+    n, k = 2048, 2048
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=11)
+    x = fx.activations(m, k, seed=12)
+    got = run_linear(ctx, x, w, m, n, k, DType.F32, DType.F32)
+    want32 = oracle_linear(oracle_lib, x, w, m, n, k)
+    ref64 = checker.linear_f64(x, checker.q4_0_dequant_np(w, n, k))
+    assert checker.rel_err_elementwise(got, ref64) <= F32_BOUND
+    assert checker.rel_err_elementwise(want32, ref64) <= F32_BOUND
+    ok, bad = checker.within_reference_tolerance(got, want32, 1e-5, 1e-5)
+    assert ok, bad
+
+
+def test_f32_output_variant(ctx, oracle_lib):
+    m, n, k = 4, 1024, 4096
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=21)
+    x = fx.activations(m, k, seed=22).astype(np.float16)
+    got = run_linear(ctx, x, w, m, n, k, DType.F16, DType.F32)
+    ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w, n, k))
+    assert checker.rel_err_elementwise(got, ref64) <= F32_BOUND
+
+
+@pytest.mark.parametrize("n", [4096, 11008, 14336])
+@pytest.mark.parametrize("m", [1, 16])
+def test_config3_batch_decode_shapes(ctx, oracle_lib, m, n):
+    """Config 3 at full size (K=4096), against the f32 oracle and f64."""
+    k = 4096
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=300 + n)
+    x = fx.activations(m, k, seed=301 + m).astype(np.float16)
+    got = run_linear(ctx, x, w, m, n, k)
+    ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w, n, k))
+    assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND
+    want32 = oracle_linear(oracle_lib, x.astype(np.float32), w, m, n, k)
+    ok, bad = checker.within_reference_tolerance(got, checker.f16_round(want32), 0.01, 0.002)
+    assert ok, bad
+
+
+def test_reference_bench_fixture_sampled(ctx, oracle_lib):
+    """benches/quantized_linear.rs:89-126 validation of 3 sampled outputs."""
+    rows, n, k = 16, 4096, 4096
+    w = fx.hip_bench_weights(n, k)
+    x = fx.hip_bench_input(rows, k)
+    got = run_linear(ctx, x, w, rows, n, k)
+    rb = (k // 32) * 18
+    for row, of in [(0, 0), (rows // 2, n // 3), (rows - 1, n - 1)]:
+        dec = oracle_lib.dequantize_quantized_row(w[of * rb:(of + 1) * rb], oracle_lib.Q4_0, k)
+        exp = np.float32(0)
+        for inner in range(k):
+            exp = np.float32(exp + np.float32(x[row, inner]) * dec[inner])
+        exp = float(np.float16(exp))
+        assert abs(got[row, of] - exp) <= max(0.25, abs(exp) * 0.005)
+
+
+def test_gate_up_swiglu_fused(ctx, oracle_lib):
+    m, f, k = 3, 1000, 2048
+    wg = fx.q4_0_weights(oracle_lib, f, k, seed=41)
+    wu = fx.q4_0_weights(oracle_lib, f, k, seed=42)
+    x = fx.activations(m, k, seed=43).astype(np.float16)
+    xt = ctx.from_bytes(plain((m, k), DType.F16), x)
+    gt = ctx.from_bytes(quantized((f, k)), wg)
+    ut = ctx.from_bytes(quantized((f, k)), wu)
+    yt = ctx.empty(plain((m, f), DType.F16))
+    ops.q4_0_gate_up_swiglu_f16(ctx, xt, gt, ut, yt)
+    got = np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(m, f)
+    x32 = x.astype(np.float32)
+    g64 = checker.linear_f64(x32, checker.q4_0_dequant_np(wg, f, k))
+    u64 = checker.linear_f64(x32, checker.q4_0_dequant_np(wu, f, k))
+    ref = checker.swiglu_f64(g64, u64)
+    assert checker.rel_err_elementwise(got, ref) <= 2e-3
+    assert checker.rel_err_normwise(got, ref) <= 1e-3
+
+
+def test_empty_outputs_return_without_launch(ctx):
+    """quantized_linear.rs:124-140."""
+    xt = ctx.from_bytes(plain((0, 32), DType.F16), b"")
+    wt = ctx.from_bytes(quantized((2, 32)), fx.hip_linear_weights(2, 32))
+    yt = ctx.empty(plain((0, 2), DType.F16))
+    ops.quantized_linear_q4_0_f16(ctx, xt, wt, yt)
+    assert ctx.read_bytes(yt) == b""
+
+
+def test_zero_input_features_writes_zeros(ctx):
+    """quantized_linear.rs:142-158."""
+    xt = ctx.from_bytes(plain((3, 0), DType.F16), b"")
+    wt = ctx.from_bytes(quantized((2, 0)), b"")
+    yt = ctx.from_bytes(plain((3, 2), DType.F16), np.full(6, 7.0, np.float16))
+    ops.quantized_linear_q4_0_f16(ctx, xt, wt, yt)
+    assert np.all(np.frombuffer(ctx.read_bytes(yt), np.float16) == 0)
+
+
+def test_validates_geometry_encoding_and_aliasing(ctx):
+    """quantized_linear.rs:64-122."""
+    x = ctx.from_bytes(plain((1, 32), DType.F16), np.zeros(32, np.float16))
+    w = ctx.from_bytes(quantized((32, 32)), fx.hip_linear_weights(32, 32))
+    y = ctx.empty(plain((1, 32), DType.F16))
+    with pytest.raises(errors.AliasedStorage) as e:
+        ops.quantized_linear_q4_0_f16(ctx, x, w, x)
+    assert (e.value.tensor, e.value.other) == ("output", "input")
+    from mote_b200.context import Tensor
+
+    y_on_w = Tensor(plain((1, 32), DType.F16), w.storage, 0)
+    with pytest.raises(errors.AliasedStorage) as e:
+        ops.quantized_linear_q4_0_f16(ctx, x, w, y_on_w)
+    assert (e.value.tensor, e.value.other) == ("output", "weights")
+    q8 = ctx.from_bytes(quantized((32, 32), QuantFormat.Q8_0), np.zeros(32 * 34, np.uint8))
+    with pytest.raises(errors.UnsupportedEncoding):
+        ops.quantized_linear_q4_0_f16(ctx, x, q8, y)
+    short = ctx.from_bytes(quantized((32, 64)), fx.hip_linear_weights(32, 64))
+    with pytest.raises(errors.ShapeMismatch) as e:
+        ops.quantized_linear_q4_0_f16(ctx, x, short, y)
+    assert e.value.tensor == "weights"
+    other = CudaContext(0)
+    y2 = other.empty(plain((1, 32), DType.F16))
+    with pytest.raises(errors.WrongStorage):
+        ops.quantized_linear_q4_0_f16(ctx, x, w, y2)
+
+
+def test_unaligned_weights_use_generic_path(ctx, oracle_lib):
+    """A weight tensor that is not 16-byte aligned still computes correctly."""
+    n, k = 24, 512
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=5)
+    x = fx.activations(2, k, seed=6).astype(np.float16)
+    from mote_b200.context import CudaStorage, Tensor
+
+    storage = CudaStorage(ctx.inner, w.nbytes + 2, np.concatenate([np.zeros(2, np.uint8), w]))
+    wt = Tensor(quantized((n, k)), storage, 2)
+    xt = ctx.from_bytes(plain((2, k), DType.F16), x)
+    yt = ctx.empty(plain((2, n), DType.F16))
+    # The typed API only takes zero-offset tensors (context.rs:150-176) ...
+    with pytest.raises(errors.UnsupportedByteOffset):
+        ops.quantized_linear_q4_0_f16(ctx, xt, wt, yt)
+    # ... the C ABI takes any pointer.
+    from mote_b200._native import lib
+
+    assert lib().mote_cuda_quantized_linear_q4_0_f16(xt.pointer, wt.pointer, yt.pointer, 2, n, k,
+                                                     ctx.stream) == 0
+    got = np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(2, n)
+    ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w, n, k))
+    assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND

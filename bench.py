@@ -135,6 +135,10 @@ class Bench:
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(self.local_rank)
         self.dev = torch.device("cuda", self.local_rank)
+        # The C ABI (like the reference shim) rejects the null stream, which is
+        # torch's default stream handle: run everything on an explicit stream.
+        self.main_stream = torch.cuda.Stream(device=self.dev)
+        torch.cuda.set_stream(self.main_stream)
         from mote_b200 import _native
 
         self.lib = _native.lib()
@@ -583,8 +587,70 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def run_single_case(args) -> None:
+    """One kernel, a few plain launches (no graph): the command ncu profiles.
+
+    --only gemv       Q4_0 linear f16 -> f16, [--m, --n, --k]
+    --only norm_rope  fused RMSNorm + RoPE at config-2 geometry
+    """
+    import torch
+
+    b = Bench(args)
+    torch = b.torch
+    times = []
+    if args.only == "gemv":
+        m, n, k = args.m, args.n, args.k
+        w = b.encode_q4_0(n, k, seed=1)
+        x = b.randn((m, k), 2, torch.float16)
+        y = torch.empty((m, n), dtype=torch.float16, device=b.dev)
+
+        def launch():
+            b.check(b.lib.mote_cuda_quantized_linear_q4_0_f16(
+                x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "gemv")
+        nbytes = linear_bytes(m, n, k)
+    elif args.only == "norm_rope":
+        t, hidden, qh, kh, hd = 512, 2048, 32, 8, 64
+        pos = torch.arange(t, dtype=torch.int32, device=b.dev)
+        cos = torch.empty((t, hd // 2), dtype=torch.float32, device=b.dev)
+        sin = torch.empty_like(cos)
+        b.check(b.lib.mote_cuda_rope_cos_sin_f32(pos.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                                 t, hd, ctypes.c_double(10000.0), b.stream()),
+                "table")
+        xs = b.randn((t, hidden), 1, torch.float16)
+        gamma = b.randn((hidden,), 3, torch.float16, 0.1, 1.0)
+        q = b.randn((t, qh, hd), 4, torch.float16)
+        kk = b.randn((t, kh, hd), 5, torch.float16)
+        xo, qo, ko = torch.empty_like(xs), torch.empty_like(q), torch.empty_like(kk)
+
+        def launch():
+            b.check(b.lib.mote_cuda_rms_norm_rope_f16(
+                xs.data_ptr(), gamma.data_ptr(), xo.data_ptr(), q.data_ptr(), qo.data_ptr(),
+                kk.data_ptr(), ko.data_ptr(), cos.data_ptr(), sin.data_ptr(), t, hidden, qh, kh,
+                hd, 0, ctypes.c_float(1e-6), b.stream()), "norm_rope")
+        nbytes = (2 * t * hidden + 2 * t * qh * hd + 2 * t * kh * hd) * 2 + hidden * 2 + \
+            2 * t * (hd // 2) * 4
+    else:
+        raise SystemExit(f"unknown --only {args.only}")
+    for _ in range(args.launches):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        launch()
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    best = min(times)
+    print(json.dumps({"only": args.only, "launches": args.launches, "best_us": round(best * 1e3, 2),
+                      "gbs_at_best": round(nbytes / best / 1e6, 1), "bytes": nbytes}), flush=True)
+
+
 def main() -> int:
     p = argparse.ArgumentParser()
+    p.add_argument("--only", default=None, help="profile one kernel: gemv | norm_rope")
+    p.add_argument("--m", type=int, default=1)
+    p.add_argument("--n", type=int, default=128256)
+    p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--launches", type=int, default=3)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
@@ -595,6 +661,9 @@ def main() -> int:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+        return 0
+    if args.only:
+        run_single_case(args)
         return 0
     from mote_b200 import build as _b
 

@@ -121,7 +121,7 @@ int mote_cuda_q4_0_gate_up_swiglu_f16(const void* input, const void* gate_weight
 int mote_cuda_q4_0_decode_f32(const void* weights, void* output, uint64_t rows,
                               uint64_t input_features, void* stream);
 
-/* Encodes f32 [rows, K] (16-byte aligned) to Q4_0 with ggml's reference
+/* Encodes f32 [rows, K] (16-byte aligned) into 2-byte aligned Q4_0 with ggml's reference
  * quantizer rule (d = signed absmax / -8, q = min(15, trunc(x/d + 8.5))).
  * No reference counterpart: the reference builds blocks by hand
  * (crates/mote-reference/tests/quantized_rows.rs:4-8). */

@@ -229,61 +229,13 @@ __global__ void __launch_bounds__(256) rope_kernel(const __half* input,
 // ---- fused RMSNorm + RoPE (one CTA per token) --------------------------------
 // Normalizes x[token] (hidden) and rotates q[token] (q_heads x HD) and
 // k[token] (kv_heads x HD) with the token's cos/sin row; rotary_dim == HD.
-// A thread owns 8 consecutive elements of a head; for the half-split layout
-// the partner of element e < HD/2 is e + HD/2, which lives in the thread
-// HD/16 lanes away (same warp for HD <= 256).
-template <int HD>
-__device__ __forceinline__ void rope_row_vec(const __half* in, __half* out,
-                                             const float* __restrict__ cs,
-                                             const float* __restrict__ sn, std::uint32_t nvec,
-                                             int layout) {
-    constexpr int kLanesPerHead = HD / 8;
-    constexpr int kHalfLanes = kLanesPerHead / 2;
-    for (std::uint32_t base = 0; base < nvec; base += blockDim.x) {
-        const std::uint32_t v = base + threadIdx.x;
-        const bool active = v < nvec;
-        H8 x;
-        if (active) x.u = reinterpret_cast<const uint4*>(in)[v];
-        else x.u = make_uint4(0, 0, 0, 0);
-        const int pos = (v % kLanesPerHead) * 8;  // element offset within the head
-        H8 o;
-        if (layout == kLayoutHalfSplit) {
-            H8 partner;
-            partner.u.x = __shfl_xor_sync(0xffffffffu, x.u.x, kHalfLanes);
-            partner.u.y = __shfl_xor_sync(0xffffffffu, x.u.y, kHalfLanes);
-            partner.u.z = __shfl_xor_sync(0xffffffffu, x.u.z, kHalfLanes);
-            partner.u.w = __shfl_xor_sync(0xffffffffu, x.u.w, kHalfLanes);
-            const bool first = pos < HD / 2;
-            const int j0 = first ? pos : pos - HD / 2;
-            if (active) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float c = cs[j0 + j];
-                    const float s = sn[j0 + j];
-                    float o1, o2;
-                    if (first) {
-                        rotate(__half2float(x.h[j]), __half2float(partner.h[j]), c, s, o1, o2);
-                        o.h[j] = __float2half_rn(o1);
-                    } else {
-                        rotate(__half2float(partner.h[j]), __half2float(x.h[j]), c, s, o1, o2);
-                        o.h[j] = __float2half_rn(o2);
-                    }
-                }
-            }
-        } else if (active) {
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-                const int pair = (pos + j) / 2;
-                float o1, o2;
-                rotate(__half2float(x.h[j]), __half2float(x.h[j + 1]), cs[pair], sn[pair], o1,
-                       o2);
-                o.h[j] = __float2half_rn(o1);
-                o.h[j + 1] = __float2half_rn(o2);
-            }
-        }
-        if (active) reinterpret_cast<uint4*>(out)[v] = o.u;
-    }
-}
+// Every load of the token (q, k and x rows, 16 bytes per thread per vector)
+// is issued before any arithmetic, so the CTA pays one memory latency.  A
+// thread owns 8 consecutive elements of a head; for the half-split layout
+// the partner of element e < HD/2 is e + HD/2, held by the thread HD/16
+// lanes away (q/k rows are whole heads, so partners never cross rows).
+constexpr int kRopeVecPerThread = 2;   // (q_heads + kv_heads) * HD / 8 <= 512
+constexpr int kNormVecPerThread = 4;   // hidden <= 8192
 
 template <int HD>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_rope_kernel(
@@ -292,45 +244,106 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_rope_kernel(
     const float* __restrict__ sin, std::uint64_t hidden, std::uint32_t q_heads,
     std::uint32_t kv_heads, float eps, int layout) {
     __shared__ float scratch[kNormThreads / 32];
+    constexpr int kLanesPerHead = HD / 8;
+    constexpr int kHalfLanes = kLanesPerHead / 2;
     const std::uint64_t token = blockIdx.x;
-    constexpr std::uint32_t kHalf = HD / 2;
-    const float* cs = cos + token * kHalf;
-    const float* sn = sin + token * kHalf;
-    // Issue the RoPE rows first: their loads overlap the norm's reduction.
-    rope_row_vec<HD>(q + token * q_heads * HD, q_out + token * q_heads * HD, cs, sn,
-                     q_heads * HD / 8, layout);
-    rope_row_vec<HD>(k + token * kv_heads * HD, k_out + token * kv_heads * HD, cs, sn,
-                     kv_heads * HD / 8, layout);
-    // RMSNorm of x[token]: up to 4 vectors of 8 per thread (hidden <= 8192).
-    const uint4* in = reinterpret_cast<const uint4*>(x + token * hidden);
-    uint4* out = reinterpret_cast<uint4*>(x_out + token * hidden);
-    const uint4* wv = reinterpret_cast<const uint4*>(gamma);
-    const std::uint32_t nvec = static_cast<std::uint32_t>(hidden / 8);
-    H8 xv[4];
-    float ss = 0.f;
+    const std::uint32_t qn = q_heads * HD / 8;
+    const std::uint32_t rn = qn + kv_heads * HD / 8;
+    const std::uint32_t xn = static_cast<std::uint32_t>(hidden / 8);
+    const uint4* qv = reinterpret_cast<const uint4*>(q + token * q_heads * HD);
+    const uint4* kv = reinterpret_cast<const uint4*>(k + token * kv_heads * HD);
+    const uint4* xv = reinterpret_cast<const uint4*>(x + token * hidden);
+
+    H8 r[kRopeVecPerThread];
+    H8 xr[kNormVecPerThread];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kRopeVecPerThread; ++i) {
         const std::uint32_t v = threadIdx.x + i * kNormThreads;
-        if (v < nvec) {
-            xv[i].u = in[v];
+        r[i].u = v < qn ? qv[v] : (v < rn ? kv[v - qn] : make_uint4(0, 0, 0, 0));
+    }
+#pragma unroll
+    for (int i = 0; i < kNormVecPerThread; ++i) {
+        const std::uint32_t v = threadIdx.x + i * kNormThreads;
+        xr[i].u = v < xn ? xv[v] : make_uint4(0, 0, 0, 0);
+    }
+
+    // RoPE of the q and k rows.
+    const float* cs = cos + token * (HD / 2);
+    const float* sn = sin + token * (HD / 2);
+#pragma unroll
+    for (int i = 0; i < kRopeVecPerThread; ++i) {
+        const std::uint32_t v = threadIdx.x + i * kNormThreads;
+        const int pos = (v % kLanesPerHead) * 8;  // element offset within the head
+        H8 o;
+        if (layout == kLayoutHalfSplit) {
+            H8 partner;
+            partner.u.x = __shfl_xor_sync(0xffffffffu, r[i].u.x, kHalfLanes);
+            partner.u.y = __shfl_xor_sync(0xffffffffu, r[i].u.y, kHalfLanes);
+            partner.u.z = __shfl_xor_sync(0xffffffffu, r[i].u.z, kHalfLanes);
+            partner.u.w = __shfl_xor_sync(0xffffffffu, r[i].u.w, kHalfLanes);
+            const bool first = pos < HD / 2;
+            const int j0 = first ? pos : pos - HD / 2;
+            const float4 c0 = *reinterpret_cast<const float4*>(cs + j0);
+            const float4 c1 = *reinterpret_cast<const float4*>(cs + j0 + 4);
+            const float4 s0 = *reinterpret_cast<const float4*>(sn + j0);
+            const float4 s1 = *reinterpret_cast<const float4*>(sn + j0 + 4);
+            const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const float f = __half2float(xv[i].h[j]);
-                ss = __fadd_rn(ss, __fmul_rn(f, f));
+                float o1, o2;
+                if (first) {
+                    rotate(__half2float(r[i].h[j]), __half2float(partner.h[j]), cc[j], ss[j], o1,
+                           o2);
+                    o.h[j] = __float2half_rn(o1);
+                } else {
+                    rotate(__half2float(partner.h[j]), __half2float(r[i].h[j]), cc[j], ss[j], o1,
+                           o2);
+                    o.h[j] = __float2half_rn(o2);
+                }
+            }
+        } else {
+            const float4 c0 = *reinterpret_cast<const float4*>(cs + pos / 2);
+            const float4 s0 = *reinterpret_cast<const float4*>(sn + pos / 2);
+            const float cc[4] = {c0.x, c0.y, c0.z, c0.w};
+            const float ss[4] = {s0.x, s0.y, s0.z, s0.w};
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                float o1, o2;
+                rotate(__half2float(r[i].h[j]), __half2float(r[i].h[j + 1]), cc[j / 2], ss[j / 2],
+                       o1, o2);
+                o.h[j] = __float2half_rn(o1);
+                o.h[j + 1] = __float2half_rn(o2);
             }
         }
+        if (v < qn)
+            reinterpret_cast<uint4*>(q_out + token * q_heads * HD)[v] = o.u;
+        else if (v < rn)
+            reinterpret_cast<uint4*>(k_out + token * kv_heads * HD)[v - qn] = o.u;
     }
-    const float inv = inv_rms(block_sum(ss, scratch), hidden, eps);
+
+    // RMSNorm of x[token].
+    float ssq = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kNormVecPerThread; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float f = __half2float(xr[i].h[j]);
+            ssq = __fadd_rn(ssq, __fmul_rn(f, f));
+        }
+    const float inv = inv_rms(block_sum(ssq, scratch), hidden, eps);
+    uint4* out = reinterpret_cast<uint4*>(x_out + token * hidden);
+    const uint4* wv = reinterpret_cast<const uint4*>(gamma);
+#pragma unroll
+    for (int i = 0; i < kNormVecPerThread; ++i) {
         const std::uint32_t v = threadIdx.x + i * kNormThreads;
-        if (v < nvec) {
+        if (v < xn) {
             H8 w, o;
             w.u = __ldg(&wv[v]);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-                o.h[j] = __float2half_rn(
-                    norm_out(__half2float(xv[i].h[j]), inv, __half2float(w.h[j])));
+                o.h[j] = __float2half_rn(norm_out(__half2float(xr[i].h[j]), inv,
+                                                  __half2float(w.h[j])));
             out[v] = o.u;
         }
     }
@@ -506,8 +519,10 @@ extern "C" int mote_cuda_rms_norm_rope_f16(const void* x, const void* gamma, voi
     if (tokens == 0) return kSuccess;
     if (tokens > kMaxGridX) return kInternalError;
     auto s = static_cast<cudaStream_t>(stream);
-    const bool vec = hidden % 8 == 0 && hidden > 0 && hidden <= 256 * 8 * 4 &&
-                     (head_dim == 64 || head_dim == 128) && aligned16(x) && aligned16(gamma) &&
+    const bool vec = hidden % 8 == 0 && hidden > 0 && hidden <= 256 * 8 * kNormVecPerThread &&
+                     (head_dim == 64 || head_dim == 128) &&
+                     (q_heads + kv_heads) * head_dim / 8 <= 256ull * kRopeVecPerThread &&
+                     aligned16(cos) && aligned16(sin) && aligned16(x) && aligned16(gamma) &&
                      aligned16(x_out) && aligned16(q) && aligned16(q_out) && aligned16(k) &&
                      aligned16(k_out) && q_heads <= 0xffffffffull && kv_heads <= 0xffffffffull;
     if (!vec) {

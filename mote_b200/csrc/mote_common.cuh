@@ -106,17 +106,58 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gm
         : "memory");
 }
 
+// Same copy with the default L2 policy (for data many CTAs re-read).
+__device__ __forceinline__ void bulk_copy_g2s_default(void* dst_smem, const void* src_gmem,
+                                                      std::uint32_t bytes, std::uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- per-thread async copies (cp.async, 16 bytes, bypassing L1) ----------
+__device__ __forceinline__ void cp_async_16(std::uint32_t dst_smem, const void* src_gmem,
+                                            std::uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst_smem),
+                 "l"(src_gmem), "l"(policy)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's committed groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---- warp MMA --------------------------------------------------------------
 // D = A(16x16, f16, row) * B(16x8, f16, col) + C, f32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], std::uint32_t a0, std::uint32_t a1,
                                           std::uint32_t a2, std::uint32_t a3, std::uint32_t b0,
                                           std::uint32_t b1, const float (&c)[4]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
           "f"(c[2]), "f"(c[3]));
+}
+
+// Shared-memory loads at a 32-bit shared address (register + immediate).
+// volatile keeps them after the mbarrier wait that publishes the data.
+__device__ __forceinline__ std::uint32_t lds32(std::uint32_t addr) {
+    std::uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(std::uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
 }
 
 // (a & b) | c in one LOP3.

@@ -58,17 +58,22 @@ __global__ void __launch_bounds__(256) q4_0_encode_kernel(const float* __restric
         }
         const float d = __fdiv_rn(mx, -8.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-        std::uint8_t* blk = w + b * 18;
-        blk[0] = static_cast<std::uint8_t>(dh & 0xFF);
-        blk[1] = static_cast<std::uint8_t>(dh >> 8);
+        // The 18-byte block is 2-byte aligned: write it as nine 16-bit words
+        // (little endian: scale first, then quant bytes 2j, 2j+1 per word).
+        unsigned short* blk = reinterpret_cast<unsigned short*>(w + b * 18);
+        blk[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const float x0 = __fmul_rn(v[j], id);
-            const float x1 = __fmul_rn(v[j + 16], id);
-            const int q0 = min(15, __float2int_rz(__fadd_rn(x0, 8.5f)));
-            const int q1 = min(15, __float2int_rz(__fadd_rn(x1, 8.5f)));
-            blk[2 + j] = static_cast<std::uint8_t>(q0 | (q1 << 4));
+        for (int j = 0; j < 16; j += 2) {
+            unsigned pair = 0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float x0 = __fmul_rn(v[j + h], id);
+                const float x1 = __fmul_rn(v[j + h + 16], id);
+                const int q0 = min(15, __float2int_rz(__fadd_rn(x0, 8.5f)));
+                const int q1 = min(15, __float2int_rz(__fadd_rn(x1, 8.5f)));
+                pair |= static_cast<unsigned>(q0 | (q1 << 4)) << (8 * h);
+            }
+            blk[1 + j / 2] = static_cast<unsigned short>(pair);
         }
     }
 }
@@ -120,12 +125,14 @@ extern "C" int mote_cuda_q4_0_decode_f32(const void* weights, void* output, std:
 }
 
 // Encodes a [rows, input_features] f32 matrix into Q4_0 blocks.  The input
-// must be 16-byte aligned (float4 loads).
+// must be 16-byte aligned (float4 loads) and the output 2-byte aligned (the
+// Q4_0 storage alignment of crates/mote-types/src/lib.rs:68-74).
 extern "C" int mote_cuda_q4_0_encode_f32(const void* input, void* weights, std::uint64_t rows,
                                          std::uint64_t input_features, void* stream) {
     if (input == nullptr || weights == nullptr || stream == nullptr) return kInvalidValue;
     if (input_features % 32 != 0) return kInvalidValue;
     if (reinterpret_cast<std::uintptr_t>(input) % 16 != 0) return kInvalidValue;
+    if (reinterpret_cast<std::uintptr_t>(weights) % 2 != 0) return kInvalidValue;
     if (rows == 0 || input_features == 0) return kSuccess;
     if (rows > (~0ull) / input_features) return kInvalidConfiguration;
     const std::uint64_t blocks = rows * (input_features / 32);

@@ -1,4 +1,4 @@
-// Q4_0 weight-only linear for decode and small batches (M <= 64).
+// Q4_0 weight-only linear for decode and small batches.
 //
 //   y[m, n] = sum_k x[m, k] * w[n, k],   w stored as ggml Q4_0 blocks:
 //   18 bytes per 32 elements = f16 scale d (little endian) + 16 bytes, byte j
@@ -6,30 +6,37 @@
 //   value = (q - 8) * d.  (crates/mote-types/src/lib.rs:48-74,
 //   crates/mote-reference/src/quantized.rs:177-201.)
 //
-// Design (B200):
-// * A CTA owns one tile of 16 weight rows and splits K over its 4 warps.
-//   Each warp streams its K-slice of the 16 rows into its own 4-slot shared
-//   memory ring with 1-D bulk copies (cp.async.bulk, TMA engine), one copy
-//   per row per stage, completion tracked by an mbarrier per slot.  Weights
-//   are read from HBM exactly once, in 144/288-byte contiguous runs.
-// * The dequantization happens in registers: each lane decodes one 4-byte
-//   quant word per row per block into exact f16 integers (q - 8) with a
-//   PRMT + LOP3 + HSUB2 sequence (1024+q / 64+q exponent tricks), and the
-//   warp issues mma.sync.m16n8k16 (f16 x f16 -> f32) with weights as the A
-//   operand and up to 8 activation tokens per n8 tile as B.  The per-block
-//   f16 scale is applied to the f32 block partial with FFMA, so products and
-//   scaling are exact and only f32 accumulation rounds.
-// * The k-slot permutation inside each 16-wide MMA is chosen so a lane's B
-//   fragment is 4 consecutive activations (one 8-byte load) and its A
-//   fragment comes from one 4-byte quant word.  The permutation is the same
-//   for A and B, so the dot product is unchanged.
-// * f32 activations are split into f16 hi + lo parts placed in adjacent MMA
-//   columns, which keeps their full precision (error ~2^-22 relative).
-// * Cross-warp reduction of the four K-slices goes through shared memory.
+// Design (B200, HBM-bound):
+// * Persistent kernel: one 8-warp CTA per SM walks over tiles of 16 weight
+//   rows.  Every warp owns a fixed K-slice of every tile and streams its
+//   slice of the 16 rows through a private shared-memory ring with 1-D bulk
+//   copies (cp.async.bulk on the TMA engine, one copy per row per stage,
+//   completion on an mbarrier per slot, L2 evict-first).  The ring runs
+//   continuously across tiles, so the copy pipeline never drains; weights
+//   are read from HBM exactly once in 144/288-byte contiguous runs.
+// * The activations (up to 16 rows, f16) are staged into shared memory once
+//   per CTA, with padded rows that make the fragment loads bank-conflict
+//   free.
+// * Dequantization happens in registers: each lane decodes one 4-byte quant
+//   word per row per block into exact f16 integers (q - 8) with PRMT + LOP3
+//   + HSUB2 (the 1024+q / 64+q exponent tricks), and the warp issues
+//   mma.sync.m16n8k16 (f16 x f16 -> f32) with the weights as the A operand
+//   and 8 activation rows per n8 tile as B.  The f16 block scale multiplies
+//   the f32 block partial (FFMA): products and scaling are exact, only the
+//   f32 accumulation rounds.
+// * The k-slot permutation inside each 16-wide MMA makes a lane's B
+//   fragment 4 consecutive activations (one 8-byte load) and its A fragment
+//   one 4-byte quant word; A and B share the permutation, so the dot product
+//   is unchanged.
+// * f32 activations are split into f16 hi + lo rows (adjacent MMA columns),
+//   keeping their full precision (error ~2^-22 relative).
+// * The eight K-slice partials of a tile meet in a double-buffered shared
+//   reduction area behind one named barrier; the warps take turns writing
+//   finished tiles, so the others keep streaming.
 //
-// K must be a multiple of 256 (so a row is a whole number of 144-byte,
-// 16-byte-aligned groups of 8 blocks) and the weights 16-byte aligned; other
-// shapes use the generic warp-per-row kernel at the end of this file.
+// Fast-path requirements: K a multiple of 256 (whole 144-byte, 16-byte
+// aligned groups of 8 blocks per row), 16-byte aligned weights and
+// activations.  Other shapes use the generic warp-per-row kernel.
 
 #include "mote_common.cuh"
 
@@ -38,17 +45,20 @@
 namespace mote {
 namespace q4 {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTileRows = 16;
-constexpr int kStages = 4;
 constexpr int kUnitBlocks = 8;            // 8 blocks = 256 elements = 144 bytes
 constexpr int kUnitBytes = kUnitBlocks * 18;
-constexpr int kStageUnits = 2;            // up to 16 blocks per stage
-constexpr int kRowStride = kStageUnits * kUnitBytes + 16;  // 304: padded, bank-conflict free
-constexpr int kStageBytes = kTileRows * kRowStride;         // 4864
-constexpr int kWarpRingBytes = kStages * kStageBytes;       // 19456
-constexpr int kSmemBytes = kWarps * kWarpRingBytes + kWarps * kStages * 8;
+constexpr int kStageUnits = 1;            // 8 blocks per stage
+// Padded row stride: 176 / 4 = 44 words = 12 (mod 32) banks apart, so the 8
+// rows a warp reads at once land in 8 disjoint groups of 4 banks.
+constexpr int kRowStride = kStageUnits * kUnitBytes + 32;  // 176
+constexpr int kStageBytes = kTileRows * kRowStride;         // 2816
+constexpr int kMaxSmem = 232448;                            // 227 KB per-CTA opt-in limit
+constexpr int kSmemPerSm = 233472;                          // 228 KB per SM
+constexpr int kSmemReservedPerCta = 1024;                   // system use per resident CTA
+constexpr int kMaxXRows = 16;                               // two n8 tiles
 
 enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1 };
 
@@ -57,25 +67,42 @@ struct Params {
     const std::uint8_t* w;    // [N, K/32*18]
     const std::uint8_t* w2;   // second matrix (up projection) for kEpiSwiGLU
     void* y;                  // [M, ldy] f16 or f32
-    std::uint32_t M;
+    std::uint32_t M;          // tokens in this launch
     std::uint32_t N;          // rows of w (and of w2)
     std::uint64_t K;
     std::uint64_t pitch;      // bytes per weight row
     std::uint32_t units;      // K / 256
+    std::uint32_t tiles;      // row tiles
     std::uint64_t ldy;        // output row stride (elements)
+    std::uint32_t x_rows;     // activation rows in shared memory (M, or 2M for f32)
+    std::uint32_t x_stride;   // bytes per shared activation row (2K + 32)
+    std::uint32_t x_bytes;    // (x_zero_row + 1) * x_stride rounded up to 128
+    std::uint32_t x_zero_row; // index of the all-zero row after the staged rows
 };
 
-__device__ __forceinline__ void decode_word(std::uint32_t u, std::uint32_t& lo01,
-                                            std::uint32_t& lo23, std::uint32_t& hi01,
-                                            std::uint32_t& hi23) {
-    const std::uint32_t v = prmt(u, 0u, 0x4140u);  // [B0, 0, B1, 0]
-    const std::uint32_t w = prmt(u, 0u, 0x4342u);  // [B2, 0, B3, 0]
+__host__ __device__ constexpr int red_bytes(int nt) { return 2 * kWarps * nt * 4 * 32 * 4; }
+
+__host__ __device__ constexpr int smem_bytes(int x_bytes, int nt, int stages) {
+    return x_bytes + kWarps * stages * kStageBytes + red_bytes(nt);
+}
+
+// Quant word u = bytes B0..B3 = qs[4t .. 4t+3] of a block.  Its low
+// nibbles are elements 4t..4t+3, its high nibbles 16+4t..16+4t+3.  The two
+// f16 halves of a register take the nibbles of bytes (B0, B2) or (B1, B3):
+//   lo02 = (q[4t],    q[4t+2])       lo13 = (q[4t+1],    q[4t+3])
+//   hi02 = (q[16+4t], q[16+4t+2])    hi13 = (q[16+4t+1], q[16+4t+3])
+// and the activations are staged in the matching order (elements 1 and 2
+// of every group of 4 swapped), so no byte shuffles are needed here.
+__device__ __forceinline__ void decode_word(std::uint32_t u, std::uint32_t& lo02,
+                                            std::uint32_t& lo13, std::uint32_t& hi02,
+                                            std::uint32_t& hi13) {
+    const std::uint32_t v = u >> 8;
     // low nibbles: f16(1024 + q) - 1032 = q - 8 (exact)
-    lo01 = hsub2_u32(and_or(v, 0x000F000Fu, 0x64006400u), 0x64086408u);
-    lo23 = hsub2_u32(and_or(w, 0x000F000Fu, 0x64006400u), 0x64086408u);
+    lo02 = hsub2_u32(and_or(u, 0x000F000Fu, 0x64006400u), 0x64086408u);
+    lo13 = hsub2_u32(and_or(v, 0x000F000Fu, 0x64006400u), 0x64086408u);
     // high nibbles sit at mantissa bits 4..7: f16(64 + q) - 72 = q - 8 (exact)
-    hi01 = hsub2_u32(and_or(v, 0x00F000F0u, 0x54005400u), 0x54805480u);
-    hi23 = hsub2_u32(and_or(w, 0x00F000F0u, 0x54005400u), 0x54805480u);
+    hi02 = hsub2_u32(and_or(u, 0x00F000F0u, 0x54005400u), 0x54805480u);
+    hi13 = hsub2_u32(and_or(v, 0x00F000F0u, 0x54005400u), 0x54805480u);
 }
 
 __device__ __forceinline__ std::uint32_t pack_half2(float lo, float hi) {
@@ -83,196 +110,39 @@ __device__ __forceinline__ std::uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const std::uint32_t*>(&h);
 }
 
-// B fragments (b0,b1 for the low-nibble MMA; c0,c1 for the high-nibble MMA)
-// for one 32-element block, for one n8 tile.
-template <bool XF32>
-__device__ __forceinline__ void load_b(const Params& p, int tile, int g, int t,
-                                       std::uint64_t kelem, std::uint32_t (&b)[4]) {
-    if constexpr (!XF32) {
-        const std::uint32_t m = tile * 8 + g;
-        if (m < p.M) {
-            const __half* xr = static_cast<const __half*>(p.x) + m * p.K + kelem + 4 * t;
-            const uint2 a = __ldg(reinterpret_cast<const uint2*>(xr));
-            const uint2 c = __ldg(reinterpret_cast<const uint2*>(xr + 16));
-            b[0] = a.x;
-            b[1] = a.y;
-            b[2] = c.x;
-            b[3] = c.y;
-        } else {
-            b[0] = b[1] = b[2] = b[3] = 0u;
-        }
-    } else {
-        // Column g of the tile holds token tile*4 + g/2; even columns carry
-        // the f16 rounding of x, odd columns the f16 rounding of the rest.
-        const std::uint32_t m = tile * 4 + (g >> 1);
-        if (m < p.M) {
-            const float* xr = static_cast<const float*>(p.x) + m * p.K + kelem + 4 * t;
-            float4 a = __ldg(reinterpret_cast<const float4*>(xr));
-            float4 c = __ldg(reinterpret_cast<const float4*>(xr + 16));
-            if (g & 1) {
-                a.x -= __half2float(__float2half_rn(a.x));
-                a.y -= __half2float(__float2half_rn(a.y));
-                a.z -= __half2float(__float2half_rn(a.z));
-                a.w -= __half2float(__float2half_rn(a.w));
-                c.x -= __half2float(__float2half_rn(c.x));
-                c.y -= __half2float(__float2half_rn(c.y));
-                c.z -= __half2float(__float2half_rn(c.z));
-                c.w -= __half2float(__float2half_rn(c.w));
-            }
-            b[0] = pack_half2(a.x, a.y);
-            b[1] = pack_half2(a.z, a.w);
-            b[2] = pack_half2(c.x, c.y);
-            b[3] = pack_half2(c.z, c.w);
-        } else {
-            b[0] = b[1] = b[2] = b[3] = 0u;
-        }
-    }
-}
-
-// One Q4_0 block for rows g and g+8: decoded A fragments plus scales,
-// multiplied into every n8 tile.
-template <int NT, bool XF32>
-__device__ __forceinline__ void block_mma(const Params& p, std::uint32_t qg, std::uint32_t qg8,
-                                          float dg, float dg8, std::uint64_t kelem, int g, int t,
-                                          float (&acc)[NT][4]) {
-    std::uint32_t al01, al23, ah01, ah23, bl01, bl23, bh01, bh23;
-    decode_word(qg, al01, al23, ah01, ah23);
-    decode_word(qg8, bl01, bl23, bh01, bh23);
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        std::uint32_t b[4];
-        load_b<XF32>(p, nt, g, t, kelem, b);
-        float tmp[4];
-        mma_16816(tmp, al01, bl01, al23, bl23, b[0], b[1], zero);
-        mma_16816(tmp, ah01, bh01, ah23, bh23, b[2], b[3], tmp);
-        acc[nt][0] = fmaf(dg, tmp[0], acc[nt][0]);
-        acc[nt][1] = fmaf(dg, tmp[1], acc[nt][1]);
-        acc[nt][2] = fmaf(dg8, tmp[2], acc[nt][2]);
-        acc[nt][3] = fmaf(dg8, tmp[3], acc[nt][3]);
-    }
+__device__ __forceinline__ float2 half2_bits_to_float2(std::uint32_t v) {
+    __half2 h;
+    memcpy(&h, &v, sizeof(h));
+    return __half22float2(h);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
     return g / (1.0f + expf(-g)) * u;
 }
 
+// Source row i (0..15) of a tile.  Plain tiles are 16 consecutive rows;
+// SwiGLU tiles pair gate rows f..f+7 (A rows 0-7) with up rows f..f+7
+// (A rows 8-15) so lane (g, t) ends up holding gate and up of the same
+// feature.  Rows past N are clamped (loaded, never stored).
+template <int EPI>
+__device__ __forceinline__ const std::uint8_t* tile_row(const Params& p, std::uint32_t tile,
+                                                        int i) {
+    if constexpr (EPI == kEpiSwiGLU) {
+        const std::uint32_t f = min(tile * 8u + (i & 7), p.N - 1);
+        return (i < 8 ? p.w : p.w2) + f * p.pitch;
+    } else {
+        const std::uint32_t r = min(tile * 16u + i, p.N - 1);
+        return p.w + r * p.pitch;
+    }
+}
+
 template <int NT, bool XF32, bool OF32, int EPI>
-__global__ void __launch_bounds__(kThreads) q4_0_linear_mma_kernel(const Params p) {
-    extern __shared__ __align__(128) std::uint8_t smem[];
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int g = lane >> 2;
-    const int t = lane & 3;
-
-    std::uint8_t* ring = smem + warp * kWarpRingBytes;
-    std::uint64_t* bars =
-        reinterpret_cast<std::uint64_t*>(smem + kWarps * kWarpRingBytes) + warp * kStages;
-
-    // Source rows of this tile.
-    const std::uint8_t* src_row = nullptr;
-    if (lane < kTileRows) {
-        if constexpr (EPI == kEpiSwiGLU) {
-            const std::uint32_t f = min(blockIdx.x * 8u + (lane & 7), p.N - 1);
-            src_row = (lane < 8 ? p.w : p.w2) + f * p.pitch;
-        } else {
-            const std::uint32_t r = min(blockIdx.x * 16u + lane, p.N - 1);
-            src_row = p.w + r * p.pitch;
-        }
-    }
-
-    const std::uint32_t u0 = (p.units * warp) / kWarps;
-    const std::uint32_t u1 = (p.units * (warp + 1)) / kWarps;
-    const std::uint32_t nstages = (u1 - u0 + kStageUnits - 1) / kStageUnits;
-
-    if (lane == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
-        fence_mbarrier_init();
-    }
-    __syncwarp();
-
-    const std::uint64_t policy = l2_evict_first_policy();
-    auto issue = [&](std::uint32_t s) {
-        const std::uint32_t ua = u0 + s * kStageUnits;
-        const std::uint32_t nu = min(static_cast<std::uint32_t>(kStageUnits), u1 - ua);
-        const std::uint32_t bytes = nu * kUnitBytes;
-        std::uint64_t* bar = &bars[s % kStages];
-        if (lane == 0) mbar_arrive_expect_tx(bar, bytes * kTileRows);
-        __syncwarp();
-        if (lane < kTileRows) {
-            bulk_copy_g2s(ring + (s % kStages) * kStageBytes + lane * kRowStride,
-                          src_row + static_cast<std::uint64_t>(ua) * kUnitBytes, bytes, bar,
-                          policy);
-        }
-    };
-
-    for (std::uint32_t s = 0; s < min(nstages, static_cast<std::uint32_t>(kStages)); ++s) issue(s);
-
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-
-    unsigned* status = &g_device_status;
-    bool ok = true;
-    for (std::uint32_t s = 0; s < nstages && ok; ++s) {
-        const int slot = s % kStages;
-        ok = mbar_wait_bounded(&bars[slot], (s / kStages) & 1u, status);
-        if (!ok) break;
-        const std::uint32_t ua = u0 + s * kStageUnits;
-        const std::uint32_t nu = min(static_cast<std::uint32_t>(kStageUnits), u1 - ua);
-        const std::uint8_t* rg = ring + slot * kStageBytes + g * kRowStride;
-        const std::uint8_t* rg8 = rg + 8 * kRowStride;
-        const std::uint64_t kbase = static_cast<std::uint64_t>(ua) * (kUnitBlocks * 32);
-        const std::uint32_t npairs = nu * (kUnitBlocks / 2);
-#pragma unroll 2
-        for (std::uint32_t pr = 0; pr < npairs; ++pr) {
-            const std::uint32_t* ra = reinterpret_cast<const std::uint32_t*>(rg + pr * 36);
-            const std::uint32_t* rb = reinterpret_cast<const std::uint32_t*>(rg8 + pr * 36);
-            const std::uint32_t a_d0 = ra[0], a_q0 = ra[t], a_q1 = ra[t + 1], a_d1 = ra[4],
-                                a_q2 = ra[5 + t];
-            const std::uint32_t b_d0 = rb[0], b_q0 = rb[t], b_q1 = rb[t + 1], b_d1 = rb[4],
-                                b_q2 = rb[5 + t];
-            const std::uint64_t ke = kbase + pr * 64;
-            // even block of the pair (4-byte aligned)
-            block_mma<NT, XF32>(p, prmt(a_q0, a_q1, 0x5432u), prmt(b_q0, b_q1, 0x5432u),
-                                half_bits_to_float(a_d0 & 0xFFFFu),
-                                half_bits_to_float(b_d0 & 0xFFFFu), ke, g, t, acc);
-            // odd block of the pair (quant words are 4-byte aligned)
-            block_mma<NT, XF32>(p, a_q2, b_q2, half_bits_to_float(a_d1 >> 16),
-                                half_bits_to_float(b_d1 >> 16), ke + 32, g, t, acc);
-        }
-        __syncwarp();
-        if (s + kStages < nstages) {
-            fence_proxy_async_smem();
-            issue(s + kStages);
-        }
-    }
-
-    // Cross-warp reduction.  The rings are dead once every warp is past its
-    // loop; reuse them for the partial sums.
-    __syncthreads();
-    float* red = reinterpret_cast<float*>(smem);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[((warp * NT + nt) * 4 + i) * 32 + lane] = acc[nt][i];
-    __syncthreads();
-    if (warp != 0) return;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float v = acc[nt][i];
-#pragma unroll
-            for (int w = 1; w < kWarps; ++w) v += red[((w * NT + nt) * 4 + i) * 32 + lane];
-            acc[nt][i] = v;
-        }
-
-    // Epilogue.  Lane (g, t) holds rows g, g+8 and MMA columns 2t, 2t+1.
+__device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, int g, int t,
+                                           const float (&acc)[NT][4]) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         if constexpr (EPI == kEpiSwiGLU) {
-            const std::uint32_t f = blockIdx.x * 8u + g;
+            const std::uint32_t f = tile * 8u + g;
             if (f >= p.N) continue;
             if constexpr (!XF32) {
 #pragma unroll
@@ -297,7 +167,7 @@ __global__ void __launch_bounds__(kThreads) q4_0_linear_mma_kernel(const Params 
         } else {
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
-                const std::uint32_t r = blockIdx.x * 16u + g + 8 * half;
+                const std::uint32_t r = tile * 16u + g + 8 * half;
                 if (r >= p.N) continue;
                 if constexpr (!XF32) {
 #pragma unroll
@@ -320,6 +190,214 @@ __global__ void __launch_bounds__(kThreads) q4_0_linear_mma_kernel(const Params 
                         static_cast<__half*>(p.y)[m * p.ldy + r] = __float2half_rn(v);
                 }
             }
+        }
+    }
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <int NT, bool XF32, bool OF32, int EPI, int STAGES>
+__global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) {
+    extern __shared__ __align__(1024) std::uint8_t smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+
+    std::uint8_t* xs = smem;
+    std::uint8_t* ring = smem + p.x_bytes + warp * STAGES * kStageBytes;
+    float* red = reinterpret_cast<float*>(smem + p.x_bytes + kWarps * STAGES * kStageBytes);
+
+    const std::uint32_t my_tiles =
+        p.tiles > blockIdx.x ? (p.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const std::uint32_t u0 = (p.units * warp) / kWarps;
+    const std::uint32_t u1 = (p.units * (warp + 1)) / kWarps;
+    const std::uint32_t spt = u1 - u0;  // stages (units) per tile
+    const std::uint32_t total = my_tiles * spt;
+    const std::uint64_t policy = l2_evict_first_policy();
+
+    // A stage is 16 rows x 144 bytes = 144 chunks of 16 bytes; lane l copies
+    // chunks l, l+32, ... (row c/9, chunk c%9) with cp.async, one commit
+    // group per stage.  Rows of the current tile are cached per lane.
+    constexpr int kChunks = kTileRows * (kUnitBytes / 16);              // 144
+    constexpr int kChunksPerLane = (kChunks + 31) / 32;                 // 5
+    std::uint32_t dst_off[kChunksPerLane];
+    std::uint32_t src_off[kChunksPerLane];
+    int chunk_row[kChunksPerLane];
+#pragma unroll
+    for (int j = 0; j < kChunksPerLane; ++j) {
+        const int c = min(lane + 32 * j, kChunks - 1);
+        chunk_row[j] = c / 9;
+        dst_off[j] = chunk_row[j] * kRowStride + (c % 9) * 16;
+        src_off[j] = (c % 9) * 16;
+    }
+    const std::uint32_t ring_s = smem_u32(ring);
+    std::uint32_t cached_tile = 0xffffffffu;
+    const std::uint8_t* row_ptr[kChunksPerLane];
+    auto issue = [&](std::uint32_t s) {
+        if (s < total) {
+            const std::uint32_t tl = s / spt;
+            const std::uint32_t tile = blockIdx.x + tl * gridDim.x;
+            if (tile != cached_tile) {
+                cached_tile = tile;
+#pragma unroll
+                for (int j = 0; j < kChunksPerLane; ++j)
+                    row_ptr[j] = tile_row<EPI>(p, tile, chunk_row[j]);
+            }
+            const std::uint32_t ua = u0 + (s - tl * spt);
+            const std::uint32_t slot_s = ring_s + (s % STAGES) * kStageBytes;
+#pragma unroll
+            for (int j = 0; j < kChunksPerLane; ++j)
+                if (lane + 32 * j < kChunks)
+                    cp_async_16(slot_s + dst_off[j],
+                                row_ptr[j] + static_cast<std::uint64_t>(ua) * kUnitBytes + src_off[j],
+                                policy);
+        }
+        cp_async_commit();
+    };
+    for (std::uint32_t s = 0; s + 1 < STAGES; ++s) issue(s);
+
+    // Stage the activations: row r of the shared copy holds activation row r
+    // (f16) -- or, for f32 input, rows 2m / 2m+1 hold f16(x[m]) and
+    // f16(x[m] - f16(x[m])) -- with elements 1 and 2 of every group of 4
+    // swapped to match decode_word's pairing.
+    {
+        const std::uint32_t groups = static_cast<std::uint32_t>(p.K / 4);
+        const std::uint32_t total_groups = p.M * groups;
+        for (std::uint32_t i = threadIdx.x; i < total_groups; i += kThreads) {
+            const std::uint32_t m = i / groups;
+            const std::uint32_t gi = i - m * groups;
+            if constexpr (!XF32) {
+                const uint2 v = __ldg(reinterpret_cast<const uint2*>(
+                    static_cast<const __half*>(p.x) + m * p.K + 4 * gi));
+                uint2 o;
+                o.x = prmt(v.x, v.y, 0x5410u);  // (x0, x2)
+                o.y = prmt(v.x, v.y, 0x7632u);  // (x1, x3)
+                *reinterpret_cast<uint2*>(xs + m * p.x_stride + 8 * gi) = o;
+            } else {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(
+                    static_cast<const float*>(p.x) + m * p.K + 4 * gi));
+                const float h0 = __half2float(__float2half_rn(v.x));
+                const float h1 = __half2float(__float2half_rn(v.y));
+                const float h2 = __half2float(__float2half_rn(v.z));
+                const float h3 = __half2float(__float2half_rn(v.w));
+                const uint2 hi = make_uint2(pack_half2(h0, h2), pack_half2(h1, h3));
+                const uint2 lo = make_uint2(pack_half2(v.x - h0, v.z - h2),
+                                            pack_half2(v.y - h1, v.w - h3));
+                *reinterpret_cast<uint2*>(xs + (2 * m) * p.x_stride + 8 * gi) = hi;
+                *reinterpret_cast<uint2*>(xs + (2 * m + 1) * p.x_stride + 8 * gi) = lo;
+            }
+        }
+        // the zero row read by lanes whose B column has no token
+        for (std::uint32_t i = threadIdx.x; i < p.x_stride / 16; i += kThreads)
+            *reinterpret_cast<uint4*>(xs + p.x_zero_row * p.x_stride + 16 * i) =
+                make_uint4(0u, 0u, 0u, 0u);
+        __syncthreads();
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    // Shared address of this lane's B fragments (row nt*8+g, group t).  Rows
+    // past the staged ones read the zero row at the end of the staging area,
+    // so every lane loads unconditionally.
+    std::uint32_t xaddr[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const std::uint32_t row = nt * 8 + g;
+        xaddr[nt] = smem_u32(xs) + (row < p.x_rows ? row : p.x_zero_row) * p.x_stride + 8 * t;
+    }
+    const std::uint32_t ring_addr = smem_u32(ring) + g * kRowStride;
+
+    std::uint32_t s = 0;
+    for (std::uint32_t tl = 0; tl < my_tiles; ++tl) {
+        for (std::uint32_t st = 0; st < spt; ++st, ++s) {
+            const int slot = s % STAGES;
+            // Keep STAGES-1 stages in flight: refill the slot freed by the
+            // previous stage, then wait for this one (own groups only; the
+            // warp's lanes together fetched the stage).
+            issue(s + STAGES - 1);
+            cp_async_wait<STAGES - 1>();
+            __syncwarp();
+            {
+                // Row g of the stage at ra, row g+8 at ra + 8 rows; qa points
+                // at this lane's quant words (4t bytes further).
+                const std::uint32_t ra = ring_addr + slot * kStageBytes;
+                const std::uint32_t qa = ra + 4 * t;
+                constexpr std::uint32_t kR8 = 8 * kRowStride;
+                const std::uint32_t xo = (u0 + st) * (kUnitBlocks * 64);
+#pragma unroll
+                for (int pr = 0; pr < kUnitBlocks / 2; ++pr) {
+                    const std::uint32_t o = pr * 36;
+                    const std::uint32_t a_d0 = lds32(ra + o), a_d1 = lds32(ra + o + 16);
+                    const std::uint32_t a_q0 = lds32(qa + o), a_q1 = lds32(qa + o + 4),
+                                        a_q2 = lds32(qa + o + 20);
+                    const std::uint32_t b_d0 = lds32(ra + kR8 + o), b_d1 = lds32(ra + kR8 + o + 16);
+                    const std::uint32_t b_q0 = lds32(qa + kR8 + o), b_q1 = lds32(qa + kR8 + o + 4),
+                                        b_q2 = lds32(qa + kR8 + o + 20);
+                    uint2 bx[NT][2][2];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int blk = 0; blk < 2; ++blk) {
+                            const std::uint32_t xb = xaddr[nt] + xo + (pr * 2 + blk) * 64;
+                            bx[nt][blk][0] = lds64(xb);
+                            bx[nt][blk][1] = lds64(xb + 32);
+                        }
+                    // scales of rows (g, g+8) for the even and the odd block
+                    const float2 d0 = half2_bits_to_float2(prmt(a_d0, b_d0, 0x5410u));
+                    const float2 d1 = half2_bits_to_float2(prmt(a_d1, b_d1, 0x7632u));
+#pragma unroll
+                    for (int blk = 0; blk < 2; ++blk) {
+                        // even block: quant words straddle a 4-byte boundary
+                        const std::uint32_t wa = blk == 0 ? prmt(a_q0, a_q1, 0x5432u) : a_q2;
+                        const std::uint32_t wb = blk == 0 ? prmt(b_q0, b_q1, 0x5432u) : b_q2;
+                        const float2 d = blk == 0 ? d0 : d1;
+                        std::uint32_t al02, al13, ah02, ah13, bl02, bl13, bh02, bh13;
+                        decode_word(wa, al02, al13, ah02, ah13);
+                        decode_word(wb, bl02, bl13, bh02, bh13);
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            float tmp[4];
+                            mma_16816(tmp, al02, bl02, al13, bl13, bx[nt][blk][0].x,
+                                      bx[nt][blk][0].y, zero);
+                            mma_16816(tmp, ah02, bh02, ah13, bh13, bx[nt][blk][1].x,
+                                      bx[nt][blk][1].y, tmp);
+                            acc[nt][0] = fmaf(d.x, tmp[0], acc[nt][0]);
+                            acc[nt][1] = fmaf(d.x, tmp[1], acc[nt][1]);
+                            acc[nt][2] = fmaf(d.y, tmp[2], acc[nt][2]);
+                            acc[nt][3] = fmaf(d.y, tmp[3], acc[nt][3]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // the slot is refilled by the next iteration's issue
+        }
+        // Meet the other K-slices of this tile.
+        float* mine = red + ((tl & 1u) * kWarps + warp) * (NT * 4 * 32);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                mine[(nt * 4 + i) * 32 + lane] = acc[nt][i];
+                acc[nt][i] = 0.f;
+            }
+        named_barrier_sync(1, kThreads);
+        if (static_cast<int>(tl % kWarps) == warp) {
+            float sum[NT][4];
+            const float* base = red + (tl & 1u) * kWarps * (NT * 4 * 32);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float v = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kWarps; ++w) v += base[w * (NT * 4 * 32) + (nt * 4 + i) * 32 + lane];
+                    sum[nt][i] = v;
+                }
+            store_tile<NT, XF32, OF32, EPI>(p, blockIdx.x + tl * gridDim.x, g, t, sum);
         }
     }
 }
@@ -406,71 +484,126 @@ int ensure_smem_attribute(Kernel kernel, int bytes, std::atomic<std::uint64_t>& 
     if (e != cudaSuccess) return static_cast<int>(e);
     const std::uint64_t bit = 1ull << (dev & 63);
     if (done.load(std::memory_order_acquire) & bit) return kSuccess;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     done.fetch_or(bit, std::memory_order_acq_rel);
     return kSuccess;
 }
 
-template <int NT, bool XF32, bool OF32, int EPI>
-int launch_mma(const Params& p, std::uint32_t grid, cudaStream_t stream) {
-    auto kernel = q4_0_linear_mma_kernel<NT, XF32, OF32, EPI>;
+// Streaming multiprocessors of the current device (cached per ordinal).
+inline int sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    int v = cache[dev & 63].load(std::memory_order_relaxed);
+    if (v == 0) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+            v = 148;
+        cache[dev & 63].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
+template <int NT, bool XF32, bool OF32, int EPI, int STAGES>
+int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
+    auto kernel = q4_0_gemv_kernel<NT, XF32, OF32, EPI, STAGES>;
     static std::atomic<std::uint64_t> configured{0};
-    const int st = ensure_smem_attribute(kernel, kSmemBytes, configured);
+    const int st = ensure_smem_attribute(kernel, kMaxSmem, configured);
     if (st != kSuccess) return st;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
+    const std::uint32_t grid =
+        min(p.tiles, static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
+    kernel<<<grid, kThreads, smem_bytes(static_cast<int>(p.x_bytes), NT, STAGES), stream>>>(p);
     return static_cast<int>(cudaGetLastError());
 }
 
-template <bool XF32, bool OF32, int EPI>
-int launch_mma_nt(const Params& p, std::uint32_t grid, cudaStream_t stream) {
-    const std::uint32_t per_tile = XF32 ? 4 : 8;
-    const std::uint32_t tiles = (p.M + per_tile - 1) / per_tile;
-    if (tiles <= 1) return launch_mma<1, XF32, OF32, EPI>(p, grid, stream);
-    if (tiles <= 2) return launch_mma<2, XF32, OF32, EPI>(p, grid, stream);
-    if (tiles <= 4) return launch_mma<4, XF32, OF32, EPI>(p, grid, stream);
-    return launch_mma<8, XF32, OF32, EPI>(p, grid, stream);
+template <bool XF32, bool OF32, int EPI, int NT>
+int launch_gemv_stages(const Params& p, int stages, int ctas, cudaStream_t stream) {
+    switch (stages) {
+        case 4: return launch_gemv<NT, XF32, OF32, EPI, 4>(p, ctas, stream);
+        case 3: return launch_gemv<NT, XF32, OF32, EPI, 3>(p, ctas, stream);
+        default: return launch_gemv<NT, XF32, OF32, EPI, 2>(p, ctas, stream);
+    }
 }
 
-// Runs the linear for M rows of x.  Token groups beyond what one launch
-// covers (64 f16 tokens / 32 f32 tokens) are processed in consecutive
-// launches on the same stream.
+template <bool XF32, bool OF32, int EPI>
+int launch_gemv_config(const Params& p, int nt, int stages, int ctas, cudaStream_t stream) {
+    return nt == 1 ? launch_gemv_stages<XF32, OF32, EPI, 1>(p, stages, ctas, stream)
+                   : launch_gemv_stages<XF32, OF32, EPI, 2>(p, stages, ctas, stream);
+}
+
+// Picks tokens per launch, n8 tiles and ring depth so the staged
+// activations fit next to the ring.  Returns false if not even one token
+// fits (then the generic kernel runs).
+inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, std::uint32_t& tokens,
+                      int& nt, int& stages, int& ctas_per_sm, std::uint32_t& x_rows,
+                      std::uint32_t& x_stride, std::uint32_t& x_bytes) {
+    const std::uint32_t rows_per_token = xf32 ? 2 : 1;
+    std::uint32_t m = static_cast<std::uint32_t>(
+        M < static_cast<std::uint64_t>(kMaxXRows / rows_per_token) ? M : kMaxXRows / rows_per_token);
+    if (K > (1ull << 24)) return false;
+    x_stride = static_cast<std::uint32_t>(K * 2 + 32);
+    // Preference: two CTAs per SM (16 warps to hide latency) with a deep
+    // ring, then one CTA per SM.
+    constexpr int kOptions[4][2] = {{2, 4}, {2, 3}, {1, 4}, {1, 2}};
+    for (; m >= 1; m = m / 2) {
+        x_rows = m * rows_per_token;
+        x_bytes = ((x_rows + 1) * x_stride + 127u) & ~127u;  // + the zero row
+        nt = x_rows <= 8 ? 1 : 2;
+        for (const auto& opt : kOptions) {
+            const int bytes = smem_bytes(static_cast<int>(x_bytes), nt, opt[1]);
+            if (bytes <= kMaxSmem && opt[0] * (bytes + kSmemReservedPerCta) <= kSmemPerSm) {
+                ctas_per_sm = opt[0];
+                stages = opt[1];
+                tokens = m;
+                return true;
+            }
+        }
+        if (m == 1) break;
+    }
+    return false;
+}
+
+// Runs the linear for M rows of x, in as few persistent launches as the
+// activation staging allows (consecutive launches on the same stream).
 template <bool XF32, bool OF32, int EPI>
 int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint64_t M,
                std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream) {
+    const std::size_t osz = OF32 ? 4 : 2;
     if (K == 0) {
         // Every dot product is empty: the reference writes zeros
         // (crates/mote-backend-hip/tests/quantized_linear.rs:142-158).  For
         // SwiGLU silu(0) * 0 = 0 as well.
-        const std::size_t esz = OF32 ? 4 : 2;
-        const cudaError_t e = cudaMemset2DAsync(y, ldy * esz, 0, N * esz, M, stream);
-        return static_cast<int>(e);
+        return static_cast<int>(cudaMemset2DAsync(y, ldy * osz, 0, N * osz, M, stream));
     }
     Params p{};
-    p.x = x;
     p.w = static_cast<const std::uint8_t*>(w);
     p.w2 = static_cast<const std::uint8_t*>(w2);
-    p.y = y;
     p.N = static_cast<std::uint32_t>(N);
     p.K = K;
     p.pitch = (K / 32) * 18;
     p.units = static_cast<std::uint32_t>(K / 256);
     p.ldy = ldy;
+    const std::uint64_t rows_per_tile = EPI == kEpiSwiGLU ? 8 : 16;
+    p.tiles = static_cast<std::uint32_t>((N + rows_per_tile - 1) / rows_per_tile);
     const std::size_t xes = XF32 ? 4 : 2;
     bool fast = (K % 256 == 0) && (reinterpret_cast<std::uintptr_t>(w) % 16 == 0) &&
-                (reinterpret_cast<std::uintptr_t>(x) % (XF32 ? 16 : 8) == 0);
+                (reinterpret_cast<std::uintptr_t>(x) % 16 == 0);
     if (EPI == kEpiSwiGLU) fast = fast && (reinterpret_cast<std::uintptr_t>(w2) % 16 == 0);
-    const std::uint64_t chunk = fast ? (XF32 ? 32 : 64) : kGenericTokens * 65535ull;
+    std::uint32_t tokens = 0;
+    int nt = 1, stages = 2, ctas = 1;
+    if (fast)
+        fast = plan_gemv(M, K, XF32, tokens, nt, stages, ctas, p.x_rows, p.x_stride, p.x_bytes);
+    const std::uint64_t chunk = fast ? tokens : kGenericTokens * 65535ull;
     for (std::uint64_t m0 = 0; m0 < M; m0 += chunk) {
         const std::uint64_t mc = (M - m0 < chunk) ? (M - m0) : chunk;
         p.M = static_cast<std::uint32_t>(mc);
         p.x = static_cast<const std::uint8_t*>(x) + m0 * K * xes;
-        p.y = static_cast<std::uint8_t*>(y) + m0 * ldy * (OF32 ? 4 : 2);
+        p.y = static_cast<std::uint8_t*>(y) + m0 * ldy * osz;
         int st;
         if (fast) {
-            const std::uint64_t rows_per_tile = EPI == kEpiSwiGLU ? 8 : 16;
-            const std::uint64_t grid = (N + rows_per_tile - 1) / rows_per_tile;
-            st = launch_mma_nt<XF32, OF32, EPI>(p, static_cast<std::uint32_t>(grid), stream);
+            p.x_rows = static_cast<std::uint32_t>(mc) * (XF32 ? 2 : 1);
+            p.x_zero_row = p.x_rows;
+            st = launch_gemv_config<XF32, OF32, EPI>(p, nt, stages, ctas, stream);
         } else {
             const dim3 grid(static_cast<unsigned>((N + 3) / 4),
                             static_cast<unsigned>((mc + kGenericTokens - 1) / kGenericTokens));
@@ -487,11 +620,12 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
 // (stream included) and K not a multiple of 32 are invalid values, empty
 // outputs succeed without a launch, and rows*N must fit the reference's
 // one-block-per-output 32-bit grid.
+constexpr int kEmpty = -2;
 inline int check_linear_args(const void* x, const void* w, const void* y, std::uint64_t rows,
                              std::uint64_t n, std::uint64_t k, const void* stream) {
     if (x == nullptr || w == nullptr || y == nullptr || stream == nullptr) return kInvalidValue;
     if (k % 32 != 0) return kInvalidValue;
-    if (rows == 0 || n == 0) return -2;  // empty: success without launch
+    if (rows == 0 || n == 0) return kEmpty;
     if (rows > 0xffffffffull || n > 0xffffffffull || rows > 0xffffffffull / n)
         return kInvalidConfiguration;
     return kSuccess;
@@ -507,7 +641,7 @@ extern "C" int mote_cuda_quantized_linear_q4_0_f16(const void* input, const void
     using namespace mote::q4;
     const int c = check_linear_args(input, weights, output, rows, output_features,
                                     input_features, stream);
-    if (c == -2) return mote::kSuccess;
+    if (c == kEmpty) return mote::kSuccess;
     if (c != 0) return c;
     return run_linear<false, false, kEpiPlain>(input, weights, nullptr, output, rows,
                                                output_features, input_features, output_features,
@@ -522,7 +656,7 @@ extern "C" int mote_cuda_quantized_linear_q4_0_f16_f32out(const void* input, con
     using namespace mote::q4;
     const int c = check_linear_args(input, weights, output, rows, output_features,
                                     input_features, stream);
-    if (c == -2) return mote::kSuccess;
+    if (c == kEmpty) return mote::kSuccess;
     if (c != 0) return c;
     return run_linear<false, true, kEpiPlain>(input, weights, nullptr, output, rows,
                                               output_features, input_features, output_features,
@@ -536,7 +670,7 @@ extern "C" int mote_cuda_quantized_linear_q4_0_f32(const void* input, const void
     using namespace mote::q4;
     const int c = check_linear_args(input, weights, output, rows, output_features,
                                     input_features, stream);
-    if (c == -2) return mote::kSuccess;
+    if (c == kEmpty) return mote::kSuccess;
     if (c != 0) return c;
     return run_linear<true, true, kEpiPlain>(input, weights, nullptr, output, rows,
                                              output_features, input_features, output_features,
@@ -551,7 +685,7 @@ extern "C" int mote_cuda_q4_0_gate_up_swiglu_f16(const void* input, const void* 
     if (up_weights == nullptr) return mote::kInvalidValue;
     const int c = check_linear_args(input, gate_weights, output, rows, ffn_features,
                                     input_features, stream);
-    if (c == -2) return mote::kSuccess;
+    if (c == kEmpty) return mote::kSuccess;
     if (c != 0) return c;
     return run_linear<false, false, kEpiSwiGLU>(input, gate_weights, up_weights, output, rows,
                                                 ffn_features, input_features, ffn_features,

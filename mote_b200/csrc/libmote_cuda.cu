@@ -2,6 +2,7 @@
 // files for reading; compiling them as one unit lets them share the
 // per-device status word without relocatable device code.
 #include "runtime.cu"
+#include "q4_0_gemm_tcgen05.cu"
 #include "q4_0_linear.cu"
 #include "layer_ops.cu"
 #include "q4_0_codec.cu"

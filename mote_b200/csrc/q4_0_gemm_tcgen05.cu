@@ -1,0 +1,499 @@
+// Prefill-shaped Q4_0 GEMM on the 5th-generation tensor cores (tcgen05/TMEM).
+//
+//   Y[M, N] = X[M, K] * W[N, K]^T,  X f16, W ggml Q4_0 (18-byte blocks), Y f16/f32,
+//   for M large enough that the contraction, not the weight stream, bounds
+//   the time (the reference computes it in f32 per output,
+//   crates/mote-reference/src/quantized.rs:89-144).
+//
+// One CTA computes a 128 (tokens) x 256 (features) tile:
+// * warp 8 (producer) streams activation tiles (64 k x 128 rows, TMA with
+//   128-byte swizzle) and raw Q4_0 row slices (256 rows x 144 bytes = 8
+//   blocks per row, TMA 2-D tile of bytes) into shared memory;
+// * warps 0-7 (converters) dequantize each 64-k slice of the raw rows into
+//   f16 (q - 8) * d -- correctly rounded, exactly what a dense f16 weight
+//   would hold -- written straight into the 128-byte-swizzled K-major
+//   layout the tensor core reads;
+// * warp 9 allocates 256 TMEM columns and one thread issues
+//   tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) per 16-k step,
+//   accumulating in f32 in TMEM; tcgen05.commit releases the operand stages;
+// * after the last k-slice the converter warps read the accumulator with
+//   tcgen05.ld (warp w owns TMEM lanes 32*(w%4).. and half of the columns)
+//   and store the tile.
+// Stages are tracked with mbarriers; every wait is bounded and an expired
+// wait aborts the whole CTA (which still frees its TMEM).  No TMA load uses
+// cluster multicast.
+
+#include "mote_common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+#include <type_traits>
+
+namespace mote {
+namespace gemm {
+
+constexpr int kBM = 128;                 // tokens per tile = TMEM lanes
+constexpr int kBN = 256;                 // features per tile = TMEM columns
+constexpr int kBK = 64;                  // k per operand stage (one 128-B f16 swizzle row)
+constexpr int kSuperK = 256;             // k per raw weight stage (8 blocks, 144 B per row)
+constexpr int kStages = 3;               // operand stages
+constexpr int kRawStages = 2;            // raw weight stages
+constexpr int kABytes = kBM * kBK * 2;   // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kRawRowBytes = 144;
+constexpr int kRawBytes = kBN * kRawRowBytes;  // 36 KB
+constexpr int kConvWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
+constexpr int kTmemCols = 256;
+
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kABytes;
+constexpr int kOffRaw = kOffB + kStages * kBBytes;
+constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
+// barriers: a_full[S], b_full[S], empty[S], raw_full[R], raw_empty[R], accum
+constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
+constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+constexpr int kOffAbort = kOffTmemSlot + 4;
+constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + slack to align the base to 1024
+
+struct Params {
+    void* y;
+    std::uint32_t M, N, K;
+    std::uint64_t ldy;
+};
+
+// ---- PTX wrappers ------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(std::uint32_t dst, const CUtensorMap* map, int x,
+                                            int y, std::uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(std::uint32_t slot_smem, std::uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     slot_smem),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(std::uint32_t taddr, std::uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, cta_group::1.
+__device__ __forceinline__ void umma_f16(std::uint32_t tmem_d, std::uint64_t adesc,
+                                         std::uint64_t bdesc, std::uint32_t idesc,
+                                         std::uint32_t accumulate) {
+    const std::uint32_t mask = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+            tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask), "r"(mask), "r"(mask),
+        "r"(mask)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(std::uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive f32 columns: thread i gets row (lane base + i).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(std::uint32_t taddr, std::uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128
+// bytes, 8-row groups 1024 bytes apart (SBO = 64 x 16 B), LBO unused (1),
+// descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ std::uint64_t smem_desc_sw128(std::uint32_t addr) {
+    std::uint64_t d = 0;
+    d |= static_cast<std::uint64_t>((addr & 0x3FFFFu) >> 4);
+    d |= static_cast<std::uint64_t>(1) << 16;   // LBO
+    d |= static_cast<std::uint64_t>(64) << 32;  // SBO
+    d |= static_cast<std::uint64_t>(1) << 46;   // version
+    d |= static_cast<std::uint64_t>(2) << 61;   // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: F32 accumulate, A = B = F16, both
+// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr std::uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) |
+                                 (static_cast<std::uint32_t>(kBN >> 3) << 17) |
+                                 (static_cast<std::uint32_t>(kBM >> 4) << 24);
+
+// Bounded wait that also gives up as soon as another role aborted.
+__device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t parity,
+                                              volatile std::uint32_t* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - start > kWaitCycles) {
+            *abort_flag = 1u;
+            atomicOr(&g_device_status, kDevWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// One Q4_0 block -- scale bits `dbits`, quant words q[0..3] = bytes 0..15 --
+// to 32 f16 values (q - 8) * d (exact subtraction, one rounding in the
+// product), written as four 16-byte chunks of the 128-byte swizzled row at
+// `dst_row`, starting at element e0 (0 or 32).
+__device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::uint32_t (&q)[4],
+                                              std::uint32_t dst_row, int e0, int swz) {
+    const std::uint32_t d2 = dbits | (dbits << 16);
+    std::uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const std::uint32_t a = prmt(q[i], 0u, 0x4140u);  // bytes 4i, 4i+1
+        const std::uint32_t b = prmt(q[i], 0u, 0x4342u);  // bytes 4i+2, 4i+3
+        lo[2 * i] = and_or(a, 0x000F000Fu, 0x64006400u);
+        lo[2 * i + 1] = and_or(b, 0x000F000Fu, 0x64006400u);
+        hi[2 * i] = and_or(a, 0x00F000F0u, 0x54005400u);
+        hi[2 * i + 1] = and_or(b, 0x00F000F0u, 0x54005400u);
+    }
+    std::uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        std::uint32_t t;
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(lo[i]), "r"(0x64086408u));
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[i]) : "r"(t), "r"(d2));
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(hi[i]), "r"(0x54805480u));
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[8 + i]) : "r"(t), "r"(d2));
+    }
+    // o[0..7]: elements 0..15, o[8..15]: elements 16..31, 8 elements per chunk
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const int chunk = (e0 / 8 + c) ^ swz;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst_row + chunk * 16),
+                     "r"(o[4 * c]), "r"(o[4 * c + 1]), "r"(o[4 * c + 2]), "r"(o[4 * c + 3])
+                     : "memory");
+    }
+}
+
+// Converts the two Q4_0 blocks of 64-k slice SUB (0..3) of one 144-byte raw
+// row (16-byte aligned at `raw_row`) into the swizzled f16 row `dst_row`.
+// The slice spans bytes [36*SUB, 36*SUB + 36); three aligned 16-byte loads
+// cover it (rows are 144 = 9 x 16 bytes apart, so a warp's loads are
+// bank-conflict free) and byte permutes pick the blocks out.
+template <int SUB>
+__device__ __forceinline__ void convert_slice(std::uint32_t raw_row, std::uint32_t dst_row,
+                                              int swz) {
+    constexpr int kStart = 36 * SUB;
+    constexpr int kChunk0 = kStart / 16;
+    constexpr int kW = (kStart % 16) / 4;  // first word of the slice within the 12 loaded
+    std::uint32_t w[12];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int chunk = kChunk0 + c < 9 ? kChunk0 + c : 8;  // never past the row
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                     : "r"(raw_row + chunk * 16));
+    }
+    // even block: scale = low half of word kW, quants start 2 bytes later
+    std::uint32_t q0[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q0[i] = prmt(w[kW + i], w[kW + i + 1], 0x5432u);
+    convert_block(w[kW] & 0xFFFFu, q0, dst_row, 0, swz);
+    // odd block: scale = high half of word kW+4, quants are words kW+5..kW+8
+    std::uint32_t q1[4] = {w[kW + 5], w[kW + 6], w[kW + 7], w[kW + 8]};
+    convert_block(w[kW + 4] >> 16, q1, dst_row, 32, swz);
+}
+
+template <bool OF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
+                             const __grid_constant__ CUtensorMap map_w, const Params p) {
+    extern __shared__ std::uint8_t smem_raw[];
+    // 1024-byte aligned base (SW128 atoms and TMA swizzle need it)
+    const std::uint32_t raw_base = smem_u32(smem_raw);
+    const std::uint32_t base = (raw_base + 1023u) & ~1023u;
+    std::uint8_t* smem = smem_raw + (base - raw_base);
+
+    std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + kOffBar);
+    std::uint64_t* a_full = bars;
+    std::uint64_t* b_full = bars + kStages;
+    std::uint64_t* empty = bars + 2 * kStages;
+    std::uint64_t* raw_full = bars + 3 * kStages;
+    std::uint64_t* raw_empty = raw_full + kRawStages;
+    std::uint64_t* accum = raw_empty + kRawStages;
+    volatile std::uint32_t* tmem_slot = reinterpret_cast<volatile std::uint32_t*>(smem + kOffTmemSlot);
+    volatile std::uint32_t* abort_flag = reinterpret_cast<volatile std::uint32_t*>(smem + kOffAbort);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const std::uint32_t n0 = blockIdx.x * kBN;
+    const std::uint32_t m0 = blockIdx.y * kBM;
+    const std::uint32_t num_kb = p.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&a_full[s], 1);
+            mbar_init(&b_full[s], kConvWarps);
+            mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < kRawStages; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], kConvWarps);
+        }
+        mbar_init(accum, 1);
+        *abort_flag = 0u;
+        fence_mbarrier_init();
+    }
+    if (warp == kMmaWarp) tmem_alloc(base + kOffTmemSlot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const std::uint32_t tmem_d = *tmem_slot;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            for (std::uint32_t kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % kStages;
+                if (kb >= kStages &&
+                    !wait_or_abort(&empty[s], ((kb / kStages) - 1) & 1u, abort_flag))
+                    break;
+                if (kb % (kSuperK / kBK) == 0) {
+                    const std::uint32_t sb = kb / (kSuperK / kBK);
+                    const int r = sb % kRawStages;
+                    if (sb >= kRawStages &&
+                        !wait_or_abort(&raw_empty[r], ((sb / kRawStages) - 1) & 1u, abort_flag))
+                        break;
+                    mbar_arrive_expect_tx(&raw_full[r], kRawBytes);
+                    tma_load_2d(base + kOffRaw + r * kRawBytes, &map_w,
+                                static_cast<int>(sb * kRawRowBytes), static_cast<int>(n0),
+                                smem_u32(&raw_full[r]));
+                }
+                mbar_arrive_expect_tx(&a_full[s], kABytes);
+                tma_load_2d(base + kOffA + s * kABytes, &map_x, static_cast<int>(kb * kBK),
+                            static_cast<int>(m0), smem_u32(&a_full[s]));
+            }
+        }
+        __syncwarp();  // reconverge before the block-wide barrier below
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            for (std::uint32_t kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % kStages;
+                const std::uint32_t ph = (kb / kStages) & 1u;
+                if (!wait_or_abort(&a_full[s], ph, abort_flag)) break;
+                if (!wait_or_abort(&b_full[s], ph, abort_flag)) break;
+                tc_fence_after();
+                const std::uint32_t a_addr = base + kOffA + s * kABytes;
+                const std::uint32_t b_addr = base + kOffB + s * kBBytes;
+#pragma unroll
+                for (int k = 0; k < kBK / 16; ++k) {
+                    // +32 bytes per 16-element step inside the 128-byte swizzle row
+                    umma_f16(tmem_d, smem_desc_sw128(a_addr + k * 32),
+                             smem_desc_sw128(b_addr + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&empty[s]));
+            }
+            umma_commit(smem_u32(accum));
+        }
+        __syncwarp();
+    } else {
+        // converters: thread t owns weight row t of the tile
+        const int row = threadIdx.x;  // 0..255
+        const int swz = row & 7;
+        const std::uint32_t nsb = num_kb / (kSuperK / kBK);
+        bool ok = true;
+        for (std::uint32_t sb = 0; sb < nsb && ok; ++sb) {
+            const int r = sb % kRawStages;
+            ok = __all_sync(0xffffffffu, wait_or_abort(&raw_full[r], (sb / kRawStages) & 1u,
+                                                       abort_flag));
+            const std::uint32_t raw_row = base + kOffRaw + r * kRawBytes + row * kRawRowBytes;
+            auto slice = [&](auto sub_tag) {
+                constexpr int SUB = decltype(sub_tag)::value;
+                const std::uint32_t kb = sb * (kSuperK / kBK) + SUB;
+                const int s = kb % kStages;
+                if (ok && kb >= kStages)
+                    ok = __all_sync(0xffffffffu, wait_or_abort(&empty[s], ((kb / kStages) - 1) & 1u,
+                                                               abort_flag));
+                if (!ok) return;  // warp-uniform
+                convert_slice<SUB>(raw_row, base + kOffB + s * kBBytes + row * 128, swz);
+                // make the generic-proxy writes visible to the tensor core
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                     smem_u32(&b_full[s]))
+                                 : "memory");
+                    if (SUB == (kSuperK / kBK) - 1)
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                         smem_u32(&raw_empty[r]))
+                                     : "memory");
+                }
+            };
+            slice(std::integral_constant<int, 0>{});
+            slice(std::integral_constant<int, 1>{});
+            slice(std::integral_constant<int, 2>{});
+            slice(std::integral_constant<int, 3>{});
+        }
+        // epilogue: warp w reads TMEM lanes 32*(w%4).. and columns 128*(w/4)..
+        if (__all_sync(0xffffffffu, ok && wait_or_abort(accum, 0, abort_flag))) {
+            tc_fence_after();
+            const int lane_base = 32 * (warp % 4);
+            const int col_base = 128 * (warp / 4);
+            const std::uint32_t m = m0 + lane_base + lane;
+#pragma unroll 1
+            for (int cb = 0; cb < 128; cb += 32) {
+                std::uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_d + (static_cast<std::uint32_t>(lane_base) << 16) +
+                                       static_cast<std::uint32_t>(col_base + cb),
+                                   v);
+                const std::uint32_t n = n0 + col_base + cb;
+                if (m < p.M && n < p.N) {
+                    if constexpr (OF32) {
+                        float* yr = static_cast<float*>(p.y) + m * p.ldy + n;
+                        if (n + 32 <= p.N && (reinterpret_cast<std::uintptr_t>(yr) & 15) == 0) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4)
+                                *reinterpret_cast<uint4*>(yr + i) =
+                                    make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        } else {
+                            for (int i = 0; i < 32 && n + i < p.N; ++i)
+                                yr[i] = __uint_as_float(v[i]);
+                        }
+                    } else {
+                        __half* yr = static_cast<__half*>(p.y) + m * p.ldy + n;
+                        std::uint32_t hv[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * i]),
+                                                                 __uint_as_float(v[2 * i + 1]));
+                            hv[i] = *reinterpret_cast<const std::uint32_t*>(&h2);
+                        }
+                        if (n + 32 <= p.N && (reinterpret_cast<std::uintptr_t>(yr) & 15) == 0) {
+#pragma unroll
+                            for (int i = 0; i < 16; i += 4)
+                                *reinterpret_cast<uint4*>(yr + 2 * i) =
+                                    make_uint4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
+                        } else {
+                            for (int i = 0; i < 32 && n + i < p.N; ++i)
+                                yr[i] = __ushort_as_half(static_cast<unsigned short>(
+                                    (hv[i / 2] >> (16 * (i & 1))) & 0xFFFFu));
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem_d, kTmemCols);
+    }
+}
+
+// ---- host side ------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* sym = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(sym);
+    });
+    return fn;
+}
+
+// Whether the tcgen05 path takes this problem: K a multiple of 256 (whole
+// 144-byte raw stages; every TMA coordinate 16-byte aligned), N a multiple
+// of 16, 16-byte aligned operands.
+inline bool supported(const void* x, const void* w, const void* y, std::uint64_t M,
+                      std::uint64_t N, std::uint64_t K, std::size_t out_size) {
+    return M > 0 && K % kSuperK == 0 && K > 0 && N % 16 == 0 && M <= 0x7fffffffull &&
+           N <= 0x7fffffffull && K <= 0x7fffffffull &&
+           reinterpret_cast<std::uintptr_t>(x) % 16 == 0 &&
+           reinterpret_cast<std::uintptr_t>(w) % 16 == 0 &&
+           reinterpret_cast<std::uintptr_t>(y) % 16 == 0 && (N * out_size) % 16 == 0;
+}
+
+template <bool OF32>
+int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
+           std::uint64_t K, cudaStream_t stream) {
+    auto encode = encode_fn();
+    if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
+    CUtensorMap map_x{}, map_w{};
+    {
+        const cuuint64_t dims[2] = {K, M};
+        const cuuint64_t strides[1] = {K * 2};
+        const cuuint32_t box[2] = {kBK, kBM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return static_cast<int>(cudaErrorInvalidValue);
+    }
+    {
+        const std::uint64_t pitch = (K / 32) * 18;
+        const cuuint64_t dims[2] = {pitch, N};
+        const cuuint64_t strides[1] = {pitch};
+        const cuuint32_t box[2] = {kRawRowBytes, kBN};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return static_cast<int>(cudaErrorInvalidValue);
+    }
+    auto kernel = q4_0_gemm_tcgen05_kernel<OF32>;
+    static std::atomic<std::uint64_t> configured{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const std::uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        configured.fetch_or(bit);
+    }
+    Params p{y, static_cast<std::uint32_t>(M), static_cast<std::uint32_t>(N),
+             static_cast<std::uint32_t>(K), N};
+    const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN),
+                    static_cast<unsigned>((M + kBM - 1) / kBM));
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_x, map_w, p);
+    return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace gemm
+}  // namespace mote

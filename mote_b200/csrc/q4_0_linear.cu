@@ -575,6 +575,13 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         // SwiGLU silu(0) * 0 = 0 as well.
         return static_cast<int>(cudaMemset2DAsync(y, ldy * osz, 0, N * osz, M, stream));
     }
+    // Prefill-shaped problems (more tokens than one GEMV launch stages) run as
+    // a dense contraction on the tcgen05 tensor cores.
+    if constexpr (!XF32 && EPI == kEpiPlain) {
+        if (M > static_cast<std::uint64_t>(kMaxXRows) && ldy == N &&
+            gemm::supported(x, w, y, M, N, K, osz))
+            return gemm::launch<OF32>(x, w, y, M, N, K, stream);
+    }
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
     p.w2 = static_cast<const std::uint8_t*>(w2);

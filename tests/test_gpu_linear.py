@@ -27,6 +27,9 @@ from mote_b200.types import DType, QuantFormat, plain, quantized  # noqa: E402
 
 F16_BOUND = 1e-3
 F32_BOUND = 1e-5
+# tcgen05 path: (q - 8) * d rounded to f16 (<= 2^-11 relative per weight)
+# plus the f16 output rounding; element-wise (rms floor) bound 2e-3.
+PREFILL_ELEMENTWISE_BOUND = 2e-3
 
 
 @pytest.fixture(scope="module")
@@ -76,7 +79,10 @@ def test_fast_path_matches_oracle(ctx, oracle_lib, m, n, k):
     ok, bad = checker.within_reference_tolerance(got, checker.f16_round(want32), 0.01, 0.002)
     assert ok, bad
     ref64 = checker.linear_f64(x32, checker.q4_0_dequant_np(w, n, k))
-    assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND
+    # M > 16 with N % 16 == 0 runs on the tcgen05 prefill path, whose weights
+    # are rounded to f16 (see test_gpu_prefill.py for its bounds).
+    bound = PREFILL_ELEMENTWISE_BOUND if (m > 16 and n % 16 == 0) else F16_BOUND
+    assert checker.rel_err_elementwise(got, ref64) <= bound
     assert checker.rel_err_normwise(got, ref64) <= F16_BOUND
 
 

@@ -134,6 +134,19 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+// launch_dependents lets the next kernel in the stream (launched with the
+// programmatic-serialization attribute) start its independent prologue;
+// wait blocks until every prerequisite grid has completed and its memory is
+// visible.  Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- warp MMA --------------------------------------------------------------
 // D = A(16x16, f16, row) * B(16x8, f16, col) + C, f32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], std::uint32_t a0, std::uint32_t a1,

@@ -257,7 +257,12 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
         }
         cp_async_commit();
     };
+    // Weights do not depend on the previous kernel in the stream: start
+    // streaming them, let the next kernel launch, and only then wait for the
+    // producer of the activations.
     for (std::uint32_t s = 0; s + 1 < STAGES; ++s) issue(s);
+    pdl_launch_dependents();
+    pdl_wait();
 
     // Stage the activations: row r of the shared copy holds activation row r
     // (f16) -- or, for f32 input, rows 2m / 2m+1 hold f16(x[m]) and
@@ -512,8 +517,17 @@ int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
     if (st != kSuccess) return st;
     const std::uint32_t grid =
         min(p.tiles, static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
-    kernel<<<grid, kThreads, smem_bytes(static_cast<int>(p.x_bytes), NT, STAGES), stream>>>(p);
-    return static_cast<int>(cudaGetLastError());
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes(static_cast<int>(p.x_bytes), NT, STAGES);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, p));
 }
 
 template <bool XF32, bool OF32, int EPI, int NT>

@@ -366,6 +366,84 @@ class Bench:
         return {"us_per_layer": round(ms * 1e3, 3), "gbs": round(nbytes / ms / 1e6, 1),
                 "bytes": nbytes, "copies": r}
 
+    def torch_view(self, ptr: int, nbytes: int):
+        """A uint8 torch view of device memory owned by a mote_b200 context."""
+        class _Array:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                        "data": (ptr, False), "strides": None, "version": 3}
+
+        return self.torch.as_tensor(_Array(), device=self.dev)
+
+    def config4(self) -> dict:
+        """Decoder-layer chain at M=1 (Llama-3.2-1B shapes) through
+        mote_b200.decoder: a stack of layers with distinct weights holding
+        >= 2.5x L2, the first gathering its input from the embedding table and
+        each next one taking the previous layer's output.  One CUDA graph
+        replays the whole stack; us/layer = replay time / layers."""
+        torch = self.torch
+        from mote_b200 import decoder
+        from mote_b200.context import CudaContext
+        from mote_b200.types import DType, plain, quantized
+
+        ctx = CudaContext(self.local_rank)
+        shape = decoder.LayerShape()
+        hdim = shape.hidden
+        per_layer = shape.weight_bytes()
+        count = copies_for(per_layer)
+        table = ctx.empty(plain((shape.vocab, hdim), DType.F16))
+        self.torch_view(table.pointer, shape.vocab * hdim * 2).view(torch.float16).copy_(
+            self.randn((shape.vocab, hdim), 400, torch.float16, 0.02).reshape(-1))
+        layers = []
+        for i in range(count):
+            def q4(n, k, seed):
+                w = ctx.empty(quantized((n, k)))
+                self.encode_into(w.pointer, n, k, seed)
+                return w
+
+            gam = []
+            for j in range(2):
+                g = ctx.empty(plain((hdim,), DType.F16))
+                self.torch_view(g.pointer, hdim * 2).view(torch.float16).copy_(
+                    self.randn((hdim,), 500 + 2 * i + j, torch.float16, 0.1, 1.0))
+                gam.append(g)
+            s0 = 600 + 8 * i
+            layer = decoder.DecoderLayerQ4_0(
+                ctx, shape, embedding=table, w_qkv=q4(shape.qkv, hdim, s0),
+                w_o=q4(hdim, hdim, s0 + 1), w_gate=q4(shape.ffn, hdim, s0 + 2),
+                w_up=q4(shape.ffn, hdim, s0 + 3), w_down=q4(hdim, shape.ffn, s0 + 4),
+                gamma1=gam[0], gamma2=gam[1])
+            self.torch_view(layer.attn.pointer, hdim * 2).view(torch.float16).copy_(
+                self.randn((hdim,), 700 + i, torch.float16))
+            layers.append(layer)
+        torch.cuda.synchronize()
+        import numpy as np
+
+        ctx.upload_numpy(layers[0].ids, np.array([1234], np.int32))
+        for layer in layers:
+            layer.set_position(77)
+
+        def run():
+            layers[0].step()
+            for prev, layer in zip(layers, layers[1:]):
+                layer.step(prev.out)
+
+        run()
+        ctx.sync()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=torch.cuda.ExternalStream(ctx.stream)):
+            run()
+        # kernels per layer: rms_norm, QKV, 2 x RoPE, O, fused add+norm,
+        # gate/up+SwiGLU, down+residual; the first layer adds the gather
+        launches = 8 * count + 1
+        ms = self.time_graph(g, 20, launches) / count
+        assert ctx.device_status() == 0
+        del g, layers
+        return {"us_per_layer": round(ms * 1e3, 3),
+                "gbs": round(per_layer / ms / 1e6, 1), "weight_bytes_per_layer": per_layer,
+                "layers_in_stack": count,
+                "kernels_per_layer": 8,
+                "bytes": "Q4_0 weight bytes of QKV, O, gate, up, down (activations < 0.3%)"}
+
     def config5(self) -> dict:
         torch = self.torch
         k, n = 4096, 128256
@@ -452,6 +530,7 @@ class Bench:
         if self.rank == 0:
             extra["config1_f32_m1_k2048_n2048"] = self.config1()
             extra["config2_rmsnorm_rope_t512"] = self.config2()
+            extra["config4_decoder_layer_m1"] = self.config4()
             extra["config5"] = self.config5()
         e2e = self.e2e(max(3, min(args.steps, 20)))
         if self.rank == 0:

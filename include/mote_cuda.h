@@ -116,6 +116,15 @@ int mote_cuda_q4_0_gate_up_swiglu_f16(const void* input, const void* gate_weight
                                       uint64_t ffn_features, uint64_t input_features,
                                       void* stream);
 
+/* output[rows, N] = input * weights^T + residual (f16 in, f16 residual and
+ * output, f32 accumulation, one rounding).  No reference counterpart: the
+ * decoder layer's down projection with its residual add.  output may equal
+ * residual.  Null residual -> 1; otherwise the linear entry points' rules. */
+int mote_cuda_quantized_linear_q4_0_f16_residual(const void* input, const void* weights,
+                                                 const void* residual, void* output,
+                                                 uint64_t rows, uint64_t output_features,
+                                                 uint64_t input_features, void* stream);
+
 /* Decodes Q4_0 [rows, K] to f32, bit-identical to mote-reference's
  * dequantize_quantized_row (crates/mote-reference/src/quantized.rs:58-74). */
 int mote_cuda_q4_0_decode_f32(const void* weights, void* output, uint64_t rows,

@@ -194,6 +194,16 @@ class CudaContext:
     def from_numpy(self, desc: TensorDesc, array: np.ndarray) -> Tensor:
         return self.from_bytes(desc, np.ascontiguousarray(array))
 
+    def upload_numpy(self, tensor: Tensor, array: np.ndarray) -> None:
+        """Synchronous host-to-device copy into an existing tensor."""
+        buf = np.ascontiguousarray(array).view(np.uint8).reshape(-1)
+        if buf.nbytes != tensor.desc.required_span_bytes:
+            raise errors.ByteLengthMismatch(expected=tensor.desc.required_span_bytes,
+                                            actual=buf.nbytes)
+        self.sync()
+        errors.check(lib().mote_cuda_memcpy_host_to_device(tensor.pointer, buf.ctypes.data,
+                                                           buf.nbytes), "upload")
+
     def read_bytes(self, tensor: Tensor) -> bytes:
         storage = self.storage(tensor)
         return storage.read_bytes()[: tensor.desc.required_span_bytes]

@@ -60,12 +60,13 @@ constexpr int kSmemPerSm = 233472;                          // 228 KB per SM
 constexpr int kSmemReservedPerCta = 1024;                   // system use per resident CTA
 constexpr int kMaxXRows = 16;                               // two n8 tiles
 
-enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1 };
+enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1, kEpiResidual = 2 };
 
 struct Params {
     const void* x;            // [M, K] f16 or f32, row stride K
     const std::uint8_t* w;    // [N, K/32*18]
     const std::uint8_t* w2;   // second matrix (up projection) for kEpiSwiGLU
+    const __half* res;        // residual added by kEpiResidual, same layout as y
     void* y;                  // [M, ldy] f16 or f32
     std::uint32_t M;          // tokens in this launch
     std::uint32_t N;          // rows of w (and of w2)
@@ -174,7 +175,8 @@ __device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, 
                     for (int c = 0; c < 2; ++c) {
                         const std::uint32_t m = nt * 8 + 2 * t + c;
                         if (m >= p.M) continue;
-                        const float v = acc[nt][2 * half + c];
+                        float v = acc[nt][2 * half + c];
+                        if constexpr (EPI == kEpiResidual) v += __half2float(p.res[m * p.ldy + r]);
                         if constexpr (OF32)
                             static_cast<float*>(p.y)[m * p.ldy + r] = v;
                         else
@@ -470,6 +472,7 @@ __global__ void __launch_bounds__(128) q4_0_linear_generic_kernel(const Params p
         if (m >= p.M) break;
         float v = acc[0][mm];
         if constexpr (EPI == kEpiSwiGLU) v = silu_mul(acc[0][mm], acc[1][mm]);
+        if constexpr (EPI == kEpiResidual) v += __half2float(p.res[m * p.ldy + warp_global]);
         if constexpr (OF32)
             static_cast<float*>(p.y)[m * p.ldy + warp_global] = v;
         else
@@ -581,12 +584,19 @@ inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, std::uint32_t
 // activation staging allows (consecutive launches on the same stream).
 template <bool XF32, bool OF32, int EPI>
 int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint64_t M,
-               std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream) {
+               std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream,
+               const void* res = nullptr) {
     const std::size_t osz = OF32 ? 4 : 2;
     if (K == 0) {
         // Every dot product is empty: the reference writes zeros
         // (crates/mote-backend-hip/tests/quantized_linear.rs:142-158).  For
         // SwiGLU silu(0) * 0 = 0 as well.
+        if constexpr (EPI == kEpiResidual) {
+            // empty dot products: y = residual
+            if (y == res) return kSuccess;
+            return static_cast<int>(cudaMemcpy2DAsync(y, ldy * osz, res, ldy * osz, N * osz, M,
+                                                      cudaMemcpyDeviceToDevice, stream));
+        }
         return static_cast<int>(cudaMemset2DAsync(y, ldy * osz, 0, N * osz, M, stream));
     }
     // Prefill-shaped problems (more tokens than one GEMV launch stages) run as
@@ -598,6 +608,7 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     }
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
+    p.res = static_cast<const __half*>(res);
     p.w2 = static_cast<const std::uint8_t*>(w2);
     p.N = static_cast<std::uint32_t>(N);
     p.K = K;
@@ -620,6 +631,7 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         p.M = static_cast<std::uint32_t>(mc);
         p.x = static_cast<const std::uint8_t*>(x) + m0 * K * xes;
         p.y = static_cast<std::uint8_t*>(y) + m0 * ldy * osz;
+        if (res != nullptr) p.res = static_cast<const __half*>(res) + m0 * ldy;
         int st;
         if (fast) {
             p.x_rows = static_cast<std::uint32_t>(mc) * (XF32 ? 2 : 1);
@@ -711,4 +723,27 @@ extern "C" int mote_cuda_q4_0_gate_up_swiglu_f16(const void* input, const void* 
     return run_linear<false, false, kEpiSwiGLU>(input, gate_weights, up_weights, output, rows,
                                                 ffn_features, input_features, ffn_features,
                                                 static_cast<cudaStream_t>(stream));
+}
+
+// output = input * weights^T + residual (f16 in, f16 residual/out, f32
+// accumulation, one rounding).  No reference counterpart: the decoder layer's
+// down projection with its residual add.  output may alias residual (each
+// element is read and written by the same thread); argument rules as the
+// linear entry points, plus a null residual is an invalid value.
+extern "C" int mote_cuda_quantized_linear_q4_0_f16_residual(const void* input, const void* weights,
+                                                            const void* residual, void* output,
+                                                            std::uint64_t rows,
+                                                            std::uint64_t output_features,
+                                                            std::uint64_t input_features,
+                                                            void* stream) {
+    using namespace mote::q4;
+    if (residual == nullptr) return mote::kInvalidValue;
+    const int c = check_linear_args(input, weights, output, rows, output_features,
+                                    input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    return run_linear<false, false, kEpiResidual>(input, weights, nullptr, output, rows,
+                                                  output_features, input_features,
+                                                  output_features,
+                                                  static_cast<cudaStream_t>(stream), residual);
 }

@@ -102,6 +102,7 @@ _ARG_KINDS = {
     "mote_cuda_quantized_linear_q4_0_f16_f32out": "pppuuup",
     "mote_cuda_quantized_linear_q4_0_f32": "pppuuup",
     "mote_cuda_q4_0_gate_up_swiglu_f16": "ppppuuup",
+    "mote_cuda_quantized_linear_q4_0_f16_residual": "ppppuuup",
     "mote_cuda_rms_norm_f16": "pppuufp",
     "mote_cuda_fused_add_rms_norm_f16": "ppppuufp",
     "mote_cuda_rope_f16": "ppppuuuuwp",
@@ -119,6 +120,7 @@ CUDA_KERNELS = {
     ("quantized_linear_q4_0_f32out", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_f32out",
     ("quantized_linear_q4_0", DType.F32): "mote_cuda_quantized_linear_q4_0_f32",
     ("gate_up_swiglu_q4_0", DType.F16): "mote_cuda_q4_0_gate_up_swiglu_f16",
+    ("quantized_linear_q4_0_residual", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_residual",
     ("rms_norm", DType.F16): "mote_cuda_rms_norm_f16",
     ("fused_add_rms_norm", DType.F16): "mote_cuda_fused_add_rms_norm_f16",
     ("rope", DType.F16): "mote_cuda_rope_f16",

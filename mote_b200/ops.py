@@ -126,6 +126,38 @@ def quantized_linear_q4_0_f32(context: CudaContext, input: Tensor, weights: Tens
     quantized_linear_q4_0(context, input, weights, output, DType.F32, DType.F32)
 
 
+def quantized_linear_q4_0_f16_residual(context: CudaContext, input: Tensor, weights: Tensor,
+                                       residual: Tensor, output: Tensor) -> None:
+    """``output = input @ weights^T + residual`` (f16, one rounding).
+
+    ``output`` may be ``residual`` (in-place residual update) but must not
+    share storage with ``input`` or ``weights``.
+    """
+    _plain(input, "input", DType.F16)
+    _rank(input, "input", 2)
+    _q4_0_matrix(weights)
+    _plain(residual, "residual", DType.F16)
+    _plain(output, "output", DType.F16)
+    rows, k = input.shape
+    n, wk = weights.shape
+    if wk != k:
+        raise errors.ShapeMismatch(tensor="weights", expected=(n, k), actual=weights.shape)
+    _shape(output, "output", (rows, n))
+    _shape(residual, "residual", (rows, n))
+    in_s, w_s, r_s, out_s = (context.storage(t) for t in (input, weights, residual, output))
+    _not_aliased(output, "output", input, "input")
+    _not_aliased(output, "output", weights, "weights")
+    if rows * n > U32_MAX:
+        raise errors.QuantizedLinearDimensionsTooLarge(rows=rows, output_features=n,
+                                                       input_features=k)
+    if rows * n == 0:
+        return
+    context.inner.select()
+    errors.check(lib().mote_cuda_quantized_linear_q4_0_f16_residual(
+        in_s.pointer, w_s.pointer, r_s.pointer, out_s.pointer, rows, n, k, context.stream),
+        "launch Q4_0 linear + residual kernel")
+
+
 def q4_0_gate_up_swiglu_f16(context: CudaContext, input: Tensor, gate: Tensor, up: Tensor,
                             output: Tensor) -> None:
     """``output = silu(input @ gate^T) * (input @ up^T)`` in one kernel."""

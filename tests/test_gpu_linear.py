@@ -227,3 +227,37 @@ def test_unaligned_weights_use_generic_path(ctx, oracle_lib):
     got = np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(2, n)
     ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w, n, k))
     assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND
+
+
+@pytest.mark.parametrize("m,n,k,in_place", [(1, 2048, 8192, False), (4, 2048, 8192, True),
+                                            (16, 200, 512, False), (24, 96, 1280, True),
+                                            (3, 40, 96, False)])
+def test_residual_epilogue(ctx, oracle_lib, m, n, k, in_place):
+    """``y = x @ W^T + r`` with one f16 rounding (fast, multi-launch and
+    generic paths; output aliasing the residual)."""
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=90 + m)
+    x = fx.activations(m, k, seed=91 + m).astype(np.float16)
+    r = np.random.default_rng(92 + m).normal(0, 1, (m, n)).astype(np.float16)
+    xt = ctx.from_bytes(plain((m, k), DType.F16), x)
+    wt = ctx.from_bytes(quantized((n, k)), w)
+    rt = ctx.from_bytes(plain((m, n), DType.F16), r)
+    yt = rt if in_place else ctx.empty(plain((m, n), DType.F16))
+    ops.quantized_linear_q4_0_f16_residual(ctx, xt, wt, rt, yt)
+    got = np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(m, n)
+    assert ctx.device_status() == 0
+    acc = oracle_linear(oracle_lib, x.astype(np.float32), w, m, n, k)
+    want = checker.f16_round(acc + r.astype(np.float32))
+    ok, bad = checker.within_reference_tolerance(got, want, 0.01, 0.002)
+    assert ok, bad
+    ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w, n, k)) + r
+    assert checker.rel_err_normwise(got, ref64) <= 1e-3
+
+
+def test_residual_zero_input_features_copies_residual(ctx):
+    xt = ctx.from_bytes(plain((3, 0), DType.F16), b"")
+    wt = ctx.from_bytes(quantized((2, 0)), b"")
+    r = np.arange(6, dtype=np.float16)
+    rt = ctx.from_bytes(plain((3, 2), DType.F16), r)
+    yt = ctx.from_bytes(plain((3, 2), DType.F16), np.full(6, 7.0, np.float16))
+    ops.quantized_linear_q4_0_f16_residual(ctx, xt, wt, rt, yt)
+    assert np.array_equal(np.frombuffer(ctx.read_bytes(yt), np.float16), r)

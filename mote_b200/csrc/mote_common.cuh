@@ -167,6 +167,35 @@ __device__ __forceinline__ std::uint32_t lds32(std::uint32_t addr) {
     return v;
 }
 
+// Shared loads at base + a compile-time byte offset: the offset goes into
+// the instruction's immediate field instead of a separate address add.
+template <int OFF>
+__device__ __forceinline__ std::uint32_t lds32i(std::uint32_t base) {
+    std::uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+
+template <int OFF>
+__device__ __forceinline__ uint2 lds64i(std::uint32_t base) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(base), "n"(OFF));
+    return v;
+}
+
+template <int OFF>
+__device__ __forceinline__ std::uint32_t lds16i(std::uint32_t base) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1+%2];" : "=h"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+
+__device__ __forceinline__ std::uint32_t lds16(std::uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ uint2 lds64(std::uint32_t addr) {
     uint2 v;
     asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));

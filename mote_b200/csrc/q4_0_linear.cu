@@ -7,23 +7,29 @@
 //   crates/mote-reference/src/quantized.rs:177-201.)
 //
 // Design (B200, HBM-bound):
-// * Persistent kernel: one 8-warp CTA per SM walks over tiles of 16 weight
-//   rows.  Every warp owns a fixed K-slice of every tile and streams its
-//   slice of the 16 rows through a private shared-memory ring with 1-D bulk
-//   copies (cp.async.bulk on the TMA engine, one copy per row per stage,
-//   completion on an mbarrier per slot, L2 evict-first).  The ring runs
-//   continuously across tiles, so the copy pipeline never drains; weights
-//   are read from HBM exactly once in 144/288-byte contiguous runs.
+// * Persistent kernel: 8-warp CTAs (two per SM when shared memory allows)
+//   walk over tiles of 16 weight rows.  Every warp owns a fixed K-slice of
+//   every tile and streams its slice of the 16 rows through a private
+//   shared-memory ring: each lane issues 16-byte cp.async copies (L2
+//   evict-first), one commit group per 144-byte-per-row stage.  The ring
+//   runs continuously across tiles, so the copy pipeline never drains;
+//   weights are read from HBM exactly once.
 // * The activations (up to 16 rows, f16) are staged into shared memory once
 //   per CTA, with padded rows that make the fragment loads bank-conflict
-//   free.
+//   free, plus one all-zero row.
 // * Dequantization happens in registers: each lane decodes one 4-byte quant
-//   word per row per block into exact f16 integers (q - 8) with PRMT + LOP3
-//   + HSUB2 (the 1024+q / 64+q exponent tricks), and the warp issues
-//   mma.sync.m16n8k16 (f16 x f16 -> f32) with the weights as the A operand
-//   and 8 activation rows per n8 tile as B.  The f16 block scale multiplies
-//   the f32 block partial (FFMA): products and scaling are exact, only the
-//   f32 accumulation rounds.
+//   word per row per block into exact f16 integers (q - 8) with LOP3 + HSUB2
+//   (the 1024+q / 64+q exponent tricks), and the warp issues
+//   mma.sync.m16n8k16 (f16 x f16 -> f32) with the weights as the A operand.
+//   The f16 block scale multiplies the f32 block partial (FFMA): products
+//   and scaling are exact, only the f32 accumulation rounds.
+// * Column packing: with 8 or fewer activation rows the eight B columns
+//   carry 8/MC consecutive blocks x MC rows (MC = 1, 2, 4 or 8), the other
+//   lanes reading the zero row, so one MMA chain covers 8/MC blocks with
+//   every column holding a single block's exact partial.  The scale FFMAs,
+//   scale loads and accumulator resets then run once per chain instead of
+//   once per block; a lane shuffle folds the columns back per row at the
+//   end of a tile.
 // * The k-slot permutation inside each 16-wide MMA makes a lane's B
 //   fragment 4 consecutive activations (one 8-byte load) and its A fragment
 //   one 4-byte quant word; A and B share the permutation, so the dot product
@@ -33,6 +39,8 @@
 // * The eight K-slice partials of a tile meet in a double-buffered shared
 //   reduction area behind one named barrier; the warps take turns writing
 //   finished tiles, so the others keep streaming.
+// * Programmatic dependent launch: the ring prologue (weights only) runs
+//   before griddepcontrol.wait, overlapping the previous kernel's tail.
 //
 // Fast-path requirements: K a multiple of 256 (whole 144-byte, 16-byte
 // aligned groups of 8 blocks per row), 16-byte aligned weights and
@@ -41,6 +49,7 @@
 #include "mote_common.cuh"
 
 #include <atomic>
+#include <type_traits>
 
 namespace mote {
 namespace q4 {
@@ -51,10 +60,10 @@ constexpr int kTileRows = 16;
 constexpr int kUnitBlocks = 8;            // 8 blocks = 256 elements = 144 bytes
 constexpr int kUnitBytes = kUnitBlocks * 18;
 constexpr int kStageUnits = 1;            // 8 blocks per stage
-// Padded row stride: 176 / 4 = 44 words = 12 (mod 32) banks apart, so the 8
-// rows a warp reads at once land in 8 disjoint groups of 4 banks.
-constexpr int kRowStride = kStageUnits * kUnitBytes + 32;  // 176
-constexpr int kStageBytes = kTileRows * kRowStride;         // 2816
+// Dense 144-byte rows: 36 words = 4 (mod 32) banks apart, so the 8 rows a
+// warp reads at once (word t of row g: bank 4g + t) hit 32 distinct banks.
+constexpr int kRowStride = kStageUnits * kUnitBytes;        // 144
+constexpr int kStageBytes = kTileRows * kRowStride;         // 2304
 constexpr int kMaxSmem = 232448;                            // 227 KB per-CTA opt-in limit
 constexpr int kSmemPerSm = 233472;                          // 228 KB per SM
 constexpr int kSmemReservedPerCta = 1024;                   // system use per resident CTA
@@ -79,6 +88,7 @@ struct Params {
     std::uint32_t x_stride;   // bytes per shared activation row (2K + 32)
     std::uint32_t x_bytes;    // (x_zero_row + 1) * x_stride rounded up to 128
     std::uint32_t x_zero_row; // index of the all-zero row after the staged rows
+    std::uint32_t split_shift; // log2 of the warps sharing a tile's K (0..3)
 };
 
 __host__ __device__ constexpr int red_bytes(int nt) { return 2 * kWarps * nt * 4 * 32 * 4; }
@@ -196,11 +206,20 @@ __device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, 
     }
 }
 
+// Compile-time loop: f(std::integral_constant<int, I>) for I in [B, E).
+template <int B, int E, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (B < E) {
+        f(std::integral_constant<int, B>{});
+        static_for<B + 1, E>(f);
+    }
+}
+
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int NT, bool XF32, bool OF32, int EPI, int STAGES>
+template <int NT, int MC, bool XF32, bool OF32, int EPI, int STAGES>
 __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) {
     extern __shared__ __align__(1024) std::uint8_t smem[];
     const int warp = threadIdx.x >> 5;
@@ -212,10 +231,19 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
     std::uint8_t* ring = smem + p.x_bytes + warp * STAGES * kStageBytes;
     float* red = reinterpret_cast<float*>(smem + p.x_bytes + kWarps * STAGES * kStageBytes);
 
-    const std::uint32_t my_tiles =
-        p.tiles > blockIdx.x ? (p.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-    const std::uint32_t u0 = (p.units * warp) / kWarps;
-    const std::uint32_t u1 = (p.units * (warp + 1)) / kWarps;
+    // Split-K: the CTA's warps form kWarps / split groups of `split` warps;
+    // a group walks its own tiles (first, first + stride, ...; groups are
+    // interleaved across CTAs so small problems spread over every SM) and
+    // warp wig of the group owns units [u0, u1) of every one of them.
+    const std::uint32_t sh = p.split_shift;
+    const std::uint32_t split = 1u << sh;
+    const std::uint32_t grp = static_cast<std::uint32_t>(warp) >> sh;
+    const std::uint32_t wig = static_cast<std::uint32_t>(warp) & (split - 1);
+    const std::uint32_t first = blockIdx.x + grp * gridDim.x;
+    const std::uint32_t stride = gridDim.x * (kWarps >> sh);
+    const std::uint32_t my_tiles = p.tiles > first ? (p.tiles - first + stride - 1) / stride : 0;
+    const std::uint32_t u0 = (p.units * wig) >> sh;
+    const std::uint32_t u1 = (p.units * (wig + 1)) >> sh;
     const std::uint32_t spt = u1 - u0;  // stages (units) per tile
     const std::uint32_t total = my_tiles * spt;
     const std::uint64_t policy = l2_evict_first_policy();
@@ -236,33 +264,40 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
         src_off[j] = (c % 9) * 16;
     }
     const std::uint32_t ring_s = smem_u32(ring);
-    std::uint32_t cached_tile = 0xffffffffu;
-    const std::uint8_t* row_ptr[kChunksPerLane];
-    auto issue = [&](std::uint32_t s) {
-        if (s < total) {
-            const std::uint32_t tl = s / spt;
-            const std::uint32_t tile = blockIdx.x + tl * gridDim.x;
-            if (tile != cached_tile) {
-                cached_tile = tile;
+    // Issue cursor: the next stage to fetch is unit u0 + iss_u of this CTA's
+    // tile number iss_tl; src[j] already points at its chunk j.
+    std::uint32_t iss_n = 0, iss_tl = 0, iss_u = 0, iss_slot = 0;
+    const std::uint8_t* src[kChunksPerLane];
+    auto seek_tile = [&](std::uint32_t tl) {
+        const std::uint32_t tile = first + tl * stride;
 #pragma unroll
-                for (int j = 0; j < kChunksPerLane; ++j)
-                    row_ptr[j] = tile_row<EPI>(p, tile, chunk_row[j]);
-            }
-            const std::uint32_t ua = u0 + (s - tl * spt);
-            const std::uint32_t slot_s = ring_s + (s % STAGES) * kStageBytes;
+        for (int j = 0; j < kChunksPerLane; ++j)
+            src[j] = tile_row<EPI>(p, tile, chunk_row[j]) + static_cast<std::uint64_t>(u0) * kUnitBytes +
+                     src_off[j];
+    };
+    if (total > 0) seek_tile(0);
+    auto issue = [&]() {
+        if (iss_n < total) {
+            const std::uint32_t slot_s = ring_s + iss_slot * kStageBytes;
 #pragma unroll
             for (int j = 0; j < kChunksPerLane; ++j)
-                if (lane + 32 * j < kChunks)
-                    cp_async_16(slot_s + dst_off[j],
-                                row_ptr[j] + static_cast<std::uint64_t>(ua) * kUnitBytes + src_off[j],
-                                policy);
+                if (lane + 32 * j < kChunks) cp_async_16(slot_s + dst_off[j], src[j], policy);
+            if (++iss_u == spt) {
+                iss_u = 0;
+                if (iss_n + 1 < total) seek_tile(++iss_tl);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kChunksPerLane; ++j) src[j] += kUnitBytes;
+            }
         }
+        ++iss_n;
+        iss_slot = iss_slot + 1 == STAGES ? 0 : iss_slot + 1;
         cp_async_commit();
     };
     // Weights do not depend on the previous kernel in the stream: start
     // streaming them, let the next kernel launch, and only then wait for the
     // producer of the activations.
-    for (std::uint32_t s = 0; s + 1 < STAGES; ++s) issue(s);
+    for (int s = 0; s + 1 < STAGES; ++s) issue();
     pdl_launch_dependents();
     pdl_wait();
 
@@ -273,6 +308,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
     {
         const std::uint32_t groups = static_cast<std::uint32_t>(p.K / 4);
         const std::uint32_t total_groups = p.M * groups;
+
         for (std::uint32_t i = threadIdx.x; i < total_groups; i += kThreads) {
             const std::uint32_t m = i / groups;
             const std::uint32_t gi = i - m * groups;
@@ -306,26 +342,37 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-    // Shared address of this lane's B fragments (row nt*8+g, group t).  Rows
-    // past the staged ones read the zero row at the end of the staging area,
-    // so every lane loads unconditionally.
-    std::uint32_t xaddr[NT];
+    // Column packing.  B column n = g of this lane is activation row
+    // (nt*8 + g) when MC = 8; with MC < 8 staged rows, the 8 columns are
+    // BC = 8/MC consecutive blocks x MC rows (n = j*MC + m): for block j of a
+    // chain only the lanes with g/MC == j see real activations, the others
+    // read the zero row, so one MMA chain accumulates BC blocks into
+    // disjoint columns and each column still holds one block's exact partial.
+    // xsel[nt][j] is this lane's shared address for chain position j.
+    constexpr int BC = 8 / MC;
+    static_assert(MC == 8 || NT == 1, "column packing needs a single n8 tile");
+    std::uint32_t xsel[NT][BC];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const std::uint32_t row = nt * 8 + g;
-        xaddr[nt] = smem_u32(xs) + (row < p.x_rows ? row : p.x_zero_row) * p.x_stride + 8 * t;
-    }
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < BC; ++j) {
+            const std::uint32_t row = nt * 8 + g % MC;
+            const bool real = (g / MC == j) && row < p.x_rows;
+            xsel[nt][j] = smem_u32(xs) + (real ? row : p.x_zero_row) * p.x_stride + 8 * t;
+        }
+    // Blocks whose scales this lane applies: columns 2t and 2t+1 belong to
+    // chain positions (2t)/MC and (2t+1)/MC.
+    const std::uint32_t doff0 = 18u * static_cast<std::uint32_t>((2 * t) / MC);
+    const std::uint32_t doff1 = 18u * static_cast<std::uint32_t>((2 * t + 1) / MC);
     const std::uint32_t ring_addr = smem_u32(ring) + g * kRowStride;
 
-    std::uint32_t s = 0;
+    std::uint32_t slot = 0;
     for (std::uint32_t tl = 0; tl < my_tiles; ++tl) {
-        for (std::uint32_t st = 0; st < spt; ++st, ++s) {
-            const int slot = s % STAGES;
+        for (std::uint32_t st = 0; st < spt; ++st) {
             // Keep STAGES-1 stages in flight: refill the slot freed by the
             // previous stage, then wait for this one (own groups only; the
             // warp's lanes together fetched the stage).
-            issue(s + STAGES - 1);
+            issue();
             cp_async_wait<STAGES - 1>();
             __syncwarp();
             {
@@ -335,55 +382,102 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
                 const std::uint32_t qa = ra + 4 * t;
                 constexpr std::uint32_t kR8 = 8 * kRowStride;
                 const std::uint32_t xo = (u0 + st) * (kUnitBlocks * 64);
+                std::uint32_t xs_j[NT][BC];  // this lane's B rows for this unit
 #pragma unroll
-                for (int pr = 0; pr < kUnitBlocks / 2; ++pr) {
-                    const std::uint32_t o = pr * 36;
-                    const std::uint32_t a_d0 = lds32(ra + o), a_d1 = lds32(ra + o + 16);
-                    const std::uint32_t a_q0 = lds32(qa + o), a_q1 = lds32(qa + o + 4),
-                                        a_q2 = lds32(qa + o + 20);
-                    const std::uint32_t b_d0 = lds32(ra + kR8 + o), b_d1 = lds32(ra + kR8 + o + 16);
-                    const std::uint32_t b_q0 = lds32(qa + kR8 + o), b_q1 = lds32(qa + kR8 + o + 4),
-                                        b_q2 = lds32(qa + kR8 + o + 20);
-                    uint2 bx[NT][2][2];
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+                    for (int j = 0; j < BC; ++j) xs_j[nt][j] = xsel[nt][j] + xo;
+                const std::uint32_t da0 = ra + doff0;
+                const std::uint32_t da1 = ra + doff1;
+                // Long chains (8/MC >= 4 blocks) keep the low- and high-nibble
+                // MMAs in two accumulators so consecutive MMAs are independent.
+                constexpr int NCH = BC >= 4 ? 2 : 1;
+                static_for<0, kUnitBlocks / BC>([&](auto cc) {
+                    constexpr int c = decltype(cc)::value;
+                    float dacc[NCH][NT][4];
 #pragma unroll
-                        for (int blk = 0; blk < 2; ++blk) {
-                            const std::uint32_t xb = xaddr[nt] + xo + (pr * 2 + blk) * 64;
-                            bx[nt][blk][0] = lds64(xb);
-                            bx[nt][blk][1] = lds64(xb + 32);
+                    for (int h = 0; h < NCH; ++h)
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+                            dacc[h][nt][0] = dacc[h][nt][1] = dacc[h][nt][2] = dacc[h][nt][3] = 0.f;
+
+                    static_for<0, BC>([&](auto jj) {
+                        constexpr int j = decltype(jj)::value;
+                        constexpr int b = c * BC + j;
+                        // Quant word t of block b (qs at byte 18b + 2): aligned
+                        // for odd b, straddling two words for even b.
+                        std::uint32_t wa, wb;
+                        if constexpr (b & 1) {
+                            wa = lds32i<18 * b + 2>(qa);
+                            wb = lds32i<kR8 + 18 * b + 2>(qa);
+                        } else {
+                            wa = prmt(lds32i<18 * b>(qa), lds32i<18 * b + 4>(qa), 0x5432u);
+                            wb = prmt(lds32i<kR8 + 18 * b>(qa), lds32i<kR8 + 18 * b + 4>(qa),
+                                      0x5432u);
                         }
-                    // scales of rows (g, g+8) for the even and the odd block
-                    const float2 d0 = half2_bits_to_float2(prmt(a_d0, b_d0, 0x5410u));
-                    const float2 d1 = half2_bits_to_float2(prmt(a_d1, b_d1, 0x7632u));
-#pragma unroll
-                    for (int blk = 0; blk < 2; ++blk) {
-                        // even block: quant words straddle a 4-byte boundary
-                        const std::uint32_t wa = blk == 0 ? prmt(a_q0, a_q1, 0x5432u) : a_q2;
-                        const std::uint32_t wb = blk == 0 ? prmt(b_q0, b_q1, 0x5432u) : b_q2;
-                        const float2 d = blk == 0 ? d0 : d1;
                         std::uint32_t al02, al13, ah02, ah13, bl02, bl13, bh02, bh13;
                         decode_word(wa, al02, al13, ah02, ah13);
                         decode_word(wb, bl02, bl13, bh02, bh13);
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt) {
-                            float tmp[4];
-                            mma_16816(tmp, al02, bl02, al13, bl13, bx[nt][blk][0].x,
-                                      bx[nt][blk][0].y, zero);
-                            mma_16816(tmp, ah02, bh02, ah13, bh13, bx[nt][blk][1].x,
-                                      bx[nt][blk][1].y, tmp);
-                            acc[nt][0] = fmaf(d.x, tmp[0], acc[nt][0]);
-                            acc[nt][1] = fmaf(d.x, tmp[1], acc[nt][1]);
-                            acc[nt][2] = fmaf(d.y, tmp[2], acc[nt][2]);
-                            acc[nt][3] = fmaf(d.y, tmp[3], acc[nt][3]);
+                            const uint2 xl = lds64i<b * 64>(xs_j[nt][j]);
+                            const uint2 xh = lds64i<b * 64 + 32>(xs_j[nt][j]);
+                            mma_16816(dacc[0][nt], al02, bl02, al13, bl13, xl.x, xl.y,
+                                      dacc[0][nt]);
+                            mma_16816(dacc[NCH - 1][nt], ah02, bh02, ah13, bh13, xh.x, xh.y,
+                                      dacc[NCH - 1][nt]);
                         }
+                    });
+                    // Scale each column's block partial by its block's d.
+                    constexpr int cb = 18 * (c * BC);
+                    const float dg0 = half_bits_to_float(lds16i<cb>(da0));
+                    const float dh0 = half_bits_to_float(lds16i<cb + kR8>(da0));
+                    float dg1 = dg0, dh1 = dh0;
+                    if constexpr (MC == 1) {
+                        dg1 = half_bits_to_float(lds16i<cb>(da1));
+                        dh1 = half_bits_to_float(lds16i<cb + kR8>(da1));
                     }
-                }
+#pragma unroll
+                    for (int h = 0; h < NCH; ++h)
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            acc[nt][0] = fmaf(dg0, dacc[h][nt][0], acc[nt][0]);
+                            acc[nt][1] = fmaf(dg1, dacc[h][nt][1], acc[nt][1]);
+                            acc[nt][2] = fmaf(dh0, dacc[h][nt][2], acc[nt][2]);
+                            acc[nt][3] = fmaf(dh1, dacc[h][nt][3], acc[nt][3]);
+                        }
+                });
             }
             __syncwarp();  // the slot is refilled by the next iteration's issue
+            slot = slot + 1 == STAGES ? 0 : slot + 1;
         }
-        // Meet the other K-slices of this tile.
-        float* mine = red + ((tl & 1u) * kWarps + warp) * (NT * 4 * 32);
+        // Fold packed columns back to one value per activation row, in the
+        // unpacked layout (lane t holds rows 2t, 2t+1): rows of a column
+        // group live in lanes with equal (2t) % MC.
+        if constexpr (MC < 8) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if constexpr (MC == 1) {
+                    if (i & 1) continue;
+                    acc[0][i] += acc[0][i + 1];
+                    acc[0][i + 1] = 0.f;
+                }
+                if constexpr (MC <= 2) acc[0][i] += __shfl_xor_sync(0xffffffffu, acc[0][i], 1);
+                acc[0][i] += __shfl_xor_sync(0xffffffffu, acc[0][i], 2);
+            }
+        }
+        const std::uint32_t tile = first + tl * stride;
+        if (split == 1) {  // the warp covered all of K
+            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, acc);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+            continue;
+        }
+        // Meet the group's other K-slices in its double-buffered reduction
+        // area: the writer of buffer b for tile tl+2 passes tile tl+1's
+        // barrier only after the reducer of tile tl has read buffer b.
+        float* gred = red + grp * 2 * split * (NT * 4 * 32);
+        float* mine = gred + ((tl & 1u) * split + wig) * (NT * 4 * 32);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -391,20 +485,21 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
                 mine[(nt * 4 + i) * 32 + lane] = acc[nt][i];
                 acc[nt][i] = 0.f;
             }
-        named_barrier_sync(1, kThreads);
-        if (static_cast<int>(tl % kWarps) == warp) {
+        named_barrier_sync(1 + static_cast<int>(grp), static_cast<int>(split) * 32);
+        if ((tl & (split - 1)) == wig) {
             float sum[NT][4];
-            const float* base = red + (tl & 1u) * kWarps * (NT * 4 * 32);
+            const float* base = gred + (tl & 1u) * split * (NT * 4 * 32);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float v = 0.f;
+                for (int i = 0; i < 4; ++i) sum[nt][i] = 0.f;
+            for (std::uint32_t w = 0; w < split; ++w)
 #pragma unroll
-                    for (int w = 0; w < kWarps; ++w) v += base[w * (NT * 4 * 32) + (nt * 4 + i) * 32 + lane];
-                    sum[nt][i] = v;
-                }
-            store_tile<NT, XF32, OF32, EPI>(p, blockIdx.x + tl * gridDim.x, g, t, sum);
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        sum[nt][i] += base[w * (NT * 4 * 32) + (nt * 4 + i) * 32 + lane];
+            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, sum);
         }
     }
 }
@@ -512,14 +607,15 @@ inline int sm_count() {
     return v;
 }
 
-template <int NT, bool XF32, bool OF32, int EPI, int STAGES>
+template <int NT, int MC, bool XF32, bool OF32, int EPI, int STAGES>
 int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
-    auto kernel = q4_0_gemv_kernel<NT, XF32, OF32, EPI, STAGES>;
+    auto kernel = q4_0_gemv_kernel<NT, MC, XF32, OF32, EPI, STAGES>;
     static std::atomic<std::uint64_t> configured{0};
     const int st = ensure_smem_attribute(kernel, kMaxSmem, configured);
     if (st != kSuccess) return st;
-    const std::uint32_t grid =
-        min(p.tiles, static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
+    const std::uint32_t groups = kWarps >> p.split_shift;
+    const std::uint32_t grid = min((p.tiles + groups - 1) / groups,
+                                   static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -533,19 +629,24 @@ int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
     return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, p));
 }
 
-template <bool XF32, bool OF32, int EPI, int NT>
+template <bool XF32, bool OF32, int EPI, int NT, int MC>
 int launch_gemv_stages(const Params& p, int stages, int ctas, cudaStream_t stream) {
     switch (stages) {
-        case 4: return launch_gemv<NT, XF32, OF32, EPI, 4>(p, ctas, stream);
-        case 3: return launch_gemv<NT, XF32, OF32, EPI, 3>(p, ctas, stream);
-        default: return launch_gemv<NT, XF32, OF32, EPI, 2>(p, ctas, stream);
+        case 4: return launch_gemv<NT, MC, XF32, OF32, EPI, 4>(p, ctas, stream);
+        case 3: return launch_gemv<NT, MC, XF32, OF32, EPI, 3>(p, ctas, stream);
+        default: return launch_gemv<NT, MC, XF32, OF32, EPI, 2>(p, ctas, stream);
     }
 }
 
+// Staged activation rows select the MMA column layout: more than 8 rows take
+// two n8 tiles; otherwise the rows are packed MC to a column group.
 template <bool XF32, bool OF32, int EPI>
-int launch_gemv_config(const Params& p, int nt, int stages, int ctas, cudaStream_t stream) {
-    return nt == 1 ? launch_gemv_stages<XF32, OF32, EPI, 1>(p, stages, ctas, stream)
-                   : launch_gemv_stages<XF32, OF32, EPI, 2>(p, stages, ctas, stream);
+int launch_gemv_config(const Params& p, int stages, int ctas, cudaStream_t stream) {
+    if (p.x_rows > 8) return launch_gemv_stages<XF32, OF32, EPI, 2, 8>(p, stages, ctas, stream);
+    if (p.x_rows > 4) return launch_gemv_stages<XF32, OF32, EPI, 1, 8>(p, stages, ctas, stream);
+    if (p.x_rows > 2) return launch_gemv_stages<XF32, OF32, EPI, 1, 4>(p, stages, ctas, stream);
+    if (p.x_rows > 1) return launch_gemv_stages<XF32, OF32, EPI, 1, 2>(p, stages, ctas, stream);
+    return launch_gemv_stages<XF32, OF32, EPI, 1, 1>(p, stages, ctas, stream);
 }
 
 // Picks tokens per launch, n8 tiles and ring depth so the staged
@@ -578,6 +679,19 @@ inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, std::uint32_t
         if (m == 1) break;
     }
     return false;
+}
+
+// log2 of the warps per tile (split-K factor).  Measured on the decode
+// shapes (K = 2048..8192, 128..8016 tiles, 8 or 16 warps per SM), the best
+// split tracks 1.2 x (warps / tiles): about one round of tile groups with
+// every warp busy.  Small problems spread each tile over 8 warps; lm_head
+// sized ones give each warp whole tiles (no barrier, no partial sums).
+inline std::uint32_t choose_split_shift(std::uint32_t tiles, std::uint32_t units,
+                                        std::uint32_t ctas) {
+    const double r = 1.2 * kWarps * static_cast<double>(ctas) / static_cast<double>(tiles);
+    std::uint32_t sh = (r >= 1.4142) + (r >= 2.8284) + (r >= 5.6569);
+    while (sh > 0 && (1u << sh) > units) --sh;
+    return sh;
 }
 
 // Runs the linear for M rows of x, in as few persistent launches as the
@@ -625,6 +739,9 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     int nt = 1, stages = 2, ctas = 1;
     if (fast)
         fast = plan_gemv(M, K, XF32, tokens, nt, stages, ctas, p.x_rows, p.x_stride, p.x_bytes);
+    if (fast)
+        p.split_shift =
+            choose_split_shift(p.tiles, p.units, static_cast<std::uint32_t>(sm_count() * ctas));
     const std::uint64_t chunk = fast ? tokens : kGenericTokens * 65535ull;
     for (std::uint64_t m0 = 0; m0 < M; m0 += chunk) {
         const std::uint64_t mc = (M - m0 < chunk) ? (M - m0) : chunk;
@@ -636,7 +753,7 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         if (fast) {
             p.x_rows = static_cast<std::uint32_t>(mc) * (XF32 ? 2 : 1);
             p.x_zero_row = p.x_rows;
-            st = launch_gemv_config<XF32, OF32, EPI>(p, nt, stages, ctas, stream);
+            st = launch_gemv_config<XF32, OF32, EPI>(p, stages, ctas, stream);
         } else {
             const dim3 grid(static_cast<unsigned>((N + 3) / 4),
                             static_cast<unsigned>((mc + kGenericTokens - 1) / kGenericTokens));

@@ -71,6 +71,20 @@ def test_reference_fixture_3x5x64(ctx, oracle_lib):
 @pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9, 16, 17, 33, 64, 70])
 @pytest.mark.parametrize("n,k", [(40, 256), (2048, 2048), (96, 1280)])
 def test_fast_path_matches_oracle(ctx, oracle_lib, m, n, k):
+    _check_fast_path(ctx, oracle_lib, m, n, k)
+
+
+# Register-resident K-slices hold one unit (256 k) per warp for 16 tokens or
+# two for 8; longer K falls back to the staged kernel.  These shapes cover
+# both kernels and every warp split (K/256 = 9, 24, 32, 33, 56 units).
+@pytest.mark.parametrize("m,n,k", [(1, 1000, 2304), (8, 304, 6144), (9, 304, 6144),
+                                   (1, 520, 8192), (16, 520, 8192), (2, 64, 8448),
+                                   (1, 528, 14336), (12, 528, 14336)])
+def test_fast_path_kernel_splits(ctx, oracle_lib, m, n, k):
+    _check_fast_path(ctx, oracle_lib, m, n, k)
+
+
+def _check_fast_path(ctx, oracle_lib, m, n, k):
     w = fx.q4_0_weights(oracle_lib, n, k, seed=1000 + n + k)
     x = fx.activations(m, k, seed=7 + m).astype(np.float16)
     got = run_linear(ctx, x, w, m, n, k)

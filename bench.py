@@ -147,6 +147,8 @@ class Bench:
         if self.world > 1:
             import datetime
 
+            # plain NVLink transports only: no NVLink multicast objects
+            os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
             torch.distributed.init_process_group(
                 "nccl", timeout=datetime.timedelta(seconds=120),
                 device_id=self.dev)
@@ -480,6 +482,88 @@ class Bench:
                                 "tflops": round(flops / ms / 1e9, 1)}
         return out
 
+    def lm_head_sharded(self) -> dict:
+        """Config 5 at N > 1: lm_head rows split over the ranks (strong
+        scaling); per step each rank runs the GEMV on its shard and the f16
+        logits are all-gathered: with NCCL (mote_cuda_comm_*), with the
+        peer-store kernel, and fused into the GEMV epilogue (stores into
+        every rank's [M, N] logits over NVLink + flag handshake).  Steps are
+        captured in CUDA graphs; times are the max over ranks; GB/s counts
+        the full 295.5 MB weight once per step."""
+        torch = self.torch
+        import torch.distributed as dist
+
+        from mote_b200 import comm
+
+        k, n = 4096, 128256
+        sh = comm.shard_rows(n, self.world, self.rank)
+        w = self.encode_q4_0(sh.rows, k, seed=700 + self.rank)
+        fn = self.lib.mote_cuda_quantized_linear_q4_0_f16
+
+        def exchange(obj):
+            out = [None] * self.world
+            dist.all_gather_object(out, obj)
+            return out
+
+        nccl = comm.NcclAllGather(self.world, self.rank, exchange)
+        result = {"shard_rows": sh.rows, "world": self.world}
+        reps, steps = 10, 8
+        try:
+            for m in (1, 16, 64):
+                x = self.randn((m, k), 60 + m, torch.float16)
+                y = torch.empty((m, sh.rows), dtype=torch.float16, device=self.dev)
+                count = m * sh.rows
+                recv = torch.empty(self.world * count, dtype=torch.float16, device=self.dev)
+                peer = comm.PeerAllGather(self.world, self.rank, count, exchange)
+                fused = comm.ShardedLinearQ4_0(self.world, self.rank, m, n, k, exchange) \
+                    if m <= 16 else None
+
+                def gemv(x=x, y=y, m=m):
+                    self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, sh.rows, k,
+                                  self.stream()), "lm_head shard")
+
+                def run_gemv():
+                    for _ in range(steps):
+                        gemv()
+
+                def run_nccl(y=y, recv=recv, count=count):
+                    for _ in range(steps):
+                        gemv()
+                        nccl.all_gather(y.data_ptr(), recv.data_ptr(), count, self.stream())
+
+                def run_p2p(y=y, peer=peer):
+                    for i in range(steps):
+                        gemv()
+                        peer.all_gather(y.data_ptr(), i % 2, self.stream())
+
+                def run_fused(x=x, fused=fused):
+                    for i in range(steps):
+                        fused(x.data_ptr(), w.data_ptr(), i % 2, self.stream())
+
+                row = {}
+                # the fused epilogue is the decode path (GEMV, <= 16 tokens a
+                # launch); larger M runs the tcgen05 GEMM and a separate gather
+                arms = [("gemv", run_gemv, 1), ("nccl", run_nccl, 1), ("p2p", run_p2p, 2)]
+                if m <= 16:
+                    arms.append(("fused", run_fused, 1))
+                for name, body, kernels in arms:
+                    self.barrier()
+                    g = self.graph(body)
+                    self.barrier()
+                    ms = self.max_over_ranks(self.time_graph(g, reps, steps * kernels)) / steps
+                    del g
+                    row[f"{name}_us"] = round(ms * 1e3, 2)
+                    row[f"{name}_gbs"] = round(linear_bytes(m, n, k) / ms / 1e6, 1)
+                result[f"m{m}"] = row
+                self.barrier()
+                peer.close(barrier=self.barrier)
+                if fused is not None:
+                    fused.close(barrier=self.barrier)
+        finally:
+            torch.cuda.synchronize()
+            nccl.close()
+        return result
+
     # -- main -------------------------------------------------------------------
     def run(self) -> dict | None:
         torch = self.torch
@@ -533,6 +617,8 @@ class Bench:
             extra["config4_decoder_layer_m1"] = self.config4()
             extra["config5"] = self.config5()
         e2e = self.e2e(max(3, min(args.steps, 20)))
+        if self.world > 1:
+            extra["lm_head_sharded"] = self.lm_head_sharded()
         if self.rank == 0:
             cpu = cpu_baseline(budget_s=args.cpu_seconds)
             c2 = extra["config2_rmsnorm_rope_t512"]
@@ -748,7 +834,17 @@ def main() -> int:
 
     if not _b.LIB_PATH.exists():
         raise SystemExit("libmote_cuda.so missing: run python -m mote_b200.build")
-    result = Bench(args).run()
+    # Libraries (NCCL's version banner, for one) may write to file
+    # descriptor 1; keep it for the one JSON line and send the rest to stderr.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        result = Bench(args).run()
+    finally:
+        sys.stdout.flush()
+        os.dup2(json_fd, 1)
+        os.close(json_fd)
     if result is not None:
         print(json.dumps(result), flush=True)
     return 0

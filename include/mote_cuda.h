@@ -193,6 +193,58 @@ int mote_cuda_rope_cos_sin_f32(const void* positions, void* cos_out, void* sin_o
                                uint64_t tokens, uint64_t rotary_dim, double theta,
                                void* stream);
 
+/* ---- multi-GPU exchange for column-sharded linears ----------------------
+ * The reference is single-device (crates/mote-backend-hip/src/context.rs:13-80
+ * holds one device and one stream); these entry points are new.  Each rank
+ * computes y_g = x @ W_g^T for its contiguous slice W_g of the weight rows;
+ * the all-gathers below deliver every slice to every rank, rank-major
+ * ([nranks][count] f16).
+ *
+ * NCCL transport (libnccl.so.2 is loaded on first use; status 10000 if it is
+ * absent, 10100 + ncclResult_t on an NCCL failure).  id is 128 bytes. */
+int mote_cuda_comm_unique_id(void* id_out);
+int mote_cuda_comm_init(void** comm, int nranks, const void* id, int rank);
+int mote_cuda_comm_all_gather_f16(void* comm, const void* send, void* recv, uint64_t count,
+                                  void* stream);
+int mote_cuda_comm_destroy(void* comm);
+
+/* Peer-store transport over NVLink.  Buffers are shared with CUDA IPC
+ * handles (64 bytes): every rank exports its receive buffer and its flag
+ * array (nranks + 2 uint32 words, zeroed once before first use) and opens
+ * the others'.  recv_ptrs and flag_ptrs are DEVICE arrays of nranks
+ * pointers (this rank's own buffers at index rank).  One launch stores this
+ * rank's slice into every receive buffer at offset rank * count, advances
+ * this rank's epoch (kept in its flag array, so graph replays work),
+ * publishes it in every flag array and waits (bounded; on timeout bit 1 of
+ * the device status is set) until every rank has published it.  A receive
+ * buffer must not be overwritten while a rank still reads the previous
+ * gather from it.  count is a multiple of 8, send 16-byte aligned. */
+int mote_cuda_ipc_get_handle(const void* dev_ptr, void* handle_out);
+int mote_cuda_ipc_open_handle(const void* handle, void** dev_ptr);
+int mote_cuda_ipc_close_handle(void* dev_ptr);
+int mote_cuda_all_gather_p2p_f16(const void* send, void* const* recv_ptrs,
+                                 unsigned* const* flag_ptrs, unsigned* own_flags,
+                                 uint64_t count, uint32_t rank, uint32_t nranks, void* stream);
+
+/* Column-sharded Q4_0 linear with the all-gather fused into the epilogue:
+ * `weights` holds this rank's rows [rank*shard, rank*shard + shard) of the
+ * full [total_features, K] matrix (rows past total_features are padding and
+ * never stored); the f16 results go straight into every rank's full output
+ * buffer [rows, total_features] at columns rank*shard.. (outputs: DEVICE
+ * array of nranks pointers, peers mapped over CUDA IPC), then the flag
+ * handshake of mote_cuda_all_gather_p2p_f16 runs at the end of the grid, so
+ * when the launch completes every rank holds all columns.  shard % 16 == 0,
+ * total_features % 8 == 0, K % 256 == 0 and K > 0, 16-byte aligned input,
+ * weights and output buffers; every rank
+ * passes the same rows (rows == 0 returns 0 without a launch on all ranks).
+ * Null pointers, rank >= nranks or other shapes -> 1. */
+int mote_cuda_quantized_linear_q4_0_f16_allgather(const void* input, const void* weights,
+                                                  void* const* outputs, unsigned* const* flag_ptrs,
+                                                  unsigned* own_flags, uint64_t rows,
+                                                  uint64_t shard_features, uint64_t input_features,
+                                                  uint64_t total_features, uint32_t rank,
+                                                  uint32_t nranks, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,17 @@ SIGNATURES: dict[str, tuple] = {
     "mote_cuda_swiglu_f16": (I, [P, P, P, U64, P]),
     "mote_cuda_embedding_gather_f16": (I, [P, P, P, U64, U64, U64, P, P]),
     "mote_cuda_rope_cos_sin_f32": (I, [P, P, P, U64, U64, D, P]),
+    # multi-GPU exchange
+    "mote_cuda_comm_unique_id": (I, [P]),
+    "mote_cuda_comm_init": (I, [ctypes.POINTER(P), I, P, I]),
+    "mote_cuda_comm_all_gather_f16": (I, [P, P, P, U64, P]),
+    "mote_cuda_comm_destroy": (I, [P]),
+    "mote_cuda_ipc_get_handle": (I, [P, P]),
+    "mote_cuda_ipc_open_handle": (I, [P, ctypes.POINTER(P)]),
+    "mote_cuda_ipc_close_handle": (I, [P]),
+    "mote_cuda_all_gather_p2p_f16": (I, [P, P, P, P, U64, U32, U32, P]),
+    "mote_cuda_quantized_linear_q4_0_f16_allgather": (I, [P, P, P, P, P, U64, U64, U64, U64, U32,
+                                                          U32, P]),
 }
 
 

@@ -6,3 +6,4 @@
 #include "q4_0_linear.cu"
 #include "layer_ops.cu"
 #include "q4_0_codec.cu"
+#include "comm.cu"

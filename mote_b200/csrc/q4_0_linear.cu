@@ -69,7 +69,11 @@ constexpr int kSmemPerSm = 233472;                          // 228 KB per SM
 constexpr int kSmemReservedPerCta = 1024;                   // system use per resident CTA
 constexpr int kMaxXRows = 16;                               // two n8 tiles
 
-enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1, kEpiResidual = 2 };
+// kEpiPeers: the plain f16 result of this rank's row shard is stored into
+// every rank's full output buffer (over NVLink for the peers) and the grid
+// ends with a flag handshake, so every rank holds all shards when the
+// kernel completes.
+enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1, kEpiResidual = 2, kEpiPeers = 3 };
 
 struct Params {
     const void* x;            // [M, K] f16 or f32, row stride K
@@ -89,12 +93,25 @@ struct Params {
     std::uint32_t x_bytes;    // (x_zero_row + 1) * x_stride rounded up to 128
     std::uint32_t x_zero_row; // index of the all-zero row after the staged rows
     std::uint32_t split_shift; // log2 of the warps sharing a tile's K (0..3)
+    // kEpiPeers: output buffers [M, ldy] of every rank (device array), this
+    // rank's first column, and the flag arrays of the handshake.
+    __half* const* peer_y;
+    unsigned* const* peer_flags;
+    unsigned* own_flags;
+    std::uint64_t col0;
+    std::uint32_t rank;
+    std::uint32_t nranks;
 };
 
 __host__ __device__ constexpr int red_bytes(int nt) { return 2 * kWarps * nt * 4 * 32 * 4; }
 
-__host__ __device__ constexpr int smem_bytes(int x_bytes, int nt, int stages) {
-    return x_bytes + kWarps * stages * kStageBytes + red_bytes(nt);
+// kEpiPeers also stages each stored tile (16 rows x up to 16 tokens of
+// f16) per warp, to send it to the peers in 16-byte vectors.
+constexpr int kPeerStageBytes = 16 * 16 * 2;
+
+__host__ __device__ constexpr int smem_bytes(int x_bytes, int nt, int stages, bool peers = false) {
+    return x_bytes + kWarps * stages * kStageBytes + red_bytes(nt) +
+           (peers ? kWarps * kPeerStageBytes : 0);
 }
 
 // Quant word u = bytes B0..B3 = qs[4t .. 4t+3] of a block.  Its low
@@ -149,7 +166,7 @@ __device__ __forceinline__ const std::uint8_t* tile_row(const Params& p, std::ui
 
 template <int NT, bool XF32, bool OF32, int EPI>
 __device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, int g, int t,
-                                           const float (&acc)[NT][4]) {
+                                           const float (&acc)[NT][4], __half* stage = nullptr) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         if constexpr (EPI == kEpiSwiGLU) {
@@ -187,6 +204,10 @@ __device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, 
                         if (m >= p.M) continue;
                         float v = acc[nt][2 * half + c];
                         if constexpr (EPI == kEpiResidual) v += __half2float(p.res[m * p.ldy + r]);
+                        if constexpr (EPI == kEpiPeers) {
+                            stage[m * 16 + g + 8 * half] = __float2half_rn(v);
+                            continue;
+                        }
                         if constexpr (OF32)
                             static_cast<float*>(p.y)[m * p.ldy + r] = v;
                         else
@@ -204,6 +225,28 @@ __device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, 
             }
         }
     }
+    if constexpr (EPI == kEpiPeers) {
+        // Staged tile [token][16 rows] -> two 16-byte vectors per token, to
+        // every rank's buffer (columns col0 + 16 * tile ..); a ragged last
+        // tile falls back to 2-byte stores of its real rows.
+        __syncwarp();
+        const int lane = 4 * g + t;
+        const std::uint32_t m = static_cast<std::uint32_t>(lane) >> 1;
+        const std::uint32_t r0 = tile * 16u + 8u * (lane & 1);
+        if (m < p.M && r0 < p.N) {
+            const std::uint64_t at = m * p.ldy + p.col0 + r0;
+            const __half* src = stage + m * 16 + 8 * (lane & 1);
+            if (r0 + 8 <= p.N) {
+                const uint4 v = *reinterpret_cast<const uint4*>(src);
+                for (std::uint32_t q = 0; q < p.nranks; ++q)
+                    *reinterpret_cast<uint4*>(p.peer_y[q] + at) = v;
+            } else {
+                for (std::uint32_t q = 0; q < p.nranks; ++q)
+                    for (std::uint32_t i = 0; r0 + i < p.N; ++i) p.peer_y[q][at + i] = src[i];
+            }
+        }
+        __syncwarp();
+    }
 }
 
 // Compile-time loop: f(std::integral_constant<int, I>) for I in [B, E).
@@ -212,6 +255,41 @@ __device__ __forceinline__ void static_for(F&& f) {
     if constexpr (B < E) {
         f(std::integral_constant<int, B>{});
         static_for<B + 1, E>(f);
+    }
+}
+
+// End of a kEpiPeers grid: the CTA's stores are published with one
+// cumulative system-scope fence after a CTA barrier; the last CTA to arrive
+// advances this rank's epoch (kept in its flag array, so graph replays
+// work), publishes it to every rank and waits -- bounded -- until every rank
+// has published it.  Flag array: [q] epoch of rank q, [n] arrival counter,
+// [n + 1] own epoch.
+__device__ __forceinline__ void peer_handshake(const Params& p) {
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const unsigned arrived = atomicAdd(&p.own_flags[p.nranks], 1u);
+    if (arrived != gridDim.x - 1) return;
+    p.own_flags[p.nranks] = 0u;
+    const unsigned epoch = p.own_flags[p.nranks + 1] + 1u;
+    p.own_flags[p.nranks + 1] = epoch;
+    __threadfence_system();
+    for (std::uint32_t q = 0; q < p.nranks; ++q)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q] + p.rank),
+                     "r"(epoch)
+                     : "memory");
+    const long long start = clock64();
+    for (std::uint32_t q = 0; q < p.nranks; ++q) {
+        for (;;) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.own_flags + q)
+                         : "memory");
+            if (static_cast<int>(v - epoch) >= 0) break;
+            if (clock64() - start > kWaitCycles) {
+                atomicOr(&g_device_status, kDevWaitTimeout);
+                return;
+            }
+        }
     }
 }
 
@@ -230,6 +308,8 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
     std::uint8_t* xs = smem;
     std::uint8_t* ring = smem + p.x_bytes + warp * STAGES * kStageBytes;
     float* red = reinterpret_cast<float*>(smem + p.x_bytes + kWarps * STAGES * kStageBytes);
+    __half* stage = reinterpret_cast<__half*>(smem + p.x_bytes + kWarps * STAGES * kStageBytes +
+                                              red_bytes(NT) + warp * kPeerStageBytes);
 
     // Split-K: the CTA's warps form kWarps / split groups of `split` warps;
     // a group walks its own tiles (first, first + stride, ...; groups are
@@ -468,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
         }
         const std::uint32_t tile = first + tl * stride;
         if (split == 1) {  // the warp covered all of K
-            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, acc);
+            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, acc, stage);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
             continue;
@@ -499,9 +579,10 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
                         sum[nt][i] += base[w * (NT * 4 * 32) + (nt * 4 + i) * 32 + lane];
-            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, sum);
+            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, sum, stage);
         }
     }
+    if constexpr (EPI == kEpiPeers) peer_handshake(p);
 }
 
 // ---------------------------------------------------------------------------
@@ -614,12 +695,13 @@ int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
     const int st = ensure_smem_attribute(kernel, kMaxSmem, configured);
     if (st != kSuccess) return st;
     const std::uint32_t groups = kWarps >> p.split_shift;
-    const std::uint32_t grid = min((p.tiles + groups - 1) / groups,
-                                   static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
+    std::uint32_t grid = min((p.tiles + groups - 1) / groups,
+                             static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
+    if (EPI == kEpiPeers && grid == 0) grid = 1;  // every rank joins the handshake
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes(static_cast<int>(p.x_bytes), NT, STAGES);
+    cfg.dynamicSmemBytes = smem_bytes(static_cast<int>(p.x_bytes), NT, STAGES, EPI == kEpiPeers);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -652,7 +734,7 @@ int launch_gemv_config(const Params& p, int stages, int ctas, cudaStream_t strea
 // Picks tokens per launch, n8 tiles and ring depth so the staged
 // activations fit next to the ring.  Returns false if not even one token
 // fits (then the generic kernel runs).
-inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, std::uint32_t& tokens,
+inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, bool peers, std::uint32_t& tokens,
                       int& nt, int& stages, int& ctas_per_sm, std::uint32_t& x_rows,
                       std::uint32_t& x_stride, std::uint32_t& x_bytes) {
     const std::uint32_t rows_per_token = xf32 ? 2 : 1;
@@ -668,7 +750,7 @@ inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, std::uint32_t
         x_bytes = ((x_rows + 1) * x_stride + 127u) & ~127u;  // + the zero row
         nt = x_rows <= 8 ? 1 : 2;
         for (const auto& opt : kOptions) {
-            const int bytes = smem_bytes(static_cast<int>(x_bytes), nt, opt[1]);
+            const int bytes = smem_bytes(static_cast<int>(x_bytes), nt, opt[1], peers);
             if (bytes <= kMaxSmem && opt[0] * (bytes + kSmemReservedPerCta) <= kSmemPerSm) {
                 ctas_per_sm = opt[0];
                 stages = opt[1];
@@ -696,11 +778,24 @@ inline std::uint32_t choose_split_shift(std::uint32_t tiles, std::uint32_t units
 
 // Runs the linear for M rows of x, in as few persistent launches as the
 // activation staging allows (consecutive launches on the same stream).
+// kEpiPeers destinations and handshake flags (see peer_handshake).
+struct PeerArgs {
+    __half* const* outputs;
+    unsigned* const* flags;
+    unsigned* own_flags;
+    std::uint64_t col0;
+    std::uint32_t rank;
+    std::uint32_t nranks;
+};
+
 template <bool XF32, bool OF32, int EPI>
 int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint64_t M,
                std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream,
-               const void* res = nullptr) {
+               const void* res = nullptr, const PeerArgs* peers = nullptr) {
     const std::size_t osz = OF32 ? 4 : 2;
+    if constexpr (EPI == kEpiPeers) {
+        if (peers == nullptr || K == 0) return kInvalidValue;
+    }
     if (K == 0) {
         // Every dot product is empty: the reference writes zeros
         // (crates/mote-backend-hip/tests/quantized_linear.rs:142-158).  For
@@ -729,6 +824,14 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     p.pitch = (K / 32) * 18;
     p.units = static_cast<std::uint32_t>(K / 256);
     p.ldy = ldy;
+    if (peers != nullptr) {
+        p.peer_y = peers->outputs;
+        p.peer_flags = peers->flags;
+        p.own_flags = peers->own_flags;
+        p.col0 = peers->col0;
+        p.rank = peers->rank;
+        p.nranks = peers->nranks;
+    }
     const std::uint64_t rows_per_tile = EPI == kEpiSwiGLU ? 8 : 16;
     p.tiles = static_cast<std::uint32_t>((N + rows_per_tile - 1) / rows_per_tile);
     const std::size_t xes = XF32 ? 4 : 2;
@@ -738,7 +841,9 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     std::uint32_t tokens = 0;
     int nt = 1, stages = 2, ctas = 1;
     if (fast)
-        fast = plan_gemv(M, K, XF32, tokens, nt, stages, ctas, p.x_rows, p.x_stride, p.x_bytes);
+        fast = plan_gemv(M, K, XF32, EPI == kEpiPeers, tokens, nt, stages, ctas, p.x_rows,
+                         p.x_stride, p.x_bytes);
+    if (EPI == kEpiPeers && !fast) return kInvalidValue;
     if (fast)
         p.split_shift =
             choose_split_shift(p.tiles, p.units, static_cast<std::uint32_t>(sm_count() * ctas));
@@ -754,11 +859,13 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
             p.x_rows = static_cast<std::uint32_t>(mc) * (XF32 ? 2 : 1);
             p.x_zero_row = p.x_rows;
             st = launch_gemv_config<XF32, OF32, EPI>(p, stages, ctas, stream);
-        } else {
+        } else if constexpr (EPI != kEpiPeers) {
             const dim3 grid(static_cast<unsigned>((N + 3) / 4),
                             static_cast<unsigned>((mc + kGenericTokens - 1) / kGenericTokens));
             q4_0_linear_generic_kernel<XF32, OF32, EPI><<<grid, 128, 0, stream>>>(p);
             st = static_cast<int>(cudaGetLastError());
+        } else {
+            st = kInvalidValue;
         }
         if (st != 0) return st;
     }
@@ -863,4 +970,39 @@ extern "C" int mote_cuda_quantized_linear_q4_0_f16_residual(const void* input, c
                                                   output_features, input_features,
                                                   output_features,
                                                   static_cast<cudaStream_t>(stream), residual);
+}
+
+// Column-sharded linear with the all-gather fused into the epilogue: this
+// rank's rows [rank * shard, rank * shard + shard) of the full weight matrix
+// (`weights` holds only those rows) produce output columns that are stored
+// directly into every rank's full output buffer [rows, total_features]
+// (outputs: device array of nranks pointers, peers mapped over CUDA IPC),
+// followed by the flag handshake of the peer all-gather.  No reference
+// counterpart.  Fast-path shapes only (K % 256 == 0, K > 0, 16-byte aligned
+// input and weights, total_features % 8 == 0); every rank must pass the
+// same rows.
+extern "C" int mote_cuda_quantized_linear_q4_0_f16_allgather(
+    const void* input, const void* weights, void* const* outputs, unsigned* const* flag_ptrs,
+    unsigned* own_flags, std::uint64_t rows, std::uint64_t shard_features,
+    std::uint64_t input_features, std::uint64_t total_features, std::uint32_t rank,
+    std::uint32_t nranks, void* stream) {
+    using namespace mote::q4;
+    if (outputs == nullptr || flag_ptrs == nullptr || own_flags == nullptr || nranks == 0 ||
+        rank >= nranks || shard_features % 16 != 0 || total_features % 8 != 0)
+        return mote::kInvalidValue;
+    const int c = check_linear_args(input, weights, outputs, rows, total_features,
+                                    input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    if (input_features == 0 || input_features % 256 != 0) return mote::kInvalidValue;
+    const std::uint64_t col0 = static_cast<std::uint64_t>(rank) * shard_features;
+    const std::uint64_t real = col0 >= total_features
+                                   ? 0
+                                   : (total_features - col0 < shard_features ? total_features - col0
+                                                                             : shard_features);
+    PeerArgs peers{reinterpret_cast<__half* const*>(outputs), flag_ptrs, own_flags, col0, rank,
+                   nranks};
+    return run_linear<false, false, kEpiPeers>(input, weights, nullptr, nullptr, rows, real,
+                                               input_features, total_features,
+                                               static_cast<cudaStream_t>(stream), nullptr, &peers);
 }

@@ -134,3 +134,38 @@ def test_new_op_argument_rules(lib):
 def test_status_strings(lib):
     assert b"invalid" in lib.mote_cuda_status_string(-1).lower()
     assert lib.mote_cuda_status_string(1)
+
+
+def test_comm_argument_rules(lib):
+    f = lib.mote_cuda_all_gather_p2p_f16
+    assert f(FAKE, FAKE, FAKE, FAKE, 12, 0, 1, STREAM) == 1  # count not a multiple of 8
+    assert f(FAKE, FAKE, FAKE, FAKE, 16, 1, 1, STREAM) == 1  # rank >= nranks
+    assert f(FAKE + 8, FAKE, FAKE, FAKE, 16, 0, 1, STREAM) == 1  # send not 16-byte aligned
+    assert f(FAKE, None, FAKE, FAKE, 16, 0, 1, STREAM) == 1
+    assert f(FAKE, FAKE, FAKE, FAKE, 16, 0, 1, None) == 1
+    assert lib.mote_cuda_comm_all_gather_f16(None, FAKE, FAKE, 8, STREAM) == 1
+    assert lib.mote_cuda_comm_destroy(None) == 0
+    comm = ctypes.c_void_p()
+    uid = ctypes.create_string_buffer(128)
+    assert lib.mote_cuda_comm_init(ctypes.byref(comm), 2, uid, 2) == 1
+    assert lib.mote_cuda_comm_init(ctypes.byref(comm), 0, uid, 0) == 1
+    assert lib.mote_cuda_ipc_get_handle(None, uid) == 1
+    assert lib.mote_cuda_ipc_close_handle(None) == 1
+
+
+def test_residual_argument_rules(lib):
+    fn = lib.mote_cuda_quantized_linear_q4_0_f16_residual
+    assert fn(FAKE, FAKE, None, FAKE, 1, 8, 32, STREAM) == 1
+    assert fn(FAKE, FAKE, FAKE, FAKE, 1, 8, 33, STREAM) == 1
+    assert fn(FAKE, FAKE, FAKE, FAKE, 0, 8, 32, STREAM) == 0
+
+
+def test_fused_allgather_argument_rules(lib):
+    fn = lib.mote_cuda_quantized_linear_q4_0_f16_allgather
+    ok = (FAKE, FAKE, FAKE, FAKE, FAKE)
+    assert fn(*ok, 1, 16, 256, 32, 2, 2, STREAM) == 1      # rank >= nranks
+    assert fn(*ok, 1, 12, 256, 32, 0, 2, STREAM) == 1      # shard not a multiple of 16
+    assert fn(*ok, 1, 16, 96, 32, 0, 2, STREAM) == 1       # K not a multiple of 256
+    assert fn(*ok, 1, 16, 33, 32, 0, 2, STREAM) == 1       # K not a multiple of 32
+    assert fn(FAKE, FAKE, None, FAKE, FAKE, 1, 16, 256, 32, 0, 2, STREAM) == 1
+    assert fn(*ok, 0, 16, 256, 32, 0, 2, STREAM) == 0      # no rows: no launch

@@ -19,6 +19,15 @@
  *     cudaMalloc'd memory), streams are opaque cudaStream_t handles and every
  *     kernel runs asynchronously on the stream it is given.
  *
+ * Stream overlap: kernels are launched with programmatic dependent launch,
+ * so a kernel may begin while earlier kernels of this library on the stream
+ * are still running; each waits for its predecessor to complete before it
+ * touches activations or outputs.  The Q4_0 linears start streaming their
+ * WEIGHTS before that wait, so a linear's weights must not be written by
+ * this library's kernels still in flight on its stream (weights written by
+ * a copy, by mote_cuda_q4_0_encode_f32 or by any kernel not from this
+ * library are ordered normally: those end the overlap).
+ *
  * Data formats: f16 is IEEE binary16 (uint16 bits), Q4_0 is the ggml block
  * layout (per 32 elements: little-endian f16 scale d, then 16 bytes where
  * byte j holds element j in its low nibble and element j+16 in its high

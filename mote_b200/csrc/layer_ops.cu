@@ -56,6 +56,8 @@ template <int VPT>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_vec_kernel(
     const __half* input, const __half* __restrict__ weight, __half* output,
     std::uint64_t hidden, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
     const std::uint64_t row = blockIdx.x;
     const uint4* in = reinterpret_cast<const uint4*>(input + row * hidden);
@@ -97,6 +99,8 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_vec_kernel(
 __global__ void __launch_bounds__(kNormThreads) rms_norm_scalar_kernel(
     const __half* input, const __half* __restrict__ weight, __half* output,
     std::uint64_t hidden, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
     const std::uint64_t row = blockIdx.x;
     const __half* in = input + row * hidden;
@@ -120,6 +124,8 @@ template <int VPT>
 __global__ void __launch_bounds__(kNormThreads) fused_add_rms_norm_vec_kernel(
     const __half* input, __half* residual, const __half* __restrict__ weight, __half* output,
     std::uint64_t hidden, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
     const std::uint64_t row = blockIdx.x;
     const uint4* in = reinterpret_cast<const uint4*>(input + row * hidden);
@@ -164,6 +170,8 @@ __global__ void __launch_bounds__(kNormThreads) fused_add_rms_norm_vec_kernel(
 __global__ void __launch_bounds__(kNormThreads) fused_add_rms_norm_scalar_kernel(
     const __half* input, __half* residual, const __half* __restrict__ weight, __half* output,
     std::uint64_t hidden, float eps) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
     const std::uint64_t row = blockIdx.x;
     const __half* in = input + row * hidden;
@@ -200,6 +208,8 @@ __global__ void __launch_bounds__(256) rope_kernel(const __half* input,
                                                    std::uint64_t vectors, std::uint64_t heads,
                                                    std::uint64_t head_dim,
                                                    std::uint64_t rotary_dim, int layout) {
+    pdl_launch_dependents();
+    pdl_wait();
     const std::uint64_t half = rotary_dim / 2;
     const std::uint64_t per_vec = half + (head_dim - rotary_dim);
     const std::uint64_t total = vectors * per_vec;
@@ -238,11 +248,13 @@ constexpr int kRopeVecPerThread = 2;   // (q_heads + kv_heads) * HD / 8 <= 512
 constexpr int kNormVecPerThread = 4;   // hidden <= 8192
 
 template <int HD>
-__global__ void __launch_bounds__(kNormThreads) rms_norm_rope_kernel(
+__global__ void __launch_bounds__(kNormThreads, 4) rms_norm_rope_kernel(
     const __half* x, const __half* __restrict__ gamma, __half* x_out, const __half* q,
     __half* q_out, const __half* k, __half* k_out, const float* __restrict__ cos,
     const float* __restrict__ sin, std::uint64_t hidden, std::uint32_t q_heads,
     std::uint32_t kv_heads, float eps, int layout) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
     constexpr int kLanesPerHead = HD / 8;
     constexpr int kHalfLanes = kLanesPerHead / 2;
@@ -356,6 +368,8 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 __global__ void __launch_bounds__(256) swiglu_vec_kernel(const __half* gate, const __half* up,
                                                         __half* out, std::uint64_t nvec) {
+    pdl_launch_dependents();
+    pdl_wait();
     for (std::uint64_t v = blockIdx.x * static_cast<std::uint64_t>(blockDim.x) + threadIdx.x;
          v < nvec; v += static_cast<std::uint64_t>(gridDim.x) * blockDim.x) {
         H8 g, u, o;
@@ -370,6 +384,8 @@ __global__ void __launch_bounds__(256) swiglu_vec_kernel(const __half* gate, con
 
 __global__ void __launch_bounds__(256) swiglu_scalar_kernel(const __half* gate, const __half* up,
                                                            __half* out, std::uint64_t n) {
+    pdl_launch_dependents();
+    pdl_wait();
     for (std::uint64_t i = blockIdx.x * static_cast<std::uint64_t>(blockDim.x) + threadIdx.x;
          i < n; i += static_cast<std::uint64_t>(gridDim.x) * blockDim.x)
         out[i] = __float2half_rn(silu_mul(__half2float(gate[i]), __half2float(up[i])));
@@ -382,6 +398,8 @@ template <bool VEC>
 __global__ void __launch_bounds__(256) embedding_gather_kernel(
     const __half* __restrict__ table, const std::int32_t* __restrict__ ids, __half* out,
     std::uint64_t vocab, std::uint64_t hidden, unsigned* flag) {
+    pdl_launch_dependents();
+    pdl_wait();
     const std::uint64_t token = blockIdx.x;
     const std::int32_t id = ids[token];
     const bool ok = id >= 0 && static_cast<std::uint64_t>(id) < vocab;
@@ -429,15 +447,14 @@ extern "C" int mote_cuda_rms_norm_f16(const void* input, const void* weight, voi
     const dim3 grid(static_cast<unsigned>(rows));
     const bool vec = hidden_size % 8 == 0 && aligned16(input) && aligned16(weight) &&
                      aligned16(output);
+    const dim3 block(kNormThreads);
     if (vec && hidden_size <= 256 * 8)
-        rms_norm_vec_kernel<1><<<grid, kNormThreads, 0, s>>>(in, w, out, hidden_size, epsilon);
-    else if (vec && hidden_size <= 256 * 8 * 2)
-        rms_norm_vec_kernel<2><<<grid, kNormThreads, 0, s>>>(in, w, out, hidden_size, epsilon);
-    else if (vec && hidden_size <= 256 * 8 * 4)
-        rms_norm_vec_kernel<4><<<grid, kNormThreads, 0, s>>>(in, w, out, hidden_size, epsilon);
-    else
-        rms_norm_scalar_kernel<<<grid, kNormThreads, 0, s>>>(in, w, out, hidden_size, epsilon);
-    return static_cast<int>(cudaGetLastError());
+        return launch_pdl(rms_norm_vec_kernel<1>, grid, block, s, in, w, out, hidden_size, epsilon);
+    if (vec && hidden_size <= 256 * 8 * 2)
+        return launch_pdl(rms_norm_vec_kernel<2>, grid, block, s, in, w, out, hidden_size, epsilon);
+    if (vec && hidden_size <= 256 * 8 * 4)
+        return launch_pdl(rms_norm_vec_kernel<4>, grid, block, s, in, w, out, hidden_size, epsilon);
+    return launch_pdl(rms_norm_scalar_kernel, grid, block, s, in, w, out, hidden_size, epsilon);
 }
 
 // Argument checks mirror mote_hip_fused_add_rms_norm_f16
@@ -461,19 +478,18 @@ extern "C" int mote_cuda_fused_add_rms_norm_f16(const void* input, void* residua
     const dim3 grid(static_cast<unsigned>(rows));
     const bool vec = hidden_size % 8 == 0 && aligned16(input) && aligned16(residual) &&
                      aligned16(weight) && aligned16(output);
+    const dim3 block(kNormThreads);
     if (vec && hidden_size <= 256 * 8)
-        fused_add_rms_norm_vec_kernel<1>
-            <<<grid, kNormThreads, 0, s>>>(in, res, w, out, hidden_size, epsilon);
-    else if (vec && hidden_size <= 256 * 8 * 2)
-        fused_add_rms_norm_vec_kernel<2>
-            <<<grid, kNormThreads, 0, s>>>(in, res, w, out, hidden_size, epsilon);
-    else if (vec && hidden_size <= 256 * 8 * 4)
-        fused_add_rms_norm_vec_kernel<4>
-            <<<grid, kNormThreads, 0, s>>>(in, res, w, out, hidden_size, epsilon);
-    else
-        fused_add_rms_norm_scalar_kernel<<<grid, kNormThreads, 0, s>>>(in, res, w, out,
-                                                                      hidden_size, epsilon);
-    return static_cast<int>(cudaGetLastError());
+        return launch_pdl(fused_add_rms_norm_vec_kernel<1>, grid, block, s, in, res, w, out,
+                          hidden_size, epsilon);
+    if (vec && hidden_size <= 256 * 8 * 2)
+        return launch_pdl(fused_add_rms_norm_vec_kernel<2>, grid, block, s, in, res, w, out,
+                          hidden_size, epsilon);
+    if (vec && hidden_size <= 256 * 8 * 4)
+        return launch_pdl(fused_add_rms_norm_vec_kernel<4>, grid, block, s, in, res, w, out,
+                          hidden_size, epsilon);
+    return launch_pdl(fused_add_rms_norm_scalar_kernel, grid, block, s, in, res, w, out,
+                      hidden_size, epsilon);
 }
 
 // Argument checks mirror mote_hip_rope_f16
@@ -490,11 +506,11 @@ extern "C" int mote_cuda_rope_f16(const void* input, const void* cos, const void
     if (tokens > kMaxGridX / heads) return kInternalError;
     const std::uint64_t vectors = tokens * heads;
     const std::uint64_t per_vec = rotary_dim / 2 + (head_dim - rotary_dim);
-    rope_kernel<<<grid_for(vectors * per_vec, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(input), static_cast<const float*>(cos),
-        static_cast<const float*>(sin), static_cast<__half*>(output), vectors, heads, head_dim,
-        rotary_dim, static_cast<int>(layout));
-    return static_cast<int>(cudaGetLastError());
+    return launch_pdl(rope_kernel, dim3(grid_for(vectors * per_vec, 256)), dim3(256),
+                      static_cast<cudaStream_t>(stream), static_cast<const __half*>(input),
+                      static_cast<const float*>(cos), static_cast<const float*>(sin),
+                      static_cast<__half*>(output), vectors, heads, head_dim, rotary_dim,
+                      static_cast<int>(layout));
 }
 
 // Fused per-token layer kernel: RMSNorm of x and RoPE of q and k in one
@@ -536,17 +552,16 @@ extern "C" int mote_cuda_rms_norm_rope_f16(const void* x, const void* gamma, voi
     }
     const dim3 grid(static_cast<unsigned>(tokens));
     auto args = [&](auto kernel) {
-        kernel<<<grid, kNormThreads, 0, s>>>(
-            static_cast<const __half*>(x), static_cast<const __half*>(gamma),
-            static_cast<__half*>(x_out), static_cast<const __half*>(q),
-            static_cast<__half*>(q_out), static_cast<const __half*>(k),
-            static_cast<__half*>(k_out), static_cast<const float*>(cos),
-            static_cast<const float*>(sin), hidden, static_cast<std::uint32_t>(q_heads),
-            static_cast<std::uint32_t>(kv_heads), epsilon, static_cast<int>(layout));
+        return launch_pdl(kernel, grid, dim3(kNormThreads), s, static_cast<const __half*>(x),
+                          static_cast<const __half*>(gamma), static_cast<__half*>(x_out),
+                          static_cast<const __half*>(q), static_cast<__half*>(q_out),
+                          static_cast<const __half*>(k), static_cast<__half*>(k_out),
+                          static_cast<const float*>(cos), static_cast<const float*>(sin), hidden,
+                          static_cast<std::uint32_t>(q_heads),
+                          static_cast<std::uint32_t>(kv_heads), epsilon,
+                          static_cast<int>(layout));
     };
-    if (head_dim == 64) args(rms_norm_rope_kernel<64>);
-    else args(rms_norm_rope_kernel<128>);
-    return static_cast<int>(cudaGetLastError());
+    return head_dim == 64 ? args(rms_norm_rope_kernel<64>) : args(rms_norm_rope_kernel<128>);
 }
 
 extern "C" int mote_cuda_swiglu_f16(const void* gate, const void* up, void* output,
@@ -556,14 +571,12 @@ extern "C" int mote_cuda_swiglu_f16(const void* gate, const void* up, void* outp
     if (n == 0) return kSuccess;
     auto s = static_cast<cudaStream_t>(stream);
     if (n % 8 == 0 && aligned16(gate) && aligned16(up) && aligned16(output))
-        swiglu_vec_kernel<<<grid_for(n / 8, 256), 256, 0, s>>>(
-            static_cast<const __half*>(gate), static_cast<const __half*>(up),
-            static_cast<__half*>(output), n / 8);
-    else
-        swiglu_scalar_kernel<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const __half*>(gate),
-                                                             static_cast<const __half*>(up),
-                                                             static_cast<__half*>(output), n);
-    return static_cast<int>(cudaGetLastError());
+        return launch_pdl(swiglu_vec_kernel, dim3(grid_for(n / 8, 256)), dim3(256), s,
+                          static_cast<const __half*>(gate), static_cast<const __half*>(up),
+                          static_cast<__half*>(output), n / 8);
+    return launch_pdl(swiglu_scalar_kernel, dim3(grid_for(n, 256)), dim3(256), s,
+                      static_cast<const __half*>(gate), static_cast<const __half*>(up),
+                      static_cast<__half*>(output), n);
 }
 
 extern "C" int mote_cuda_embedding_gather_f16(const void* table, const void* ids, void* output,
@@ -579,13 +592,10 @@ extern "C" int mote_cuda_embedding_gather_f16(const void* table, const void* ids
     const dim3 grid(static_cast<unsigned>(tokens));
     const bool vec = hidden % 8 == 0 && aligned16(table) && aligned16(output);
     auto* flag = static_cast<unsigned*>(error_flag);
-    if (vec)
-        embedding_gather_kernel<true><<<grid, 256, 0, s>>>(
-            static_cast<const __half*>(table), static_cast<const std::int32_t*>(ids),
-            static_cast<__half*>(output), vocab, hidden, flag);
-    else
-        embedding_gather_kernel<false><<<grid, 256, 0, s>>>(
-            static_cast<const __half*>(table), static_cast<const std::int32_t*>(ids),
-            static_cast<__half*>(output), vocab, hidden, flag);
-    return static_cast<int>(cudaGetLastError());
+    auto args = [&](auto kernel) {
+        return launch_pdl(kernel, grid, dim3(256), s, static_cast<const __half*>(table),
+                          static_cast<const std::int32_t*>(ids), static_cast<__half*>(output),
+                          vocab, hidden, flag);
+    };
+    return vec ? args(embedding_gather_kernel<true>) : args(embedding_gather_kernel<false>);
 }

@@ -232,6 +232,28 @@ __device__ __forceinline__ float half_bits_to_float(std::uint32_t bits16) {
 // every component), so this definition is unique.
 __device__ unsigned g_device_status = 0;
 
+// Launches `kernel` with programmatic dependent launch allowed: it may be
+// scheduled while its predecessor in the stream drains.  Every such kernel
+// calls pdl_wait() before it reads or writes memory the predecessor may
+// touch (the wait returns once the predecessor grid has completed and its
+// writes are visible), and pdl_launch_dependents() to let its own successor
+// be scheduled early.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                      Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 }  // namespace mote
 
 #define MOTE_RETURN_IF_LAUNCH_FAILED() return static_cast<int>(cudaGetLastError())

@@ -374,9 +374,13 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
         iss_slot = iss_slot + 1 == STAGES ? 0 : iss_slot + 1;
         cp_async_commit();
     };
-    // Weights do not depend on the previous kernel in the stream: start
-    // streaming them, let the next kernel launch, and only then wait for the
-    // producer of the activations.
+    // Programmatic dependent launch: this grid may start while earlier
+    // kernels of this library are still running on the stream (each lets
+    // its successor start at once).  The weights are not written by them --
+    // the documented precondition -- so the ring starts streaming them
+    // immediately; activations, outputs and everything else are touched only
+    // after griddepcontrol.wait, which returns once the previous grid has
+    // completed.
     for (int s = 0; s + 1 < STAGES; ++s) issue();
     pdl_launch_dependents();
     pdl_wait();

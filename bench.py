@@ -643,8 +643,12 @@ class Bench:
                     "frac": round(achieved / peaks["hbm_gbs"], 4),
                     "frac_of_8tbs_spec": round(achieved / SPEC_HBM_GBS, 4),
                     "peak_source": peaks["source"],
-                    "traffic": traffic_per_launch(),
-                    "kernel": "q4_0_linear_mma_kernel (per-case averages below)"},
+                    "traffic": (round(traffic_ratio() * kern_bytes / len(cases))
+                                if traffic_ratio() else None),
+                    "traffic_note": "ncu DRAM bytes / algorithmic bytes of the GEMV (lm_head "
+                                    "capture, profiles/q4_0_gemv_lm_head_m1.txt) x the average "
+                                    "algorithmic bytes of one sweep launch",
+                    "kernel": "q4_0_gemv_kernel (average over the sweep cases below)"},
                 "norm_rope_us_per_layer": c2["us_per_layer"],
                 "norm_rope_roofline": {"bound": "hbm", "achieved": c2["gbs"],
                                        "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -662,14 +666,16 @@ class Bench:
         return result
 
 
-def traffic_per_launch():
-    """DRAM bytes per launch from the committed ncu summary, if present."""
-    path = ROOT / "profiles" / "q4_0_linear_traffic.json"
-    if path.exists():
-        try:
-            return json.loads(path.read_text()).get("traffic_bytes_per_launch")
-        except (ValueError, OSError):
-            return None
+def traffic_ratio():
+    """(DRAM read + write) / algorithmic bytes of the GEMV, from the committed
+    ncu summary (``traffic_ratio:`` line), or None."""
+    path = ROOT / "profiles" / "q4_0_gemv_lm_head_m1.txt"
+    try:
+        for line in path.read_text().splitlines():
+            if line.strip().startswith("traffic_ratio:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except (OSError, ValueError, IndexError):
+        return None
     return None
 
 

@@ -5,20 +5,24 @@
 //   the time (the reference computes it in f32 per output,
 //   crates/mote-reference/src/quantized.rs:89-144).
 //
-// One CTA computes a 128 (tokens) x 256 (features) tile:
-// * warp 8 (producer) streams activation tiles (64 k x 128 rows, TMA with
-//   128-byte swizzle) and raw Q4_0 row slices (256 rows x 144 bytes = 8
+// One CTA computes a tile of 128 features x 256 tokens.  The dequantized
+// weights are the MMA's A operand (M = 128 rows) and the activations its B
+// operand (N = 256), so every weight converted to f16 feeds 256 tokens:
+// * warp 8 (producer) streams activation tiles (64 k x 256 tokens, TMA with
+//   128-byte swizzle) and raw Q4_0 row slices (128 rows x 144 bytes = 8
 //   blocks per row, TMA 2-D tile of bytes) into shared memory;
 // * warps 0-7 (converters) dequantize each 64-k slice of the raw rows into
 //   f16 (q - 8) * d -- correctly rounded, exactly what a dense f16 weight
 //   would hold -- written straight into the 128-byte-swizzled K-major
-//   layout the tensor core reads;
+//   layout the tensor core reads (warps 0-3 the even block of every slice,
+//   warps 4-7 the odd one: no divergence);
 // * warp 9 allocates 256 TMEM columns and one thread issues
 //   tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) per 16-k step,
 //   accumulating in f32 in TMEM; tcgen05.commit releases the operand stages;
 // * after the last k-slice the converter warps read the accumulator with
-//   tcgen05.ld (warp w owns TMEM lanes 32*(w%4).. and half of the columns)
-//   and store the tile.
+//   tcgen05.ld (warp w owns TMEM lanes = features 32*(w%4).. and half of the
+//   token columns) and store it: for each token, a warp writes 32
+//   consecutive features.
 // Stages are tracked with mbarriers; every wait is bounded and an expired
 // wait aborts the whole CTA (which still frees its TMEM).  No TMA load uses
 // cluster multicast.
@@ -35,31 +39,39 @@
 namespace mote {
 namespace gemm {
 
-constexpr int kBM = 128;                 // tokens per tile = TMEM lanes
-constexpr int kBN = 256;                 // features per tile = TMEM columns
+constexpr int kFT = 128;                 // features per tile = A rows = TMEM lanes
 constexpr int kBK = 64;                  // k per operand stage (one 128-B f16 swizzle row)
 constexpr int kSuperK = 256;             // k per raw weight stage (8 blocks, 144 B per row)
 constexpr int kStages = 3;               // operand stages
 constexpr int kRawStages = 2;            // raw weight stages
-constexpr int kABytes = kBM * kBK * 2;   // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kWBytes = kFT * kBK * 2;   // 16 KB converted weights per stage (A)
 constexpr int kRawRowBytes = 144;
-constexpr int kRawBytes = kBN * kRawRowBytes;  // 36 KB
+constexpr int kRawBytes = kFT * kRawRowBytes;  // 18 KB
 constexpr int kConvWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 10 * 32;
-constexpr int kTmemCols = 256;
 
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kABytes;
-constexpr int kOffRaw = kOffB + kStages * kBBytes;
-constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
-// barriers: a_full[S], b_full[S], empty[S], raw_full[R], raw_empty[R], accum
-constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
-constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
-constexpr int kOffAbort = kOffTmemSlot + 4;
-constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + slack to align the base to 1024
+// Shared-memory layout for a token tile of TT (64, 128 or 256) tokens = the
+// MMA's N and the TMEM columns: activations TT x 64 k per stage (B).
+template <int TT>
+struct Layout {
+    static constexpr int kXBytes = TT * kBK * 2;
+    static constexpr int kOffX = 0;
+    static constexpr int kOffW = kOffX + kStages * kXBytes;
+    static constexpr int kOffRaw = kOffW + kStages * kWBytes;
+    static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
+    // barriers: x_full[S], w_full[S], empty[S], raw_full[R], raw_empty[R], accum
+    static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
+    static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+    static constexpr int kOffAbort = kOffTmemSlot + 4;
+    static constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + slack for 1024-B alignment
+    // Instruction descriptor, kind::f16: F32 accumulate, A = B = F16, both
+    // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+    static constexpr std::uint32_t kIdesc = (1u << 4) | (static_cast<std::uint32_t>(TT >> 3) << 17) |
+                                            (static_cast<std::uint32_t>(kFT >> 4) << 24);
+    static_assert(TT == 64 || TT == 128 || TT == 256, "token tile");
+};
 
 struct Params {
     void* y;
@@ -147,12 +159,6 @@ __device__ __forceinline__ std::uint64_t smem_desc_sw128(std::uint32_t addr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: F32 accumulate, A = B = F16, both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr std::uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) |
-                                 (static_cast<std::uint32_t>(kBN >> 3) << 17) |
-                                 (static_cast<std::uint32_t>(kBM >> 4) << 24);
-
 // Bounded wait that also gives up as soon as another role aborted.
 __device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t parity,
                                               volatile std::uint32_t* abort_flag) {
@@ -205,14 +211,15 @@ __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::ui
     }
 }
 
-// Converts the two Q4_0 blocks of 64-k slice SUB (0..3) of one 144-byte raw
-// row (16-byte aligned at `raw_row`) into the swizzled f16 row `dst_row`.
-// The slice spans bytes [36*SUB, 36*SUB + 36); three aligned 16-byte loads
-// cover it (rows are 144 = 9 x 16 bytes apart, so a warp's loads are
-// bank-conflict free) and byte permutes pick the blocks out.
-template <int SUB>
-__device__ __forceinline__ void convert_slice(std::uint32_t raw_row, std::uint32_t dst_row,
-                                              int swz) {
+// Converts one Q4_0 block (PAR = 0: the even, 1: the odd block) of 64-k
+// slice SUB (0..3) of a 144-byte raw row (16-byte aligned at `raw_row`) into
+// the swizzled f16 row `dst_row`.  The slice spans bytes [36*SUB, 36*SUB +
+// 36); three aligned 16-byte loads cover it (rows are 144 = 9 x 16 bytes
+// apart, so a warp's loads are bank-conflict free) and byte permutes pick
+// the block out.
+template <int SUB, int PAR>
+__device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::uint32_t dst_row,
+                                                   int swz) {
     constexpr int kStart = 36 * SUB;
     constexpr int kChunk0 = kStart / 16;
     constexpr int kW = (kStart % 16) / 4;  // first word of the slice within the 12 loaded
@@ -224,20 +231,28 @@ __device__ __forceinline__ void convert_slice(std::uint32_t raw_row, std::uint32
                      : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
                      : "r"(raw_row + chunk * 16));
     }
-    // even block: scale = low half of word kW, quants start 2 bytes later
-    std::uint32_t q0[4];
+    if constexpr (PAR == 0) {
+        // even block: scale = low half of word kW, quants start 2 bytes later
+        std::uint32_t q0[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) q0[i] = prmt(w[kW + i], w[kW + i + 1], 0x5432u);
-    convert_block(w[kW] & 0xFFFFu, q0, dst_row, 0, swz);
-    // odd block: scale = high half of word kW+4, quants are words kW+5..kW+8
-    std::uint32_t q1[4] = {w[kW + 5], w[kW + 6], w[kW + 7], w[kW + 8]};
-    convert_block(w[kW + 4] >> 16, q1, dst_row, 32, swz);
+        for (int i = 0; i < 4; ++i) q0[i] = prmt(w[kW + i], w[kW + i + 1], 0x5432u);
+        convert_block(w[kW] & 0xFFFFu, q0, dst_row, 0, swz);
+    } else {
+        // odd block: scale = high half of word kW+4, quants are words kW+5..kW+8
+        const std::uint32_t q1[4] = {w[kW + 5], w[kW + 6], w[kW + 7], w[kW + 8]};
+        convert_block(w[kW + 4] >> 16, q1, dst_row, 32, swz);
+    }
 }
 
-template <bool OF32>
+template <int TT, bool OF32>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
                              const __grid_constant__ CUtensorMap map_w, const Params p) {
+    using L = Layout<TT>;
+    constexpr int kOffX = L::kOffX, kOffW = L::kOffW, kOffRaw = L::kOffRaw, kOffBar = L::kOffBar;
+    constexpr int kOffTmemSlot = L::kOffTmemSlot, kOffAbort = L::kOffAbort;
+    constexpr int kXBytes = L::kXBytes;
+    constexpr int kTmemCols = TT;
     extern __shared__ std::uint8_t smem_raw[];
     // 1024-byte aligned base (SW128 atoms and TMA swizzle need it)
     const std::uint32_t raw_base = smem_u32(smem_raw);
@@ -245,8 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     std::uint8_t* smem = smem_raw + (base - raw_base);
 
     std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + kOffBar);
-    std::uint64_t* a_full = bars;
-    std::uint64_t* b_full = bars + kStages;
+    std::uint64_t* x_full = bars;
+    std::uint64_t* w_full = bars + kStages;
     std::uint64_t* empty = bars + 2 * kStages;
     std::uint64_t* raw_full = bars + 3 * kStages;
     std::uint64_t* raw_empty = raw_full + kRawStages;
@@ -256,14 +271,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const std::uint32_t n0 = blockIdx.x * kBN;
-    const std::uint32_t m0 = blockIdx.y * kBM;
+    const std::uint32_t n0 = blockIdx.x * kFT;   // first feature (weight row)
+    const std::uint32_t m0 = blockIdx.y * TT;    // first token
     const std::uint32_t num_kb = p.K / kBK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&a_full[s], 1);
-            mbar_init(&b_full[s], kConvWarps);
+            mbar_init(&x_full[s], 1);
+            mbar_init(&w_full[s], kConvWarps);
             mbar_init(&empty[s], 1);
         }
         for (int r = 0; r < kRawStages; ++r) {
@@ -298,9 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 static_cast<int>(sb * kRawRowBytes), static_cast<int>(n0),
                                 smem_u32(&raw_full[r]));
                 }
-                mbar_arrive_expect_tx(&a_full[s], kABytes);
-                tma_load_2d(base + kOffA + s * kABytes, &map_x, static_cast<int>(kb * kBK),
-                            static_cast<int>(m0), smem_u32(&a_full[s]));
+                mbar_arrive_expect_tx(&x_full[s], kXBytes);
+                tma_load_2d(base + kOffX + s * kXBytes, &map_x, static_cast<int>(kb * kBK),
+                            static_cast<int>(m0), smem_u32(&x_full[s]));
             }
         }
         __syncwarp();  // reconverge before the block-wide barrier below
@@ -309,16 +324,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (std::uint32_t kb = 0; kb < num_kb; ++kb) {
                 const int s = kb % kStages;
                 const std::uint32_t ph = (kb / kStages) & 1u;
-                if (!wait_or_abort(&a_full[s], ph, abort_flag)) break;
-                if (!wait_or_abort(&b_full[s], ph, abort_flag)) break;
+                if (!wait_or_abort(&x_full[s], ph, abort_flag)) break;
+                if (!wait_or_abort(&w_full[s], ph, abort_flag)) break;
                 tc_fence_after();
-                const std::uint32_t a_addr = base + kOffA + s * kABytes;
-                const std::uint32_t b_addr = base + kOffB + s * kBBytes;
+                const std::uint32_t w_addr = base + kOffW + s * kWBytes;
+                const std::uint32_t x_addr = base + kOffX + s * kXBytes;
 #pragma unroll
                 for (int k = 0; k < kBK / 16; ++k) {
                     // +32 bytes per 16-element step inside the 128-byte swizzle row
-                    umma_f16(tmem_d, smem_desc_sw128(a_addr + k * 32),
-                             smem_desc_sw128(b_addr + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    umma_f16(tmem_d, smem_desc_sw128(w_addr + k * 32),
+                             smem_desc_sw128(x_addr + k * 32), L::kIdesc, (kb | k) != 0 ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&empty[s]));
             }
@@ -326,9 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // converters: thread t owns weight row t of the tile
-        const int row = threadIdx.x;  // 0..255
+        // converters: warp w converts the even (w < 4) or odd (w >= 4) block
+        // of every 64-k slice of weight row 32*(w%4) + lane
+        const int row = 32 * (warp % 4) + lane;  // 0..127
         const int swz = row & 7;
+        const bool odd = warp >= 4;
         const std::uint32_t nsb = num_kb / (kSuperK / kBK);
         bool ok = true;
         for (std::uint32_t sb = 0; sb < nsb && ok; ++sb) {
@@ -344,13 +361,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = __all_sync(0xffffffffu, wait_or_abort(&empty[s], ((kb / kStages) - 1) & 1u,
                                                                abort_flag));
                 if (!ok) return;  // warp-uniform
-                convert_slice<SUB>(raw_row, base + kOffB + s * kBBytes + row * 128, swz);
+                const std::uint32_t dst = base + kOffW + s * kWBytes + row * 128;
+                if (odd)  // warp-uniform
+                    convert_half_slice<SUB, 1>(raw_row, dst, swz);
+                else
+                    convert_half_slice<SUB, 0>(raw_row, dst, swz);
                 // make the generic-proxy writes visible to the tensor core
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                                     smem_u32(&b_full[s]))
+                                     smem_u32(&w_full[s]))
                                  : "memory");
                     if (SUB == (kSuperK / kBK) - 1)
                         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
@@ -363,50 +384,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             slice(std::integral_constant<int, 2>{});
             slice(std::integral_constant<int, 3>{});
         }
-        // epilogue: warp w reads TMEM lanes 32*(w%4).. and columns 128*(w/4)..
+        // epilogue: warp w reads TMEM lanes (features) 32*(w%4).. and token
+        // columns (TT/2)*(w/4)..; for each token the warp stores 32
+        // consecutive features
         if (__all_sync(0xffffffffu, ok && wait_or_abort(accum, 0, abort_flag))) {
             tc_fence_after();
             const int lane_base = 32 * (warp % 4);
-            const int col_base = 128 * (warp / 4);
-            const std::uint32_t m = m0 + lane_base + lane;
+            const int col_base = (TT / 2) * (warp / 4);
+            const std::uint32_t n = n0 + lane_base + lane;
+            const bool n_ok = n < p.N;
 #pragma unroll 1
-            for (int cb = 0; cb < 128; cb += 32) {
+            for (int cb = 0; cb < TT / 2; cb += 32) {
                 std::uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem_d + (static_cast<std::uint32_t>(lane_base) << 16) +
                                        static_cast<std::uint32_t>(col_base + cb),
                                    v);
-                const std::uint32_t n = n0 + col_base + cb;
-                if (m < p.M && n < p.N) {
-                    if constexpr (OF32) {
-                        float* yr = static_cast<float*>(p.y) + m * p.ldy + n;
-                        if (n + 32 <= p.N && (reinterpret_cast<std::uintptr_t>(yr) & 15) == 0) {
+                const std::uint32_t mb = m0 + col_base + cb;
 #pragma unroll
-                            for (int i = 0; i < 32; i += 4)
-                                *reinterpret_cast<uint4*>(yr + i) =
-                                    make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                        } else {
-                            for (int i = 0; i < 32 && n + i < p.N; ++i)
-                                yr[i] = __uint_as_float(v[i]);
-                        }
-                    } else {
-                        __half* yr = static_cast<__half*>(p.y) + m * p.ldy + n;
-                        std::uint32_t hv[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * i]),
-                                                                 __uint_as_float(v[2 * i + 1]));
-                            hv[i] = *reinterpret_cast<const std::uint32_t*>(&h2);
-                        }
-                        if (n + 32 <= p.N && (reinterpret_cast<std::uintptr_t>(yr) & 15) == 0) {
-#pragma unroll
-                            for (int i = 0; i < 16; i += 4)
-                                *reinterpret_cast<uint4*>(yr + 2 * i) =
-                                    make_uint4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
-                        } else {
-                            for (int i = 0; i < 32 && n + i < p.N; ++i)
-                                yr[i] = __ushort_as_half(static_cast<unsigned short>(
-                                    (hv[i / 2] >> (16 * (i & 1))) & 0xFFFFu));
-                        }
+                for (int i = 0; i < 32; ++i) {
+                    const std::uint32_t m = mb + i;
+                    if (n_ok && m < p.M) {
+                        if constexpr (OF32)
+                            static_cast<float*>(p.y)[m * p.ldy + n] = __uint_as_float(v[i]);
+                        else
+                            static_cast<__half*>(p.y)[m * p.ldy + n] =
+                                __float2half_rn(__uint_as_float(v[i]));
                     }
                 }
             }
@@ -447,16 +449,17 @@ inline bool supported(const void* x, const void* w, const void* y, std::uint64_t
            reinterpret_cast<std::uintptr_t>(y) % 16 == 0 && (N * out_size) % 16 == 0;
 }
 
-template <bool OF32>
-int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
-           std::uint64_t K, cudaStream_t stream) {
+template <int TT, bool OF32>
+int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
+                std::uint64_t K, cudaStream_t stream) {
+    using L = Layout<TT>;
     auto encode = encode_fn();
     if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
     CUtensorMap map_x{}, map_w{};
     {
         const cuuint64_t dims[2] = {K, M};
         const cuuint64_t strides[1] = {K * 2};
-        const cuuint32_t box[2] = {kBK, kBM};
+        const cuuint32_t box[2] = {kBK, TT};
         const cuuint32_t estr[2] = {1, 1};
         if (encode(&map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -468,7 +471,7 @@ int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t
         const std::uint64_t pitch = (K / 32) * 18;
         const cuuint64_t dims[2] = {pitch, N};
         const cuuint64_t strides[1] = {pitch};
-        const cuuint32_t box[2] = {kRawRowBytes, kBN};
+        const cuuint32_t box[2] = {kRawRowBytes, kFT};
         const cuuint32_t estr[2] = {1, 1};
         if (encode(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -476,23 +479,34 @@ int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return static_cast<int>(cudaErrorInvalidValue);
     }
-    auto kernel = q4_0_gemm_tcgen05_kernel<OF32>;
+    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32>;
     static std::atomic<std::uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_cast<int>(e);
     const std::uint64_t bit = 1ull << (dev & 63);
     if (!(configured.load() & bit)) {
-        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 L::kSmemBytes);
         if (e != cudaSuccess) return static_cast<int>(e);
         configured.fetch_or(bit);
     }
     Params p{y, static_cast<std::uint32_t>(M), static_cast<std::uint32_t>(N),
              static_cast<std::uint32_t>(K), N};
-    const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN),
-                    static_cast<unsigned>((M + kBM - 1) / kBM));
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_x, map_w, p);
+    const dim3 grid(static_cast<unsigned>((N + kFT - 1) / kFT),
+                    static_cast<unsigned>((M + TT - 1) / TT));
+    kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(map_x, map_w, p);
     return static_cast<int>(cudaGetLastError());
+}
+
+// Token tile: the narrowest of 64 / 128 / 256 that holds M (wider tiles
+// waste MMA columns on missing tokens), 256 beyond.
+template <bool OF32>
+int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
+           std::uint64_t K, cudaStream_t stream) {
+    if (M <= 64) return launch_tile<64, OF32>(x, w, y, M, N, K, stream);
+    if (M <= 128) return launch_tile<128, OF32>(x, w, y, M, N, K, stream);
+    return launch_tile<256, OF32>(x, w, y, M, N, K, stream);
 }
 
 }  // namespace gemm

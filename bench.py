@@ -424,27 +424,36 @@ class Bench:
         for layer in layers:
             layer.set_position(77)
 
-        def run():
+        def run_chain():
             layers[0].step()
             for prev, layer in zip(layers, layers[1:]):
                 layer.step(prev.out)
 
-        run()
-        ctx.sync()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=torch.cuda.ExternalStream(ctx.stream)):
-            run()
-        # kernels per layer: rms_norm, QKV, 2 x RoPE, O, fused add+norm,
-        # gate/up+SwiGLU, down+residual; the first layer adds the gather
-        launches = 8 * count + 1
-        ms = self.time_graph(g, 20, launches) / count
-        assert ctx.device_status() == 0
-        del g, layers
-        return {"us_per_layer": round(ms * 1e3, 3),
-                "gbs": round(per_layer / ms / 1e6, 1), "weight_bytes_per_layer": per_layer,
-                "layers_in_stack": count,
-                "kernels_per_layer": 8,
-                "bytes": "Q4_0 weight bytes of QKV, O, gate, up, down (activations < 0.3%)"}
+        def run_fused():
+            layers[0].step_fused()
+            for prev, layer in zip(layers, layers[1:]):
+                layer.step_fused(prev.out)
+
+        result = {"weight_bytes_per_layer": per_layer, "layers_in_stack": count,
+                  "bytes": "Q4_0 weight bytes of QKV, O, gate, up, down (activations < 0.3%)"}
+        # kernels per layer -- chain: rms_norm, QKV, 2 x RoPE, O, fused
+        # add+norm, gate/up+SwiGLU, down+residual; fused: norm+QKV+RoPE,
+        # O+residual, norm+gate/up+SwiGLU, down+residual; plus one gather
+        for name, body, kernels in (("chain", run_chain, 8), ("fused", run_fused, 4)):
+            body()
+            ctx.sync()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=torch.cuda.ExternalStream(ctx.stream)):
+                body()
+            ms = self.time_graph(g, 20, kernels * count + 1) / count
+            assert ctx.device_status() == 0
+            del g
+            result[name] = {"us_per_layer": round(ms * 1e3, 3),
+                            "gbs": round(per_layer / ms / 1e6, 1), "kernels_per_layer": kernels}
+        del layers
+        result["us_per_layer"] = min(result["chain"]["us_per_layer"],
+                                     result["fused"]["us_per_layer"])
+        return result
 
     def config5(self) -> dict:
         torch = self.torch

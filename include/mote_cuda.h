@@ -134,6 +134,34 @@ int mote_cuda_quantized_linear_q4_0_f16_residual(const void* input, const void* 
                                                  uint64_t rows, uint64_t output_features,
                                                  uint64_t input_features, void* stream);
 
+/* Decoder-layer fusions (no reference counterpart: the reference launches
+ * rms_norm_f16, crates/mote-backend-hip/src/rms_norm.hip, and the linear
+ * separately).  The f16 input rows are RMS-normalised with gamma [K] (f16)
+ * and epsilon (finite, >= 0) inside the projection's activation staging --
+ * mote-reference's rms_norm_f32 arithmetic, rounded to f16 -- then
+ * projected.  Fast-path shapes only: K % 256 == 0, K > 0, 16-byte aligned
+ * input, gamma and weights, else 1; rows == 0 or no outputs -> 0 without a
+ * launch; rows * N beyond 32 bits -> 9. */
+int mote_cuda_q4_0_rms_norm_linear_f16(const void* input, const void* gamma, const void* weights,
+                                       void* output, uint64_t rows, uint64_t output_features,
+                                       uint64_t input_features, float epsilon, void* stream);
+/* ... then gate/up projection with the SwiGLU epilogue. */
+int mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16(const void* input, const void* gamma,
+                                               const void* gate_weights, const void* up_weights,
+                                               void* output, uint64_t rows, uint64_t ffn_features,
+                                               uint64_t input_features, float epsilon,
+                                               void* stream);
+/* ... then the QKV projection [rows, (q_heads + 2 kv_heads) * head_dim] with
+ * RoPE (HalfSplit, rotary_dim = head_dim) applied to the q and k heads from
+ * the f32 accumulators (one f16 rounding); cos/sin are f32
+ * [rows, head_dim/2] as mote_cuda_rope_f16 takes them, 4-byte aligned;
+ * head_dim a multiple of 16. */
+int mote_cuda_q4_0_rms_norm_qkv_rope_f16(const void* input, const void* gamma, const void* weights,
+                                         const void* cos, const void* sin, void* output,
+                                         uint64_t rows, uint64_t q_heads, uint64_t kv_heads,
+                                         uint64_t head_dim, uint64_t input_features,
+                                         float epsilon, void* stream);
+
 /* Decodes Q4_0 [rows, K] to f32, bit-identical to mote-reference's
  * dequantize_quantized_row (crates/mote-reference/src/quantized.rs:58-74). */
 int mote_cuda_q4_0_decode_f32(const void* weights, void* output, uint64_t rows,

@@ -52,6 +52,10 @@ SIGNATURES: dict[str, tuple] = {
     "mote_cuda_quantized_linear_q4_0_f32": (I, [P, P, P, U64, U64, U64, P]),
     "mote_cuda_q4_0_gate_up_swiglu_f16": (I, [P, P, P, P, U64, U64, U64, P]),
     "mote_cuda_quantized_linear_q4_0_f16_residual": (I, [P, P, P, P, U64, U64, U64, P]),
+    "mote_cuda_q4_0_rms_norm_linear_f16": (I, [P, P, P, P, U64, U64, U64, F, P]),
+    "mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16": (I, [P, P, P, P, P, U64, U64, U64, F, P]),
+    "mote_cuda_q4_0_rms_norm_qkv_rope_f16": (I, [P, P, P, P, P, P, U64, U64, U64, U64, U64, F,
+                                                 P]),
     "mote_cuda_q4_0_decode_f32": (I, [P, P, U64, U64, P]),
     "mote_cuda_q4_0_encode_f32": (I, [P, P, U64, U64, P]),
     # layer kernels

@@ -36,14 +36,6 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
 
 // 1 / sqrt(mean_square + eps) exactly as the oracle: correctly rounded sqrt
 // and division.
-__device__ __forceinline__ float inv_rms(float sum_sq, std::uint64_t hidden, float eps) {
-    const float mean_square = __fdiv_rn(sum_sq, static_cast<float>(hidden));
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_square, eps)));
-}
-
-__device__ __forceinline__ float norm_out(float x, float inv, float w) {
-    return __fmul_rn(__fmul_rn(x, inv), w);
-}
 
 union H8 {
     uint4 u;
@@ -193,11 +185,6 @@ __global__ void __launch_bounds__(kNormThreads) fused_add_rms_norm_scalar_kernel
 }
 
 // ---- RoPE -------------------------------------------------------------------
-__device__ __forceinline__ void rotate(float a, float b, float c, float s, float& o1,
-                                       float& o2) {
-    o1 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-    o2 = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-}
 
 // One thread per rotation pair or tail element of every (token, head)
 // vector.  Each element is read and written by one thread only, so

@@ -230,6 +230,24 @@ __device__ __forceinline__ float half_bits_to_float(std::uint32_t bits16) {
 // Per-device status word (error codes from bounded waits / index checks).
 // The library is compiled as one translation unit (libmote_cuda.cu includes
 // every component), so this definition is unique.
+// RMSNorm and RoPE arithmetic in mote-reference's operation order
+// (crates/mote-reference/src/lib.rs:289-299 and 170-244), correctly rounded
+// f32 steps, shared by the layer kernels and the GEMV prologue/epilogue.
+__device__ __forceinline__ float inv_rms(float sum_sq, std::uint64_t hidden, float eps) {
+    const float mean_square = __fdiv_rn(sum_sq, static_cast<float>(hidden));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_square, eps)));
+}
+
+__device__ __forceinline__ float norm_out(float x, float inv, float w) {
+    return __fmul_rn(__fmul_rn(x, inv), w);
+}
+
+__device__ __forceinline__ void rotate(float a, float b, float c, float s, float& o1,
+                                       float& o2) {
+    o1 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    o2 = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
 __device__ unsigned g_device_status = 0;
 
 // Launches `kernel` with programmatic dependent launch allowed: it may be

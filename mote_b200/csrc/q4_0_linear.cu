@@ -73,7 +73,26 @@ constexpr int kMaxXRows = 16;                               // two n8 tiles
 // every rank's full output buffer (over NVLink for the peers) and the grid
 // ends with a flag handshake, so every rank holds all shards when the
 // kernel completes.
-enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1, kEpiResidual = 2, kEpiPeers = 3 };
+// kEpiNorm*: the staged activation rows are first RMS-normalised (with
+// gamma, in mote-reference's operation order) -- the norm that precedes a
+// projection in a decoder layer, fused into its prologue.  kEpiNormRope
+// also rotates the q and k rows of a QKV projection (RoPE, HalfSplit) in
+// the epilogue, before the single f16 rounding.
+enum Epilogue : int {
+    kEpiPlain = 0,
+    kEpiSwiGLU = 1,
+    kEpiResidual = 2,
+    kEpiPeers = 3,
+    kEpiNormPlain = 4,
+    kEpiNormSwiGLU = 5,
+    kEpiNormRope = 6
+};
+
+__host__ __device__ constexpr bool epi_norm(int e) { return e >= kEpiNormPlain; }
+__host__ __device__ constexpr bool epi_swiglu(int e) {
+    return e == kEpiSwiGLU || e == kEpiNormSwiGLU;
+}
+__host__ __device__ constexpr bool epi_rope(int e) { return e == kEpiNormRope; }
 
 struct Params {
     const void* x;            // [M, K] f16 or f32, row stride K
@@ -101,6 +120,17 @@ struct Params {
     std::uint64_t col0;
     std::uint32_t rank;
     std::uint32_t nranks;
+    // kEpiNorm*: RMSNorm of the staged rows
+    const __half* gamma;
+    float eps;
+    // kEpiNormRope: the first rope_rows output rows are rope_rows / head_dim
+    // heads rotated with cos/sin [M, head_dim/2] (f32); tiles below
+    // rope_tiles pair rows d and d + head_dim/2 of a head
+    const float* rope_cos;
+    const float* rope_sin;
+    std::uint32_t rope_rows;
+    std::uint32_t rope_tiles;
+    std::uint32_t head_dim;
 };
 
 __host__ __device__ constexpr int red_bytes(int nt) { return 2 * kWarps * nt * 4 * 32 * 4; }
@@ -148,6 +178,25 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return g / (1.0f + expf(-g)) * u;
 }
 
+// Output row held by A row i (0..15) of a kEpiNormRope tile.  A rope tile
+// (tile < rope_tiles) covers 8 consecutive rows d of the first half of a
+// head (A rows 0-7) and their partners d + head_dim/2 (A rows 8-15), so
+// lane (g, t) holds both elements of a rotation pair; the later tiles are
+// plain runs of 16 rows (the v heads).
+__device__ __forceinline__ std::uint32_t rope_tile_row(const Params& p, std::uint32_t tile,
+                                                       int i) {
+    std::uint32_t r;
+    if (tile < p.rope_tiles) {
+        const std::uint32_t per_head = p.head_dim / 16;
+        const std::uint32_t h = tile / per_head;
+        const std::uint32_t j0 = (tile - h * per_head) * 8;
+        r = h * p.head_dim + j0 + (i & 7) + (i < 8 ? 0u : p.head_dim / 2);
+    } else {
+        r = p.rope_rows + (tile - p.rope_tiles) * 16u + i;
+    }
+    return min(r, p.N - 1);
+}
+
 // Source row i (0..15) of a tile.  Plain tiles are 16 consecutive rows;
 // SwiGLU tiles pair gate rows f..f+7 (A rows 0-7) with up rows f..f+7
 // (A rows 8-15) so lane (g, t) ends up holding gate and up of the same
@@ -155,9 +204,11 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 template <int EPI>
 __device__ __forceinline__ const std::uint8_t* tile_row(const Params& p, std::uint32_t tile,
                                                         int i) {
-    if constexpr (EPI == kEpiSwiGLU) {
+    if constexpr (epi_swiglu(EPI)) {
         const std::uint32_t f = min(tile * 8u + (i & 7), p.N - 1);
         return (i < 8 ? p.w : p.w2) + f * p.pitch;
+    } else if constexpr (epi_rope(EPI)) {
+        return p.w + rope_tile_row(p, tile, i) * p.pitch;
     } else {
         const std::uint32_t r = min(tile * 16u + i, p.N - 1);
         return p.w + r * p.pitch;
@@ -169,7 +220,42 @@ __device__ __forceinline__ void store_tile(const Params& p, std::uint32_t tile, 
                                            const float (&acc)[NT][4], __half* stage = nullptr) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-        if constexpr (EPI == kEpiSwiGLU) {
+        if constexpr (epi_rope(EPI)) {
+            if (tile < p.rope_tiles) {
+                // rows (d, d + head_dim/2) of one head: rotate, round once
+                const std::uint32_t per_head = p.head_dim / 16;
+                const std::uint32_t h = tile / per_head;
+                const std::uint32_t j = (tile - h * per_head) * 8 + g;
+                const std::uint32_t r1 = h * p.head_dim + j;
+                const std::uint32_t r2 = r1 + p.head_dim / 2;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const std::uint32_t m = nt * 8 + 2 * t + c;
+                    if (m >= p.M) continue;
+                    const float cs = p.rope_cos[m * (p.head_dim / 2) + j];
+                    const float sn = p.rope_sin[m * (p.head_dim / 2) + j];
+                    float o1, o2;
+                    rotate(acc[nt][c], acc[nt][2 + c], cs, sn, o1, o2);
+                    static_cast<__half*>(p.y)[m * p.ldy + r1] = __float2half_rn(o1);
+                    static_cast<__half*>(p.y)[m * p.ldy + r2] = __float2half_rn(o2);
+                }
+            } else {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const std::uint32_t r = p.rope_rows + (tile - p.rope_tiles) * 16u + g + 8 * half;
+                    if (r >= p.N) continue;
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        const std::uint32_t m = nt * 8 + 2 * t + c;
+                        if (m >= p.M) continue;
+                        static_cast<__half*>(p.y)[m * p.ldy + r] =
+                            __float2half_rn(acc[nt][2 * half + c]);
+                    }
+                }
+            }
+            continue;
+        }
+        if constexpr (epi_swiglu(EPI)) {
             const std::uint32_t f = tile * 8u + g;
             if (f >= p.N) continue;
             if constexpr (!XF32) {
@@ -423,6 +509,74 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
                 make_uint4(0u, 0u, 0u, 0u);
         __syncthreads();
     }
+    if constexpr (epi_norm(EPI)) {
+        static_assert(!XF32, "the fused norm takes f16 activations");
+        // RMSNorm of the staged rows, in place: every CTA normalises the rows
+        // it uses.  Per-row sums of squares (f32, correctly rounded steps),
+        // a block reduction, inv = 1/sqrt(mean + eps), then x * inv * gamma
+        // rounded once to f16 -- mote-reference's rms_norm_f32 arithmetic
+        // (crates/mote-reference/src/lib.rs:289-299), in the staged order
+        // (gamma permuted like the activations).
+        // scratch in the (not yet used) reduction area: partial sums per
+        // warp and row, then the per-row 1/rms
+        float (*norm_part)[kMaxXRows] = reinterpret_cast<float (*)[kMaxXRows]>(red);
+        float* norm_inv = red + kWarps * kMaxXRows;
+        static_assert((kWarps + 1) * kMaxXRows * 4 <= red_bytes(1), "norm scratch");
+        const std::uint32_t chunks = static_cast<std::uint32_t>(p.K / 8);
+        float ss[kMaxXRows];
+#pragma unroll
+        for (int m = 0; m < kMaxXRows; ++m) ss[m] = 0.f;
+        for (std::uint32_t i = threadIdx.x; i < chunks; i += kThreads) {
+#pragma unroll
+            for (int m = 0; m < kMaxXRows; ++m) {
+                if (static_cast<std::uint32_t>(m) < p.M) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(xs + m * p.x_stride + 16 * i);
+                    const std::uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 f = half2_bits_to_float2(words[q]);
+                        ss[m] = __fadd_rn(ss[m], __fmul_rn(f.x, f.x));
+                        ss[m] = __fadd_rn(ss[m], __fmul_rn(f.y, f.y));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < kMaxXRows; ++m) {
+            float v = ss[m];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) norm_part[warp][m] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < p.M) {
+            float total = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) total += norm_part[w][threadIdx.x];
+            norm_inv[threadIdx.x] = inv_rms(total, p.K, p.eps);
+        }
+        __syncthreads();
+        for (std::uint32_t i = threadIdx.x; i < chunks; i += kThreads) {
+            const uint4 gr = __ldg(reinterpret_cast<const uint4*>(p.gamma) + i);
+            const std::uint32_t gw[4] = {prmt(gr.x, gr.y, 0x5410u), prmt(gr.x, gr.y, 0x7632u),
+                                         prmt(gr.z, gr.w, 0x5410u), prmt(gr.z, gr.w, 0x7632u)};
+            for (std::uint32_t m = 0; m < p.M; ++m) {
+                uint4* at = reinterpret_cast<uint4*>(xs + m * p.x_stride + 16 * i);
+                const uint4 v = *at;
+                const std::uint32_t words[4] = {v.x, v.y, v.z, v.w};
+                std::uint32_t out[4];
+                const float inv = norm_inv[m];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f = half2_bits_to_float2(words[q]);
+                    const float2 w = half2_bits_to_float2(gw[q]);
+                    out[q] = pack_half2(norm_out(f.x, inv, w.x), norm_out(f.y, inv, w.y));
+                }
+                *at = make_uint4(out[0], out[1], out[2], out[3]);
+            }
+        }
+        __syncthreads();
+    }
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
@@ -606,7 +760,7 @@ __global__ void __launch_bounds__(128) q4_0_linear_generic_kernel(const Params p
     float acc[2][kGenericTokens];
 #pragma unroll
     for (int j = 0; j < kGenericTokens; ++j) acc[0][j] = acc[1][j] = 0.f;
-    const int nmat = EPI == kEpiSwiGLU ? 2 : 1;
+    const int nmat = epi_swiglu(EPI) ? 2 : 1;
     for (int mat = 0; mat < nmat; ++mat) {
         const std::uint8_t* row = (mat == 0 ? p.w : p.w2) + warp_global * p.pitch;
         for (std::uint64_t b = lane; b < nb; b += 32) {
@@ -651,7 +805,7 @@ __global__ void __launch_bounds__(128) q4_0_linear_generic_kernel(const Params p
         const std::uint32_t m = m0 + mm;
         if (m >= p.M) break;
         float v = acc[0][mm];
-        if constexpr (EPI == kEpiSwiGLU) v = silu_mul(acc[0][mm], acc[1][mm]);
+        if constexpr (epi_swiglu(EPI)) v = silu_mul(acc[0][mm], acc[1][mm]);
         if constexpr (EPI == kEpiResidual) v += __half2float(p.res[m * p.ldy + warp_global]);
         if constexpr (OF32)
             static_cast<float*>(p.y)[m * p.ldy + warp_global] = v;
@@ -790,15 +944,35 @@ struct PeerArgs {
     std::uint64_t col0;
     std::uint32_t rank;
     std::uint32_t nranks;
+    // kEpiNorm*: RMSNorm of the staged rows
+    const __half* gamma;
+    float eps;
+    // kEpiNormRope: the first rope_rows output rows are rope_rows / head_dim
+    // heads rotated with cos/sin [M, head_dim/2] (f32); tiles below
+    // rope_tiles pair rows d and d + head_dim/2 of a head
+    const float* rope_cos;
+    const float* rope_sin;
+    std::uint32_t rope_rows;
+    std::uint32_t rope_tiles;
+    std::uint32_t head_dim;
 };
 
 template <bool XF32, bool OF32, int EPI>
 int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint64_t M,
                std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream,
-               const void* res = nullptr, const PeerArgs* peers = nullptr) {
+               const void* res = nullptr, const PeerArgs* peers = nullptr,
+               const Params* fused = nullptr) {
     const std::size_t osz = OF32 ? 4 : 2;
+    // epilogues that exist only on the fast path
+    constexpr bool kFastOnly = EPI == kEpiPeers || epi_norm(EPI);
     if constexpr (EPI == kEpiPeers) {
-        if (peers == nullptr || K == 0) return kInvalidValue;
+        if (peers == nullptr) return kInvalidValue;
+    }
+    if constexpr (epi_norm(EPI)) {
+        if (fused == nullptr) return kInvalidValue;
+    }
+    if constexpr (kFastOnly) {
+        if (K == 0) return kInvalidValue;
     }
     if (K == 0) {
         // Every dot product is empty: the reference writes zeros
@@ -836,18 +1010,29 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         p.rank = peers->rank;
         p.nranks = peers->nranks;
     }
-    const std::uint64_t rows_per_tile = EPI == kEpiSwiGLU ? 8 : 16;
+    if (fused != nullptr) {
+        p.gamma = fused->gamma;
+        p.eps = fused->eps;
+        p.rope_cos = fused->rope_cos;
+        p.rope_sin = fused->rope_sin;
+        p.rope_rows = fused->rope_rows;
+        p.rope_tiles = fused->rope_tiles;
+        p.head_dim = fused->head_dim;
+    }
+    const std::uint64_t rows_per_tile = epi_swiglu(EPI) ? 8 : 16;
     p.tiles = static_cast<std::uint32_t>((N + rows_per_tile - 1) / rows_per_tile);
+    if constexpr (epi_rope(EPI))
+        p.tiles = p.rope_tiles + static_cast<std::uint32_t>((N - p.rope_rows + 15) / 16);
     const std::size_t xes = XF32 ? 4 : 2;
     bool fast = (K % 256 == 0) && (reinterpret_cast<std::uintptr_t>(w) % 16 == 0) &&
                 (reinterpret_cast<std::uintptr_t>(x) % 16 == 0);
-    if (EPI == kEpiSwiGLU) fast = fast && (reinterpret_cast<std::uintptr_t>(w2) % 16 == 0);
+    if (epi_swiglu(EPI)) fast = fast && (reinterpret_cast<std::uintptr_t>(w2) % 16 == 0);
     std::uint32_t tokens = 0;
     int nt = 1, stages = 2, ctas = 1;
     if (fast)
         fast = plan_gemv(M, K, XF32, EPI == kEpiPeers, tokens, nt, stages, ctas, p.x_rows,
                          p.x_stride, p.x_bytes);
-    if (EPI == kEpiPeers && !fast) return kInvalidValue;
+    if (kFastOnly && !fast) return kInvalidValue;
     if (fast)
         p.split_shift =
             choose_split_shift(p.tiles, p.units, static_cast<std::uint32_t>(sm_count() * ctas));
@@ -858,12 +1043,16 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         p.x = static_cast<const std::uint8_t*>(x) + m0 * K * xes;
         p.y = static_cast<std::uint8_t*>(y) + m0 * ldy * osz;
         if (res != nullptr) p.res = static_cast<const __half*>(res) + m0 * ldy;
+        if (fused != nullptr && fused->rope_cos != nullptr) {  // per-token RoPE tables
+            p.rope_cos = fused->rope_cos + m0 * (fused->head_dim / 2);
+            p.rope_sin = fused->rope_sin + m0 * (fused->head_dim / 2);
+        }
         int st;
         if (fast) {
             p.x_rows = static_cast<std::uint32_t>(mc) * (XF32 ? 2 : 1);
             p.x_zero_row = p.x_rows;
             st = launch_gemv_config<XF32, OF32, EPI>(p, stages, ctas, stream);
-        } else if constexpr (EPI != kEpiPeers) {
+        } else if constexpr (!kFastOnly) {
             const dim3 grid(static_cast<unsigned>((N + 3) / 4),
                             static_cast<unsigned>((mc + kGenericTokens - 1) / kGenericTokens));
             q4_0_linear_generic_kernel<XF32, OF32, EPI><<<grid, 128, 0, stream>>>(p);
@@ -1009,4 +1198,100 @@ extern "C" int mote_cuda_quantized_linear_q4_0_f16_allgather(
     return run_linear<false, false, kEpiPeers>(input, weights, nullptr, nullptr, rows, real,
                                                input_features, total_features,
                                                static_cast<cudaStream_t>(stream), nullptr, &peers);
+}
+
+// ---------------------------------------------------------------------------
+// Decoder-layer fusions.  No reference counterparts: the reference runs
+// rms_norm_f16 (crates/mote-backend-hip/src/rms_norm.hip) and the linear as
+// separate launches.  Each takes f16 input rows, RMS-normalises them with
+// gamma (eps finite and >= 0) inside the projection's activation staging,
+// then projects.  Fast-path shapes only: K % 256 == 0, K > 0, 16-byte
+// aligned input, gamma and weights; otherwise 1.  rows == 0 or no output
+// features -> 0 without a launch; rows * N beyond 32 bits -> 9.
+// ---------------------------------------------------------------------------
+namespace mote {
+namespace q4 {
+inline int check_fused_norm(const void* gamma, float eps) {
+    if (gamma == nullptr || !isfinite(eps) || eps < 0.0f) return kInvalidValue;
+    if (reinterpret_cast<std::uintptr_t>(gamma) % 16 != 0) return kInvalidValue;
+    return kSuccess;
+}
+}  // namespace q4
+}  // namespace mote
+
+extern "C" int mote_cuda_q4_0_rms_norm_linear_f16(const void* input, const void* gamma,
+                                                  const void* weights, void* output,
+                                                  std::uint64_t rows,
+                                                  std::uint64_t output_features,
+                                                  std::uint64_t input_features, float epsilon,
+                                                  void* stream) {
+    using namespace mote::q4;
+    const int c = check_linear_args(input, weights, output, rows, output_features,
+                                    input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    if (const int n = check_fused_norm(gamma, epsilon); n != 0) return n;
+    Params f{};
+    f.gamma = static_cast<const __half*>(gamma);
+    f.eps = epsilon;
+    return run_linear<false, false, kEpiNormPlain>(input, weights, nullptr, output, rows,
+                                                   output_features, input_features,
+                                                   output_features,
+                                                   static_cast<cudaStream_t>(stream), nullptr,
+                                                   nullptr, &f);
+}
+
+extern "C" int mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16(
+    const void* input, const void* gamma, const void* gate_weights, const void* up_weights,
+    void* output, std::uint64_t rows, std::uint64_t ffn_features, std::uint64_t input_features,
+    float epsilon, void* stream) {
+    using namespace mote::q4;
+    if (up_weights == nullptr) return mote::kInvalidValue;
+    const int c = check_linear_args(input, gate_weights, output, rows, ffn_features,
+                                    input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    if (const int n = check_fused_norm(gamma, epsilon); n != 0) return n;
+    Params f{};
+    f.gamma = static_cast<const __half*>(gamma);
+    f.eps = epsilon;
+    return run_linear<false, false, kEpiNormSwiGLU>(input, gate_weights, up_weights, output, rows,
+                                                    ffn_features, input_features, ffn_features,
+                                                    static_cast<cudaStream_t>(stream), nullptr,
+                                                    nullptr, &f);
+}
+
+// QKV projection of a decoder layer: output [rows, (q_heads + 2 kv_heads) *
+// head_dim] = norm(input) @ W^T, with RoPE (HalfSplit, rotary_dim =
+// head_dim) applied to the q and k heads from the f32 accumulators, cos/sin
+// f32 [rows, head_dim/2] as mote_cuda_rope_f16 takes them.  head_dim a
+// multiple of 16.
+extern "C" int mote_cuda_q4_0_rms_norm_qkv_rope_f16(
+    const void* input, const void* gamma, const void* weights, const void* cos, const void* sin,
+    void* output, std::uint64_t rows, std::uint64_t q_heads, std::uint64_t kv_heads,
+    std::uint64_t head_dim, std::uint64_t input_features, float epsilon, void* stream) {
+    using namespace mote::q4;
+    if (cos == nullptr || sin == nullptr) return mote::kInvalidValue;
+    if (head_dim == 0 || head_dim % 16 != 0 || head_dim > 65536 || q_heads > 65536 ||
+        kv_heads > 65536)
+        return mote::kInvalidValue;
+    if ((reinterpret_cast<std::uintptr_t>(cos) | reinterpret_cast<std::uintptr_t>(sin)) % 4 != 0)
+        return mote::kInvalidValue;
+    const std::uint64_t n = (q_heads + 2 * kv_heads) * head_dim;
+    const int c = check_linear_args(input, weights, output, rows, n, input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    if (const int e = check_fused_norm(gamma, epsilon); e != 0) return e;
+    Params f{};
+    f.gamma = static_cast<const __half*>(gamma);
+    f.eps = epsilon;
+    f.rope_cos = static_cast<const float*>(cos);
+    f.rope_sin = static_cast<const float*>(sin);
+    f.head_dim = static_cast<std::uint32_t>(head_dim);
+    f.rope_rows = static_cast<std::uint32_t>((q_heads + kv_heads) * head_dim);
+    f.rope_tiles = f.rope_rows / 16;
+    return run_linear<false, false, kEpiNormRope>(input, weights, nullptr, output, rows, n,
+                                                  input_features, n,
+                                                  static_cast<cudaStream_t>(stream), nullptr,
+                                                  nullptr, &f);
 }

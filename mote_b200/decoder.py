@@ -117,6 +117,30 @@ class DecoderLayerQ4_0:
         ops.quantized_linear_q4_0_f16_residual(ctx, self.a, self.w_down, h, self.out)
 
 
+    def step_fused(self, hidden: Tensor | None = None) -> None:
+        """The same layer in four kernels (five with the gather): the norms
+        run inside the activation staging of the projection that follows
+        them, RoPE inside the QKV epilogue, and the two residual adds in the
+        O and down projections' epilogues.
+
+            h   (gather, or ``hidden``)
+            qkv = rope(rms_norm(h) @ Wqkv^T)              q4_0_rms_norm_qkv_rope_f16
+            h1  = h + attn @ Wo^T        (in place in h)  quantized_linear_q4_0_f16_residual
+            a   = swiglu(rms_norm(h1) @ [Wg; Wu]^T)       q4_0_rms_norm_gate_up_swiglu_f16
+            out = h1 + a @ Wd^T                           quantized_linear_q4_0_f16_residual
+        """
+        ctx, s = self.ctx, self.shape
+        h = self.h if hidden is None else hidden
+        if hidden is None:
+            ops.embedding_gather_f16(ctx, self.embedding, self.ids, self.h, check=False)
+        ops.q4_0_rms_norm_qkv_rope_f16(ctx, h, self.gamma1, self.w_qkv, self.cos, self.sin,
+                                       self.qkv, s.q_heads, s.kv_heads, s.head_dim, s.eps)
+        ops.quantized_linear_q4_0_f16_residual(ctx, self.attn, self.w_o, h, h)
+        ops.q4_0_rms_norm_gate_up_swiglu_f16(ctx, h, self.gamma2, self.w_gate, self.w_up, self.a,
+                                             s.eps)
+        ops.quantized_linear_q4_0_f16_residual(ctx, self.a, self.w_down, h, self.out)
+
+
 def random_layer(ctx: CudaContext, shape: LayerShape, seed: int = 0, vocab: int | None = None):
     """A layer with seeded N(0, 0.02) weights Q4_0-encoded on the device,
     gammas 1 + N(0, 0.1) and an N(0, 0.02) f16 embedding table."""

@@ -103,6 +103,9 @@ _ARG_KINDS = {
     "mote_cuda_quantized_linear_q4_0_f32": "pppuuup",
     "mote_cuda_q4_0_gate_up_swiglu_f16": "ppppuuup",
     "mote_cuda_quantized_linear_q4_0_f16_residual": "ppppuuup",
+    "mote_cuda_q4_0_rms_norm_linear_f16": "ppppuuufp",
+    "mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16": "pppppuuufp",
+    "mote_cuda_q4_0_rms_norm_qkv_rope_f16": "ppppppuuuuufp",
     "mote_cuda_rms_norm_f16": "pppuufp",
     "mote_cuda_fused_add_rms_norm_f16": "ppppuufp",
     "mote_cuda_rope_f16": "ppppuuuuwp",
@@ -121,6 +124,9 @@ CUDA_KERNELS = {
     ("quantized_linear_q4_0", DType.F32): "mote_cuda_quantized_linear_q4_0_f32",
     ("gate_up_swiglu_q4_0", DType.F16): "mote_cuda_q4_0_gate_up_swiglu_f16",
     ("quantized_linear_q4_0_residual", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_residual",
+    ("rms_norm_linear_q4_0", DType.F16): "mote_cuda_q4_0_rms_norm_linear_f16",
+    ("rms_norm_gate_up_swiglu_q4_0", DType.F16): "mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16",
+    ("rms_norm_qkv_rope_q4_0", DType.F16): "mote_cuda_q4_0_rms_norm_qkv_rope_f16",
     ("rms_norm", DType.F16): "mote_cuda_rms_norm_f16",
     ("fused_add_rms_norm", DType.F16): "mote_cuda_fused_add_rms_norm_f16",
     ("rope", DType.F16): "mote_cuda_rope_f16",

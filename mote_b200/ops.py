@@ -186,6 +186,103 @@ def q4_0_gate_up_swiglu_f16(context: CudaContext, input: Tensor, gate: Tensor, u
         "launch gate/up SwiGLU kernel")
 
 
+# ------------------------------------------------- decoder-layer fusions --
+def _norm_gamma(gamma: Tensor, k: int) -> None:
+    _plain(gamma, "gamma", DType.F16)
+    _shape(gamma, "gamma", (k,))
+
+
+def q4_0_rms_norm_linear_f16(context: CudaContext, input: Tensor, gamma: Tensor, weights: Tensor,
+                             output: Tensor, epsilon: float) -> None:
+    """``output = rms_norm(input) * gamma @ weights^T`` (norm fused into the
+    projection's activation staging; f16 in, f16 out)."""
+    _plain(input, "input", DType.F16)
+    _rank(input, "input", 2)
+    _q4_0_matrix(weights)
+    _plain(output, "output", DType.F16)
+    _epsilon(epsilon)
+    rows, k = input.shape
+    n = weights.shape[0]
+    _shape(weights, "weights", (n, k))
+    _shape(output, "output", (rows, n))
+    _norm_gamma(gamma, k)
+    in_s, g_s, w_s, out_s = (context.storage(t) for t in (input, gamma, weights, output))
+    for other, name in ((input, "input"), (weights, "weights"), (gamma, "gamma")):
+        _not_aliased(output, "output", other, name)
+    if rows * n > U32_MAX:
+        raise errors.QuantizedLinearDimensionsTooLarge(rows=rows, output_features=n,
+                                                       input_features=k)
+    if rows * n == 0:
+        return
+    context.inner.select()
+    errors.check(lib().mote_cuda_q4_0_rms_norm_linear_f16(
+        in_s.pointer, g_s.pointer, w_s.pointer, out_s.pointer, rows, n, k,
+        ctypes.c_float(epsilon), context.stream), "launch RMSNorm + Q4_0 linear kernel")
+
+
+def q4_0_rms_norm_gate_up_swiglu_f16(context: CudaContext, input: Tensor, gamma: Tensor,
+                                     gate: Tensor, up: Tensor, output: Tensor,
+                                     epsilon: float) -> None:
+    """``output = silu(x_n @ gate^T) * (x_n @ up^T)``, x_n = rms_norm(input) * gamma."""
+    _plain(input, "input", DType.F16)
+    _rank(input, "input", 2)
+    _q4_0_matrix(gate, "gate")
+    _q4_0_matrix(up, "up")
+    _plain(output, "output", DType.F16)
+    _epsilon(epsilon)
+    rows, k = input.shape
+    f = gate.shape[0]
+    _shape(gate, "gate", (f, k))
+    _shape(up, "up", (f, k))
+    _shape(output, "output", (rows, f))
+    _norm_gamma(gamma, k)
+    in_s, gm_s, g_s, u_s, out_s = (context.storage(t) for t in (input, gamma, gate, up, output))
+    for other, name in ((input, "input"), (gate, "gate"), (up, "up"), (gamma, "gamma")):
+        _not_aliased(output, "output", other, name)
+    if rows * f > U32_MAX:
+        raise errors.QuantizedLinearDimensionsTooLarge(rows=rows, output_features=f,
+                                                       input_features=k)
+    if rows * f == 0:
+        return
+    context.inner.select()
+    errors.check(lib().mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16(
+        in_s.pointer, gm_s.pointer, g_s.pointer, u_s.pointer, out_s.pointer, rows, f, k,
+        ctypes.c_float(epsilon), context.stream), "launch RMSNorm + gate/up SwiGLU kernel")
+
+
+def q4_0_rms_norm_qkv_rope_f16(context: CudaContext, input: Tensor, gamma: Tensor,
+                               weights: Tensor, cos: Tensor, sin: Tensor, output: Tensor,
+                               q_heads: int, kv_heads: int, head_dim: int,
+                               epsilon: float) -> None:
+    """QKV projection of ``rms_norm(input) * gamma`` with RoPE (HalfSplit)
+    applied to the q and k heads before the f16 rounding.  ``output`` is
+    ``[rows, (q_heads + 2 kv_heads) * head_dim]``; cos/sin ``[rows, head_dim/2]``."""
+    _plain(input, "input", DType.F16)
+    _rank(input, "input", 2)
+    _q4_0_matrix(weights)
+    _plain(output, "output", DType.F16)
+    _plain(cos, "cos", DType.F32)
+    _plain(sin, "sin", DType.F32)
+    _epsilon(epsilon)
+    rows, k = input.shape
+    n = (q_heads + 2 * kv_heads) * head_dim
+    _shape(weights, "weights", (n, k))
+    _shape(output, "output", (rows, n))
+    _shape(cos, "cos", (rows, head_dim // 2))
+    _shape(sin, "sin", (rows, head_dim // 2))
+    _norm_gamma(gamma, k)
+    ptrs = [context.storage(t).pointer for t in (input, gamma, weights, cos, sin, output)]
+    for other, name in ((input, "input"), (weights, "weights"), (gamma, "gamma"), (cos, "cos"),
+                        (sin, "sin")):
+        _not_aliased(output, "output", other, name)
+    if rows * n == 0:
+        return
+    context.inner.select()
+    errors.check(lib().mote_cuda_q4_0_rms_norm_qkv_rope_f16(
+        *ptrs, rows, q_heads, kv_heads, head_dim, k, ctypes.c_float(epsilon), context.stream),
+        "launch RMSNorm + QKV + RoPE kernel")
+
+
 def q4_0_encode_f32(context: CudaContext, input: Tensor, weights: Tensor) -> None:
     """Quantizes f32 [N, K] into Q4_0 [N, K] (ggml reference rule)."""
     _plain(input, "input", DType.F32)

@@ -169,3 +169,21 @@ def test_fused_allgather_argument_rules(lib):
     assert fn(*ok, 1, 16, 33, 32, 0, 2, STREAM) == 1       # K not a multiple of 32
     assert fn(FAKE, FAKE, None, FAKE, FAKE, 1, 16, 256, 32, 0, 2, STREAM) == 1
     assert fn(*ok, 0, 16, 256, 32, 0, 2, STREAM) == 0      # no rows: no launch
+
+
+def test_fused_norm_argument_rules(lib):
+    eps = ctypes.c_float(1e-5)
+    lin = lib.mote_cuda_q4_0_rms_norm_linear_f16
+    assert lin(FAKE, None, FAKE, FAKE, 1, 16, 256, eps, STREAM) == 1          # null gamma
+    assert lin(FAKE, FAKE, FAKE, FAKE, 1, 16, 256, ctypes.c_float(float("nan")), STREAM) == 1
+    assert lin(FAKE, FAKE, FAKE, FAKE, 1, 16, 256, ctypes.c_float(-1.0), STREAM) == 1
+    assert lin(FAKE, FAKE + 2, FAKE, FAKE, 1, 16, 256, eps, STREAM) == 1      # gamma alignment
+    assert lin(FAKE, FAKE, FAKE, FAKE, 0, 16, 256, eps, STREAM) == 0          # empty
+    assert lin(FAKE, FAKE, FAKE, FAKE, 1, 16, 33, eps, STREAM) == 1           # K % 32
+    gu = lib.mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16
+    assert gu(FAKE, FAKE, FAKE, None, FAKE, 1, 16, 256, eps, STREAM) == 1    # null up
+    qkv = lib.mote_cuda_q4_0_rms_norm_qkv_rope_f16
+    assert qkv(FAKE, FAKE, FAKE, None, FAKE, FAKE, 1, 2, 1, 64, 256, eps, STREAM) == 1
+    assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 2, 1, 24, 256, eps, STREAM) == 1  # hd % 16
+    assert qkv(FAKE, FAKE, FAKE, FAKE + 2, FAKE, FAKE, 1, 2, 1, 64, 256, eps, STREAM) == 1
+    assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 2, 1, 64, 256, eps, STREAM) == 0

@@ -241,16 +241,27 @@ class Bench:
         self.sweep_x = {m: self.randn((m, k), 77 + m, torch.float16) for m in SWEEP_M}
         self.sweep_y = {(m, n): torch.empty((m, n), dtype=torch.float16, device=self.dev)
                         for m in SWEEP_M for n in SWEEP_N}
+        # one zeroed workspace for the split-K path (its counters return to
+        # zero after every call; the sweep runs on one stream)
+        need = max(self.workspace_bytes(m, n, k) for m in SWEEP_M for n in SWEEP_N)
+        self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.dev)
         self.sweep_launches = sum(len(self.sweep_w[n]) for n in SWEEP_N) * len(SWEEP_M)
         self.sweep_bytes = sum(linear_bytes(m, n, k) * len(self.sweep_w[n])
                                for m in SWEEP_M for n in SWEEP_N)
 
+    def workspace_bytes(self, m, n, k) -> int:
+        need = ctypes.c_uint64(0)
+        self.check(self.lib.mote_cuda_q4_0_linear_workspace_bytes(m, n, k, ctypes.byref(need)),
+                   "workspace size")
+        return need.value
+
     def sweep_case(self, m, n):
-        fn = self.lib.mote_cuda_quantized_linear_q4_0_f16
+        fn = self.lib.mote_cuda_quantized_linear_q4_0_f16_ws
         x, y = self.sweep_x[m], self.sweep_y[(m, n)]
+        ws = self.workspace
         for w in self.sweep_w[n]:
-            self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, SWEEP_K,
-                          self.stream()), "q4_0 linear")
+            self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, SWEEP_K, ws.data_ptr(),
+                          ws.numel(), self.stream()), "q4_0 linear")
 
     def sweep_step(self):
         for m in SWEEP_M:
@@ -461,13 +472,16 @@ class Bench:
         w = self.encode_q4_0(n, k, seed=55)  # 295.5 MB > 2 x L2: no rotation needed
         out = {}
         fn = self.lib.mote_cuda_quantized_linear_q4_0_f16
+        fn_ws = self.lib.mote_cuda_quantized_linear_q4_0_f16_ws
+        ws = torch.zeros(max(self.workspace_bytes(16, n, k), 256), dtype=torch.uint8,
+                         device=self.dev)
         for m in (1, 16, 64):
             x = self.randn((m, k), 60 + m, torch.float16)
             y = torch.empty((m, n), dtype=torch.float16, device=self.dev)
 
             def run(x=x, y=y, m=m):
-                self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, self.stream()),
-                           "lm_head")
+                self.check(fn_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, ws.data_ptr(),
+                                 ws.numel(), self.stream()), "lm_head")
 
             g = self.graph(run)
             ms = self.time_graph(g, 20, 1)
@@ -640,7 +654,8 @@ class Bench:
                         "N(0,1) f16 activations)",
                 "config": {
                     "workload": "config3 batch-decode sweep: Q4_0 linear M in {1,2,4,8,16} x "
-                                "N in {4096,11008,14336}, K=4096, f16 act, f32 acc, f16 out",
+                                "N in {4096,11008,14336}, K=4096, f16 act, f32 acc, f16 out "
+                                "(mote_cuda_quantized_linear_q4_0_f16_ws, one workspace)",
                     "weight_copies_per_n": {str(n): len(self.sweep_w[n]) for n in SWEEP_N},
                     "l2": "inputs larger than L2: each case rotates over copies holding "
                           ">= 2.5x L2 (126 MB)",

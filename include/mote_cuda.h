@@ -116,6 +116,25 @@ int mote_cuda_quantized_linear_q4_0_f32(const void* input, const void* weights, 
                                         uint64_t rows, uint64_t output_features,
                                         uint64_t input_features, void* stream);
 
+/* The f16 linear with a caller workspace (256-byte aligned, zeroed once
+ * before first use; its first 256 KiB hold per-tile counters that every call
+ * leaves zero, the partial sums come after).  When a launch stages more
+ * than 8 activation rows that leave room for only one CTA per SM (9 or more
+ * tokens at K = 4096) and N has at most 4096 row tiles, K is split over 2 or
+ * 4 CTAs whose partial sums
+ * meet in the workspace (added in a fixed order: results do not depend on
+ * timing).  A null or too small workspace gives the unsplit kernel.  Calls
+ * sharing a workspace must not overlap.  No reference counterpart; argument
+ * rules as mote_cuda_quantized_linear_q4_0_f16, plus an unaligned workspace
+ * -> 1. */
+int mote_cuda_quantized_linear_q4_0_f16_ws(const void* input, const void* weights, void* output,
+                                           uint64_t rows, uint64_t output_features,
+                                           uint64_t input_features, void* workspace,
+                                           uint64_t workspace_bytes, void* stream);
+/* Workspace bytes that allow the widest split for these sizes (0: none). */
+int mote_cuda_q4_0_linear_workspace_bytes(uint64_t rows, uint64_t output_features,
+                                          uint64_t input_features, uint64_t* bytes);
+
 /* Fused FFN gate/up projection with SwiGLU epilogue:
  * output[rows, F] (f16) = silu(input * gate^T) * (input * up^T), with gate and
  * up both Q4_0 [F, K].  No reference counterpart (SwiGLU is named only in

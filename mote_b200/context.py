@@ -204,6 +204,19 @@ class CudaContext:
         errors.check(lib().mote_cuda_memcpy_host_to_device(tensor.pointer, buf.ctypes.data,
                                                            buf.nbytes), "upload")
 
+    def linear_workspace(self, nbytes: int) -> tuple[int, int]:
+        """A zeroed device workspace of at least ``nbytes`` owned by this
+        context (for the split-K linear), grown on demand.  The kernels leave
+        it zeroed; growing synchronizes the stream, so the first call of a
+        new, larger shape must come before any CUDA-graph capture."""
+        ws = getattr(self, "_workspace", None)
+        if ws is None or ws.size_bytes < nbytes:
+            self.sync()
+            size = max(int(nbytes), 1 << 20)
+            ws = CudaStorage(self.inner, size, np.zeros(size, np.uint8))
+            self._workspace = ws
+        return ws.pointer, ws.size_bytes
+
     def read_bytes(self, tensor: Tensor) -> bytes:
         storage = self.storage(tensor)
         return storage.read_bytes()[: tensor.desc.required_span_bytes]

@@ -131,6 +131,14 @@ struct Params {
     std::uint32_t rope_rows;
     std::uint32_t rope_tiles;
     std::uint32_t head_dim;
+    // K split across CTAs: CTA b works on part b % parts of K (its own
+    // units and activation columns); the parts of a tile meet in the
+    // workspace -- partial sums part_buf[part][tile][NT*128] and arrival
+    // counters part_cnt[tile] (zero between calls: the last part to arrive
+    // adds the partials in part order, stores and resets its counter)
+    std::uint32_t parts;
+    float* part_buf;
+    unsigned* part_cnt;
 };
 
 __host__ __device__ constexpr int red_bytes(int nt) { return 2 * kWarps * nt * 4 * 32 * 4; }
@@ -401,15 +409,23 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
     // a group walks its own tiles (first, first + stride, ...; groups are
     // interleaved across CTAs so small problems spread over every SM) and
     // warp wig of the group owns units [u0, u1) of every one of them.
+    // Parts: CTA b takes part b % parts of K (units [pu0, pu1)); the grid
+    // is a multiple of parts.
+    const std::uint32_t parts = p.parts;
+    const std::uint32_t part = blockIdx.x % parts;
+    const std::uint32_t cta_in_part = blockIdx.x / parts;
+    const std::uint32_t ctas_per_part = gridDim.x / parts;
+    const std::uint32_t pu0 = (p.units * part) / parts;
+    const std::uint32_t pun = (p.units * (part + 1)) / parts - pu0;
     const std::uint32_t sh = p.split_shift;
     const std::uint32_t split = 1u << sh;
     const std::uint32_t grp = static_cast<std::uint32_t>(warp) >> sh;
     const std::uint32_t wig = static_cast<std::uint32_t>(warp) & (split - 1);
-    const std::uint32_t first = blockIdx.x + grp * gridDim.x;
-    const std::uint32_t stride = gridDim.x * (kWarps >> sh);
+    const std::uint32_t first = cta_in_part + grp * ctas_per_part;
+    const std::uint32_t stride = ctas_per_part * (kWarps >> sh);
     const std::uint32_t my_tiles = p.tiles > first ? (p.tiles - first + stride - 1) / stride : 0;
-    const std::uint32_t u0 = (p.units * wig) >> sh;
-    const std::uint32_t u1 = (p.units * (wig + 1)) >> sh;
+    const std::uint32_t u0 = pu0 + ((pun * wig) >> sh);
+    const std::uint32_t u1 = pu0 + ((pun * (wig + 1)) >> sh);
     const std::uint32_t spt = u1 - u0;  // stages (units) per tile
     const std::uint32_t total = my_tiles * spt;
     const std::uint64_t policy = l2_evict_first_policy();
@@ -476,7 +492,9 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
     // f16(x[m] - f16(x[m])) -- with elements 1 and 2 of every group of 4
     // swapped to match decode_word's pairing.
     {
-        const std::uint32_t groups = static_cast<std::uint32_t>(p.K / 4);
+        // only this part's columns: elements [256 * pu0, 256 * (pu0 + pun))
+        const std::uint64_t kx0 = static_cast<std::uint64_t>(pu0) * 256;
+        const std::uint32_t groups = pun * 64;
         const std::uint32_t total_groups = p.M * groups;
 
         for (std::uint32_t i = threadIdx.x; i < total_groups; i += kThreads) {
@@ -484,14 +502,14 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
             const std::uint32_t gi = i - m * groups;
             if constexpr (!XF32) {
                 const uint2 v = __ldg(reinterpret_cast<const uint2*>(
-                    static_cast<const __half*>(p.x) + m * p.K + 4 * gi));
+                    static_cast<const __half*>(p.x) + m * p.K + kx0 + 4 * gi));
                 uint2 o;
                 o.x = prmt(v.x, v.y, 0x5410u);  // (x0, x2)
                 o.y = prmt(v.x, v.y, 0x7632u);  // (x1, x3)
                 *reinterpret_cast<uint2*>(xs + m * p.x_stride + 8 * gi) = o;
             } else {
                 const float4 v = __ldg(reinterpret_cast<const float4*>(
-                    static_cast<const float*>(p.x) + m * p.K + 4 * gi));
+                    static_cast<const float*>(p.x) + m * p.K + kx0 + 4 * gi));
                 const float h0 = __half2float(__float2half_rn(v.x));
                 const float h1 = __half2float(__float2half_rn(v.y));
                 const float h2 = __half2float(__float2half_rn(v.z));
@@ -619,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
                 const std::uint32_t ra = ring_addr + slot * kStageBytes;
                 const std::uint32_t qa = ra + 4 * t;
                 constexpr std::uint32_t kR8 = 8 * kRowStride;
-                const std::uint32_t xo = (u0 + st) * (kUnitBlocks * 64);
+                const std::uint32_t xo = (u0 - pu0 + st) * (kUnitBlocks * 64);
                 std::uint32_t xs_j[NT][BC];  // this lane's B rows for this unit
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
@@ -705,8 +723,43 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
             }
         }
         const std::uint32_t tile = first + tl * stride;
-        if (split == 1) {  // the warp covered all of K
-            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, acc, stage);
+        // The part's sums for a tile (warp-uniform call): stored directly
+        // with one part; otherwise parked in the workspace, and the last
+        // part to arrive adds all parts in part order and stores.
+        auto finish = [&](const float (&v)[NT][4]) {
+            if (parts == 1) {
+                store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, v, stage);
+                return;
+            }
+            float* slot = p.part_buf + (static_cast<std::uint64_t>(part) * p.tiles + tile) * (NT * 128);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) slot[(nt * 4 + i) * 32 + lane] = v[nt][i];
+            __threadfence();
+            __syncwarp();
+            unsigned before = 0;
+            if (lane == 0) before = atomicAdd(&p.part_cnt[tile], 1u);
+            before = __shfl_sync(0xffffffffu, before, 0);
+            if (before != parts - 1) return;
+            __threadfence();
+            float total[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) total[nt][i] = 0.f;
+            for (std::uint32_t q = 0; q < parts; ++q) {
+                const float* src = p.part_buf + (static_cast<std::uint64_t>(q) * p.tiles + tile) * (NT * 128);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) total[nt][i] += __ldcg(src + (nt * 4 + i) * 32 + lane);
+            }
+            if (lane == 0) p.part_cnt[tile] = 0u;  // ready for the next call
+            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, total, stage);
+        };
+        if (split == 1) {  // the warp covered all of its part of K
+            finish(acc);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
             continue;
@@ -737,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
                         sum[nt][i] += base[w * (NT * 4 * 32) + (nt * 4 + i) * 32 + lane];
-            store_tile<NT, XF32, OF32, EPI>(p, tile, g, t, sum, stage);
+            finish(sum);
         }
     }
     if constexpr (EPI == kEpiPeers) peer_handshake(p);
@@ -853,8 +906,9 @@ int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
     const int st = ensure_smem_attribute(kernel, kMaxSmem, configured);
     if (st != kSuccess) return st;
     const std::uint32_t groups = kWarps >> p.split_shift;
-    std::uint32_t grid = min((p.tiles + groups - 1) / groups,
-                             static_cast<std::uint32_t>(sm_count() * ctas_per_sm));
+    // CTAs per part of K; the grid holds the same number for every part
+    const std::uint32_t cap = max(1u, static_cast<std::uint32_t>(sm_count() * ctas_per_sm) / p.parts);
+    std::uint32_t grid = min((p.tiles + groups - 1) / groups, cap) * p.parts;
     if (EPI == kEpiPeers && grid == 0) grid = 1;  // every rank joins the handshake
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -936,6 +990,18 @@ inline std::uint32_t choose_split_shift(std::uint32_t tiles, std::uint32_t units
 
 // Runs the linear for M rows of x, in as few persistent launches as the
 // activation staging allows (consecutive launches on the same stream).
+// Workspace of a K split over `parts` CTAs.  The first kCounterBytes hold
+// one arrival counter per tile (tile t at word t, for up to kCounterTiles
+// tiles) at a fixed place: the counters must be zero before the first call,
+// every call leaves them zero, and no call ever writes partial sums there,
+// whatever the shapes of earlier calls.  The partial sums [parts][tiles]
+// [nt * 128] floats follow.
+constexpr std::uint64_t kCounterTiles = 65536;
+constexpr std::uint64_t kCounterBytes = kCounterTiles * 4;
+inline std::uint64_t part_workspace_bytes(std::uint64_t parts, std::uint64_t tiles, int nt) {
+    return kCounterBytes + parts * tiles * nt * 128 * 4;
+}
+
 // kEpiPeers destinations and handshake flags (see peer_handshake).
 struct PeerArgs {
     __half* const* outputs;
@@ -955,13 +1021,22 @@ struct PeerArgs {
     std::uint32_t rope_rows;
     std::uint32_t rope_tiles;
     std::uint32_t head_dim;
+    // K split across CTAs: CTA b works on part b % parts of K (its own
+    // units and activation columns); the parts of a tile meet in the
+    // workspace -- partial sums part_buf[part][tile][NT*128] and arrival
+    // counters part_cnt[tile] (zero between calls: the last part to arrive
+    // adds the partials in part order, stores and resets its counter)
+    std::uint32_t parts;
+    float* part_buf;
+    unsigned* part_cnt;
 };
 
 template <bool XF32, bool OF32, int EPI>
 int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint64_t M,
                std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream,
                const void* res = nullptr, const PeerArgs* peers = nullptr,
-               const Params* fused = nullptr) {
+               const Params* fused = nullptr, void* workspace = nullptr,
+               std::uint64_t workspace_bytes = 0) {
     const std::size_t osz = OF32 ? 4 : 2;
     // epilogues that exist only on the fast path
     constexpr bool kFastOnly = EPI == kEpiPeers || epi_norm(EPI);
@@ -1033,9 +1108,39 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         fast = plan_gemv(M, K, XF32, EPI == kEpiPeers, tokens, nt, stages, ctas, p.x_rows,
                          p.x_stride, p.x_bytes);
     if (kFastOnly && !fast) return kInvalidValue;
+    p.parts = 1;
+    // With a workspace, when the staged activations leave room for only one
+    // CTA per SM, split K over 2 or 4 CTAs: each stages its part's columns
+    // only, two CTAs fit per SM, and the parts meet in the workspace.
+    if constexpr (!kFastOnly) {
+        // Measured on the decode sweep: worth it with two n8 tiles of tokens
+        // (more than 8 staged rows) and up to a few thousand tiles; with
+        // fewer rows or lm_head-sized N the unsplit kernel is as fast.
+        if (fast && workspace != nullptr && ctas == 1 && nt == 2 && p.tiles <= 4096) {
+            for (std::uint32_t parts = 2; parts <= 4; parts *= 2) {
+                if (p.units < parts) break;
+                const std::uint64_t kp = ((p.units + parts - 1) / parts) * 256ull;
+                std::uint32_t tk = 0, xr = 0, xst = 0, xb = 0;
+                int nt2 = 1, st2 = 2, c2 = 1;
+                if (!plan_gemv(M, kp, XF32, false, tk, nt2, st2, c2, xr, xst, xb)) continue;
+                if (c2 < 2 || tk < tokens) continue;
+                if (part_workspace_bytes(parts, p.tiles, nt2) > workspace_bytes) continue;
+                p.parts = parts;
+                stages = st2;
+                ctas = c2;
+                p.x_stride = xst;
+                p.x_bytes = xb;
+                p.part_cnt = static_cast<unsigned*>(workspace);
+                p.part_buf = reinterpret_cast<float*>(static_cast<std::uint8_t*>(workspace) +
+                                                      kCounterBytes);
+                break;
+            }
+        }
+    }
     if (fast)
-        p.split_shift =
-            choose_split_shift(p.tiles, p.units, static_cast<std::uint32_t>(sm_count() * ctas));
+        p.split_shift = choose_split_shift(
+            p.tiles, (p.units + p.parts - 1) / p.parts,
+            max(1u, static_cast<std::uint32_t>(sm_count() * ctas) / p.parts));
     const std::uint64_t chunk = fast ? tokens : kGenericTokens * 65535ull;
     for (std::uint64_t m0 = 0; m0 < M; m0 += chunk) {
         const std::uint64_t mc = (M - m0 < chunk) ? (M - m0) : chunk;
@@ -1294,4 +1399,48 @@ extern "C" int mote_cuda_q4_0_rms_norm_qkv_rope_f16(
                                                   input_features, n,
                                                   static_cast<cudaStream_t>(stream), nullptr,
                                                   nullptr, &f);
+}
+
+// The f16 linear with a caller workspace (zeroed once before its first use;
+// every call leaves its first 256 KiB -- the tile counters -- zero again).
+// When a launch stages more than 8 activation rows and they would leave
+// room for only one CTA per SM (9 or more tokens at K = 4096), and N has at
+// most 4096 row tiles, K is split over 2 or 4 CTAs through the workspace; with a null or
+// too small workspace the call behaves as mote_cuda_quantized_linear_q4_0_f16.
+// Calls sharing a workspace must not overlap (one stream per workspace).
+// No reference counterpart.
+extern "C" int mote_cuda_quantized_linear_q4_0_f16_ws(const void* input, const void* weights,
+                                                      void* output, std::uint64_t rows,
+                                                      std::uint64_t output_features,
+                                                      std::uint64_t input_features,
+                                                      void* workspace,
+                                                      std::uint64_t workspace_bytes,
+                                                      void* stream) {
+    using namespace mote::q4;
+    const int c = check_linear_args(input, weights, output, rows, output_features,
+                                    input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    if (workspace != nullptr && reinterpret_cast<std::uintptr_t>(workspace) % 256 != 0)
+        return mote::kInvalidValue;
+    return run_linear<false, false, kEpiPlain>(input, weights, nullptr, output, rows,
+                                               output_features, input_features, output_features,
+                                               static_cast<cudaStream_t>(stream), nullptr,
+                                               nullptr, nullptr, workspace, workspace_bytes);
+}
+
+// Workspace size that lets mote_cuda_quantized_linear_q4_0_f16_ws use its
+// widest K split for these sizes (an upper bound; 0 if no split applies).
+extern "C" int mote_cuda_q4_0_linear_workspace_bytes(std::uint64_t rows,
+                                                     std::uint64_t output_features,
+                                                     std::uint64_t input_features,
+                                                     std::uint64_t* bytes) {
+    using namespace mote::q4;
+    if (bytes == nullptr) return mote::kInvalidValue;
+    *bytes = 0;
+    if (rows == 0 || output_features == 0 || input_features % 256 != 0 || input_features == 0)
+        return mote::kSuccess;
+    const std::uint64_t tiles = (output_features + 15) / 16;
+    if (tiles <= kCounterTiles) *bytes = part_workspace_bytes(4, tiles, 2);
+    return mote::kSuccess;
 }

@@ -110,6 +110,16 @@ def quantized_linear_q4_0(context: CudaContext, input: Tensor, weights: Tensor, 
     if rows * n == 0:
         return
     context.inner.select()
+    if (input_dtype, output_dtype) == (DType.F16, DType.F16):
+        # the split-K path, with the context's workspace
+        need = ctypes.c_uint64(0)
+        errors.check(lib().mote_cuda_q4_0_linear_workspace_bytes(rows, n, k, ctypes.byref(need)),
+                     "query linear workspace")
+        ws_ptr, ws_bytes = context.linear_workspace(need.value) if need.value else (None, 0)
+        errors.check(lib().mote_cuda_quantized_linear_q4_0_f16_ws(
+            in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k, ws_ptr, ws_bytes,
+            context.stream), "launch Q4_0 linear kernel")
+        return
     errors.check(getattr(lib(), symbol)(in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k,
                                         context.stream), "launch Q4_0 linear kernel")
 

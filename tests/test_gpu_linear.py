@@ -275,3 +275,40 @@ def test_residual_zero_input_features_copies_residual(ctx):
     yt = ctx.from_bytes(plain((3, 2), DType.F16), np.full(6, 7.0, np.float16))
     ops.quantized_linear_q4_0_f16_residual(ctx, xt, wt, rt, yt)
     assert np.array_equal(np.frombuffer(ctx.read_bytes(yt), np.float16), r)
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 4096, 4096), (8, 1000, 4096), (9, 4096, 4096),
+                                   (16, 14336, 4096), (16, 300, 8192), (12, 528, 14336),
+                                   (16, 64, 1024)])
+def test_split_k_workspace_path(ctx, oracle_lib, m, n, k):
+    """mote_cuda_quantized_linear_q4_0_f16_ws: K split over CTAs through the
+    workspace.  Two calls in a row (into NaN-filled outputs) give identical,
+    complete outputs -- the second only works if the first reset every tile
+    counter -- and a too-small workspace falls back to the unsplit kernel."""
+    import ctypes
+
+    from mote_b200._native import lib
+
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=500 + n)
+    x = fx.activations(m, k, seed=501 + m).astype(np.float16)
+    xt = ctx.from_bytes(plain((m, k), DType.F16), x)
+    wt = ctx.from_bytes(quantized((n, k)), w)
+    need = ctypes.c_uint64(0)
+    assert lib().mote_cuda_q4_0_linear_workspace_bytes(m, n, k, ctypes.byref(need)) == 0
+    assert need.value > 0
+    ws = ctx.from_bytes(plain((need.value,), DType.U8), np.zeros(need.value, np.uint8))
+    outs = []
+    nan = np.full(m * n, np.nan, np.float16)  # any tile left unstored stays NaN
+    for ws_bytes in (need.value, need.value, 16):
+        yt = ctx.from_bytes(plain((m, n), DType.F16), nan)
+        assert lib().mote_cuda_quantized_linear_q4_0_f16_ws(
+            xt.pointer, wt.pointer, yt.pointer, m, n, k, ws.pointer, ws_bytes, ctx.stream) == 0
+        outs.append(np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(m, n))
+    assert ctx.device_status() == 0
+    assert np.array_equal(outs[0], outs[1]) and not np.isnan(outs[1]).any()
+    want = oracle_linear(oracle_lib, x.astype(np.float32), w, m, n, k)
+    ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w, n, k))
+    for got in (outs[0], outs[2]):
+        ok, bad = checker.within_reference_tolerance(got, checker.f16_round(want), 0.01, 0.002)
+        assert ok, bad
+        assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND

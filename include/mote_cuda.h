@@ -131,6 +131,20 @@ int mote_cuda_quantized_linear_q4_0_f16_ws(const void* input, const void* weight
                                            uint64_t rows, uint64_t output_features,
                                            uint64_t input_features, void* workspace,
                                            uint64_t workspace_bytes, void* stream);
+/* mote_cuda_quantized_linear_q4_0_f16_ws without a workspace argument, for
+ * callers that cannot allocate or pass one (a kernel reached through
+ * mote-kernel's KernelImpl::launch gets only its opaque argument words).  No
+ * reference counterpart.  The split-K scratch is a static 8 MiB device
+ * array per device, zero at load and left zero by every call; no memory is
+ * allocated.  A request whose split needs more scratch returns 10200 before
+ * anything is enqueued.  Calls on the same device must not overlap (one
+ * scratch per device, shared by all streams).  The first call on a device
+ * looks up the scratch address and must be made before any stream capture
+ * that includes this entry point. */
+int mote_cuda_quantized_linear_q4_0_f16_noalloc(const void* input, const void* weights,
+                                                void* output, uint64_t rows,
+                                                uint64_t output_features, uint64_t input_features,
+                                                void* stream);
 /* Workspace bytes that allow the widest split for these sizes (0: none). */
 int mote_cuda_q4_0_linear_workspace_bytes(uint64_t rows, uint64_t output_features,
                                           uint64_t input_features, uint64_t* bytes);

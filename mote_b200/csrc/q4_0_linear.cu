@@ -1002,6 +1002,10 @@ inline std::uint64_t part_workspace_bytes(std::uint64_t parts, std::uint64_t til
     return kCounterBytes + parts * tiles * nt * 128 * 4;
 }
 
+// Status of mote_cuda_quantized_linear_q4_0_f16_noalloc when the request's
+// K split needs more than its static scratch (above every CUDA runtime code).
+constexpr int kScratchTooSmall = 10200;
+
 // kEpiPeers destinations and handshake flags (see peer_handshake).
 struct PeerArgs {
     __half* const* outputs;
@@ -1036,7 +1040,7 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
                std::uint64_t N, std::uint64_t K, std::uint64_t ldy, cudaStream_t stream,
                const void* res = nullptr, const PeerArgs* peers = nullptr,
                const Params* fused = nullptr, void* workspace = nullptr,
-               std::uint64_t workspace_bytes = 0) {
+               std::uint64_t workspace_bytes = 0, bool workspace_must_fit = false) {
     const std::size_t osz = OF32 ? 4 : 2;
     // epilogues that exist only on the fast path
     constexpr bool kFastOnly = EPI == kEpiPeers || epi_norm(EPI);
@@ -1124,7 +1128,11 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
                 int nt2 = 1, st2 = 2, c2 = 1;
                 if (!plan_gemv(M, kp, XF32, false, tk, nt2, st2, c2, xr, xst, xb)) continue;
                 if (c2 < 2 || tk < tokens) continue;
-                if (part_workspace_bytes(parts, p.tiles, nt2) > workspace_bytes) continue;
+                if (part_workspace_bytes(parts, p.tiles, nt2) > workspace_bytes) {
+                    // a fixed-size workspace that cannot hold the split
+                    if (workspace_must_fit) return kScratchTooSmall;
+                    continue;
+                }
                 p.parts = parts;
                 stages = st2;
                 ctas = c2;
@@ -1443,4 +1451,63 @@ extern "C" int mote_cuda_q4_0_linear_workspace_bytes(std::uint64_t rows,
     const std::uint64_t tiles = (output_features + 15) / 16;
     if (tiles <= kCounterTiles) *bytes = part_workspace_bytes(4, tiles, 2);
     return mote::kSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of mote_cuda_quantized_linear_q4_0_f16_ws.
+//
+// For callers that cannot allocate or pass a workspace -- e.g. a kernel
+// resolved through mote-kernel's KernelImpl::launch, which receives only the
+// opaque argument words -- the split-K scratch is a file-scope device array,
+// one per device, zero at module load (its tile counters must be zero before
+// a call, and every call leaves them zero).  Its address is looked up once
+// per device with cudaGetSymbolAddress; no memory is allocated.  Limits:
+// kNoAllocScratchBytes of scratch per device -- a request whose K split
+// needs more returns kScratchTooSmall (10200) before anything is enqueued --
+// and one scratch per device, so calls on that device must not overlap (on
+// any stream).  The first call on a device performs the lookup and must be
+// made before any stream capture that includes this entry point.  No
+// reference counterpart.
+// ---------------------------------------------------------------------------
+namespace mote {
+namespace q4 {
+constexpr std::uint64_t kNoAllocScratchBytes = 8ull << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Address of this device's scratch (cached per device ordinal).
+inline int noalloc_scratch(void** out) {
+    static std::atomic<void*> cache[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    void* p = cache[dev & 63].load(std::memory_order_acquire);
+    if (p == nullptr) {
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        cache[dev & 63].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return kSuccess;
+}
+}  // namespace q4
+}  // namespace mote
+
+extern "C" int mote_cuda_quantized_linear_q4_0_f16_noalloc(const void* input, const void* weights,
+                                                           void* output, std::uint64_t rows,
+                                                           std::uint64_t output_features,
+                                                           std::uint64_t input_features,
+                                                           void* stream) {
+    using namespace mote::q4;
+    const int c = check_linear_args(input, weights, output, rows, output_features,
+                                    input_features, stream);
+    if (c == kEmpty) return mote::kSuccess;
+    if (c != 0) return c;
+    void* scratch = nullptr;
+    const int st = noalloc_scratch(&scratch);
+    if (st != mote::kSuccess) return st;
+    return run_linear<false, false, kEpiPlain>(input, weights, nullptr, output, rows,
+                                               output_features, input_features, output_features,
+                                               static_cast<cudaStream_t>(stream), nullptr,
+                                               nullptr, nullptr, scratch, kNoAllocScratchBytes,
+                                               true);
 }

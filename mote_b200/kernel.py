@@ -104,6 +104,7 @@ _ARG_KINDS = {
     "mote_cuda_q4_0_gate_up_swiglu_f16": "ppppuuup",
     "mote_cuda_quantized_linear_q4_0_f16_residual": "ppppuuup",
     "mote_cuda_quantized_linear_q4_0_f16_ws": "pppuuupup",
+    "mote_cuda_quantized_linear_q4_0_f16_noalloc": "pppuuup",
     "mote_cuda_q4_0_rms_norm_linear_f16": "ppppuuufp",
     "mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16": "pppppuuufp",
     "mote_cuda_q4_0_rms_norm_qkv_rope_f16": "ppppppuuuuufp",
@@ -126,6 +127,7 @@ CUDA_KERNELS = {
     ("gate_up_swiglu_q4_0", DType.F16): "mote_cuda_q4_0_gate_up_swiglu_f16",
     ("quantized_linear_q4_0_residual", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_residual",
     ("quantized_linear_q4_0_ws", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_ws",
+    ("quantized_linear_q4_0_noalloc", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_noalloc",
     ("rms_norm_linear_q4_0", DType.F16): "mote_cuda_q4_0_rms_norm_linear_f16",
     ("rms_norm_gate_up_swiglu_q4_0", DType.F16): "mote_cuda_q4_0_rms_norm_gate_up_swiglu_f16",
     ("rms_norm_qkv_rope_q4_0", DType.F16): "mote_cuda_q4_0_rms_norm_qkv_rope_f16",

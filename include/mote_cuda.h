@@ -23,8 +23,9 @@
  * so a kernel may begin while earlier kernels of this library on the stream
  * are still running; each waits for its predecessor to complete before it
  * touches activations or outputs.  The Q4_0 linears start streaming their
- * WEIGHTS before that wait, so a linear's weights must not be written by
- * this library's kernels still in flight on its stream (weights written by
+ * WEIGHTS before that wait (and mote_cuda_rms_norm_rope_f16 reads gamma and
+ * the cos/sin rows before it), so such parameters must not be written by
+ * this library's kernels still in flight on its stream (parameters written by
  * a copy, by mote_cuda_q4_0_encode_f32 or by any kernel not from this
  * library are ordered normally: those end the overlap).
  *

@@ -226,8 +226,12 @@ __global__ void __launch_bounds__(256) rope_kernel(const __half* input,
 // ---- fused RMSNorm + RoPE (one CTA per token) --------------------------------
 // Normalizes x[token] (hidden) and rotates q[token] (q_heads x HD) and
 // k[token] (kv_heads x HD) with the token's cos/sin row; rotary_dim == HD.
-// Every load of the token (q, k and x rows, 16 bytes per thread per vector)
-// is issued before any arithmetic, so the CTA pays one memory latency.  A
+// gamma and the token's cos/sin row are parameters, not activations: they
+// are copied to shared memory before griddepcontrol.wait, so their latency
+// hides behind the previous kernel's tail (the caller must not have them
+// written by this library's kernels still in flight on the stream).  Every
+// load of the token (q, k and x rows, 16 bytes per thread per vector) is
+// issued right after the wait, so the CTA pays one memory latency.  A
 // thread owns 8 consecutive elements of a head; for the half-split layout
 // the partner of element e < HD/2 is e + HD/2, held by the thread HD/16
 // lanes away (q/k rows are whole heads, so partners never cross rows).
@@ -241,14 +245,30 @@ __global__ void __launch_bounds__(kNormThreads, 4) rms_norm_rope_kernel(
     const float* __restrict__ sin, std::uint64_t hidden, std::uint32_t q_heads,
     std::uint32_t kv_heads, float eps, int layout) {
     pdl_launch_dependents();
-    pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
+    // gamma (hidden f16; a thread copies exactly the vectors it later reads)
+    // and the token's cos | sin row (HD/2 + HD/2 f32, shared by all threads)
+    __shared__ __align__(16) uint4 gamma_s[kNormVecPerThread * kNormThreads];
+    __shared__ __align__(16) float cs_s[HD];
     constexpr int kLanesPerHead = HD / 8;
     constexpr int kHalfLanes = kLanesPerHead / 2;
     const std::uint64_t token = blockIdx.x;
     const std::uint32_t qn = q_heads * HD / 8;
     const std::uint32_t rn = qn + kv_heads * HD / 8;
     const std::uint32_t xn = static_cast<std::uint32_t>(hidden / 8);
+#pragma unroll
+    for (int i = 0; i < kNormVecPerThread; ++i) {
+        const std::uint32_t v = threadIdx.x + i * kNormThreads;
+        if (v < xn) cp_async_16_default(smem_u32(&gamma_s[v]), reinterpret_cast<const uint4*>(gamma) + v);
+    }
+    if (threadIdx.x < HD / 4) {  // HD/8 16-byte chunks of cos, then HD/8 of sin
+        const std::uint32_t c = threadIdx.x;
+        const float* src = c < HD / 8 ? cos + token * (HD / 2) + c * 4
+                                      : sin + token * (HD / 2) + (c - HD / 8) * 4;
+        cp_async_16_default(smem_u32(&cs_s[c * 4]), src);
+    }
+    cp_async_commit();
+    pdl_wait();
     const uint4* qv = reinterpret_cast<const uint4*>(q + token * q_heads * HD);
     const uint4* kv = reinterpret_cast<const uint4*>(k + token * kv_heads * HD);
     const uint4* xv = reinterpret_cast<const uint4*>(x + token * hidden);
@@ -266,9 +286,11 @@ __global__ void __launch_bounds__(kNormThreads, 4) rms_norm_rope_kernel(
         xr[i].u = v < xn ? xv[v] : make_uint4(0, 0, 0, 0);
     }
 
-    // RoPE of the q and k rows.
-    const float* cs = cos + token * (HD / 2);
-    const float* sn = sin + token * (HD / 2);
+    // RoPE of the q and k rows (the barrier runs while the loads are in flight).
+    cp_async_wait<0>();
+    __syncthreads();
+    const float* cs = cs_s;
+    const float* sn = cs_s + HD / 2;
 #pragma unroll
     for (int i = 0; i < kRopeVecPerThread; ++i) {
         const std::uint32_t v = threadIdx.x + i * kNormThreads;
@@ -332,13 +354,12 @@ __global__ void __launch_bounds__(kNormThreads, 4) rms_norm_rope_kernel(
         }
     const float inv = inv_rms(block_sum(ssq, scratch), hidden, eps);
     uint4* out = reinterpret_cast<uint4*>(x_out + token * hidden);
-    const uint4* wv = reinterpret_cast<const uint4*>(gamma);
 #pragma unroll
     for (int i = 0; i < kNormVecPerThread; ++i) {
         const std::uint32_t v = threadIdx.x + i * kNormThreads;
         if (v < xn) {
             H8 w, o;
-            w.u = __ldg(&wv[v]);
+            w.u = gamma_s[v];
 #pragma unroll
             for (int j = 0; j < 8; ++j)
                 o.h[j] = __float2half_rn(norm_out(__half2float(xr[i].h[j]), inv,

@@ -124,6 +124,12 @@ __device__ __forceinline__ void cp_async_16(std::uint32_t dst_smem, const void* 
                  : "memory");
 }
 
+// Same copy with the default L2 policy (small tables many CTAs re-read).
+__device__ __forceinline__ void cp_async_16_default(std::uint32_t dst_smem, const void* src_gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src_gmem)
+                 : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }

@@ -975,15 +975,20 @@ inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, bool peers, s
     return false;
 }
 
-// log2 of the warps per tile (split-K factor).  Measured on the decode
-// shapes (K = 2048..8192, 128..8016 tiles, 8 or 16 warps per SM), the best
-// split tracks 1.2 x (warps / tiles): about one round of tile groups with
-// every warp busy.  Small problems spread each tile over 8 warps; lm_head
-// sized ones give each warp whole tiles (no barrier, no partial sums).
+// log2 of the warps per tile (split-K factor).  Measured with every split
+// forced (K = 2048..8192, 128..8016 tiles, 8 or 16 warps per SM), the best
+// split follows r = 1.2 x (warps / tiles).  With the whole K in one CTA:
+// 8 warps per tile for r >= 5.66 (small problems spread every tile over a
+// CTA), 4 for r >= 2, else 2 -- whole tiles per warp were never the
+// fastest: at lm_head size (r = 0.18..0.35) pairs of warps beat them by
+// 3.5-4.6 %, the rounds of tiles per group divide more evenly.  With K
+// split over `parts` CTAs (a quarter of K each, two n8 token tiles) every
+// extra split costs more: 2 warps from r >= 1.41, 4 from 2.83, 8 from 5.66.
 inline std::uint32_t choose_split_shift(std::uint32_t tiles, std::uint32_t units,
-                                        std::uint32_t ctas) {
+                                        std::uint32_t ctas, std::uint32_t parts) {
     const double r = 1.2 * kWarps * static_cast<double>(ctas) / static_cast<double>(tiles);
-    std::uint32_t sh = (r >= 1.4142) + (r >= 2.8284) + (r >= 5.6569);
+    std::uint32_t sh = parts > 1 ? (r >= 1.4142) + (r >= 2.8284) + (r >= 5.6569)
+                                 : 1 + (r >= 2.0) + (r >= 5.6569);
     while (sh > 0 && (1u << sh) > units) --sh;
     return sh;
 }
@@ -1148,7 +1153,7 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     if (fast)
         p.split_shift = choose_split_shift(
             p.tiles, (p.units + p.parts - 1) / p.parts,
-            max(1u, static_cast<std::uint32_t>(sm_count() * ctas) / p.parts));
+            max(1u, static_cast<std::uint32_t>(sm_count() * ctas) / p.parts), p.parts);
     const std::uint64_t chunk = fast ? tokens : kGenericTokens * 65535ull;
     for (std::uint64_t m0 = 0; m0 < M; m0 += chunk) {
         const std::uint64_t mc = (M - m0 < chunk) ? (M - m0) : chunk;

@@ -74,9 +74,8 @@ def test_fast_path_matches_oracle(ctx, oracle_lib, m, n, k):
     _check_fast_path(ctx, oracle_lib, m, n, k)
 
 
-# Register-resident K-slices hold one unit (256 k) per warp for 16 tokens or
-# two for 8; longer K falls back to the staged kernel.  These shapes cover
-# both kernels and every warp split (K/256 = 9, 24, 32, 33, 56 units).
+# Odd and long K (K/256 = 9, 24, 32, 33, 56 units of 256) with few tiles:
+# every warp split (2, 4 or 8 warps per tile) divides K unevenly somewhere.
 @pytest.mark.parametrize("m,n,k", [(1, 1000, 2304), (8, 304, 6144), (9, 304, 6144),
                                    (1, 520, 8192), (16, 520, 8192), (2, 64, 8448),
                                    (1, 528, 14336), (12, 528, 14336)])

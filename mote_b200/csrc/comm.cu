@@ -78,8 +78,11 @@ struct GatherArgs {
     std::uint32_t nranks;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// A strong relaxed store: after a system-scope fence by the same thread it
+// completes a release pattern, and the stores to several ranks' flags can
+// be in flight together (a st.release per flag would fence before each).
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -108,8 +111,8 @@ __global__ void __launch_bounds__(256) all_gather_p2p_kernel(const GatherArgs a)
     a.own_flags[a.nranks] = 0u;  // counter ready for the next call
     const unsigned epoch = a.own_flags[a.nranks + 1] + 1u;
     a.own_flags[a.nranks + 1] = epoch;
-    __threadfence_system();
-    for (std::uint32_t p = 0; p < a.nranks; ++p) st_release_sys(a.flags[p] + a.rank, epoch);
+    __threadfence_system();  // with the relaxed flag stores below: one release pattern
+    for (std::uint32_t p = 0; p < a.nranks; ++p) st_relaxed_sys(a.flags[p] + a.rank, epoch);
     // Wait (bounded) for every rank's slice of this epoch.  A peer that has
     // already moved on to a later epoch also delivered this one.
     const long long start = clock64();

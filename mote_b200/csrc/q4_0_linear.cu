@@ -367,9 +367,12 @@ __device__ __forceinline__ void peer_handshake(const Params& p) {
     p.own_flags[p.nranks] = 0u;
     const unsigned epoch = p.own_flags[p.nranks + 1] + 1u;
     p.own_flags[p.nranks + 1] = epoch;
+    // One system fence, then strong relaxed flag stores (a release pattern):
+    // the stores to all ranks are in flight together instead of each
+    // st.release fencing behind the previous one.
     __threadfence_system();
     for (std::uint32_t q = 0; q < p.nranks; ++q)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q] + p.rank),
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q] + p.rank),
                      "r"(epoch)
                      : "memory");
     const long long start = clock64();

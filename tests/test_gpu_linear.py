@@ -276,9 +276,12 @@ def test_residual_zero_input_features_copies_residual(ctx):
     assert np.array_equal(np.frombuffer(ctx.read_bytes(yt), np.float16), r)
 
 
+# K split over CTAs (9-16 tokens, up to 4096 tiles); the other shapes take
+# the unsplit kernel with the workspace present (1-16 tokens, 3-896 tiles).
 @pytest.mark.parametrize("m,n,k", [(5, 4096, 4096), (8, 1000, 4096), (9, 4096, 4096),
                                    (16, 14336, 4096), (16, 300, 8192), (12, 528, 14336),
-                                   (16, 64, 1024)])
+                                   (16, 64, 1024), (1, 40, 2304), (1, 4016, 4096),
+                                   (3, 11008, 4096), (1, 14336, 4096), (4, 2000, 12288)])
 def test_split_k_workspace_path(ctx, oracle_lib, m, n, k):
     """mote_cuda_quantized_linear_q4_0_f16_ws: K split over CTAs through the
     workspace.  Two calls in a row (into NaN-filled outputs) give identical,

@@ -270,9 +270,9 @@ class Bench:
 
     # -- public-API end-to-end leg ------------------------------------------------
     def e2e(self, steps: int) -> dict:
-        """Config-3 sweep through mote_b200.ops with host buffers: each case
-        copies its activations from pinned host memory, runs the op and copies
-        the output back, every step."""
+        """Config-3 sweep through mote_b200.ops with host buffers: every step
+        copies the five activation matrices from pinned host memory, runs the
+        15 linears and copies the 15 outputs back, then synchronizes."""
         import numpy as np
 
         from mote_b200 import ops
@@ -281,11 +281,15 @@ class Bench:
 
         ctx = CudaContext(self.local_rank)
         k = SWEEP_K
+        # each step takes the next of R_N copies of every weight matrix (the
+        # copies of one N hold >= 2.5x L2), so every step streams from HBM
         weights = {}
         for n in SWEEP_N:
-            wt = ctx.empty(quantized((n, k)))
-            self.encode_into(wt.pointer, n, k, seed=1000 + n)
-            weights[n] = wt
+            weights[n] = []
+            for _ in range(copies_for(q4_bytes(n, k))):
+                wt = ctx.empty(quantized((n, k)))
+                self.encode_into(wt.pointer, n, k, seed=1000 + n)
+                weights[n].append(wt)
         xs = {m: ctx.empty(plain((m, k), DType.F16)) for m in SWEEP_M}
         ys = {(m, n): ctx.empty(plain((m, n), DType.F16)) for m in SWEEP_M for n in SWEEP_N}
         hx = {m: PinnedBuffer(m * k * 2) for m in SWEEP_M}
@@ -293,31 +297,38 @@ class Bench:
         rng = np.random.default_rng(5)
         for m in SWEEP_M:
             hx[m].view(np.float16)[:] = rng.normal(0, 1, m * k).astype(np.float16)
-        h2d = sum(m * k * 2 for m in SWEEP_M) * len(SWEEP_N)
+        h2d = sum(m * k * 2 for m in SWEEP_M)
         d2h = sum(m * n * 2 for m in SWEEP_M for n in SWEEP_N)
         alg = sum(linear_bytes(m, n, k) for m in SWEEP_M for n in SWEEP_N)
 
-        def step():
+        def step(i):
+            # a step's inputs up, its 15 linears, its outputs down, one sync
+            for m in SWEEP_M:
+                ctx.upload_async(xs[m], hx[m])
             for m in SWEEP_M:
                 for n in SWEEP_N:
-                    ctx.upload_async(xs[m], hx[m])
-                    ops.quantized_linear_q4_0_f16(ctx, xs[m], weights[n], ys[(m, n)])
+                    ops.quantized_linear_q4_0_f16(ctx, xs[m], weights[n][i % len(weights[n])],
+                                                  ys[(m, n)])
+            for m in SWEEP_M:
+                for n in SWEEP_N:
                     ctx.download_async(hy[(m, n)], ys[(m, n)])
             ctx.sync()
 
-        for _ in range(3):
-            step()
+        for i in range(3):
+            step(i)
         t0 = time.perf_counter()
-        for _ in range(steps):
-            step()
+        for i in range(steps):
+            step(i)
         dt = time.perf_counter() - t0
         self.launches += steps * len(SWEEP_M) * len(SWEEP_N)
         dt = self.max_over_ranks(dt)
         return {"value": round(alg * steps * self.world / dt / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(dt * 1e3 / steps, 4),
-                "path": "mote_b200.ops.quantized_linear_q4_0_f16 (C ABI) with pinned-host "
-                        "H2D/D2H per case, stream sync per step"}
+                "path": "mote_b200.ops.quantized_linear_q4_0_f16 (C ABI); per step: the "
+                        "activations H2D from pinned host memory, the 15 linears, the outputs "
+                        "D2H, one stream sync; weights rotated over copies holding >= 2.5x L2 "
+                        "per N"}
 
     # -- extra configs ----------------------------------------------------------
     def config1(self) -> dict:
@@ -512,7 +523,8 @@ class Bench:
         peer-store kernel, and fused into the GEMV epilogue (stores into
         every rank's [M, N] logits over NVLink + flag handshake).  Steps are
         captured in CUDA graphs; times are the max over ranks; GB/s counts
-        the full 295.5 MB weight once per step."""
+        the full 295.5 MB weight once per step.  A shard smaller than 2.5x
+        L2 (G >= 2) is rotated over copies, one per step, like the sweep."""
         torch = self.torch
         import torch.distributed as dist
 
@@ -520,7 +532,8 @@ class Bench:
 
         k, n = 4096, 128256
         sh = comm.shard_rows(n, self.world, self.rank)
-        w = self.encode_q4_0(sh.rows, k, seed=700 + self.rank)
+        w0 = self.encode_q4_0(sh.rows, k, seed=700 + self.rank)
+        ws = [w0] + [w0.clone() for _ in range(copies_for(w0.numel()) - 1)]
         fn = self.lib.mote_cuda_quantized_linear_q4_0_f16
 
         def exchange(obj):
@@ -529,8 +542,8 @@ class Bench:
             return out
 
         nccl = comm.NcclAllGather(self.world, self.rank, exchange)
-        result = {"shard_rows": sh.rows, "world": self.world}
-        reps, steps = 10, 8
+        result = {"shard_rows": sh.rows, "world": self.world, "weight_copies": len(ws)}
+        reps, steps = 10, max(8, len(ws))
         try:
             for m in (1, 16, 64):
                 x = self.randn((m, k), 60 + m, torch.float16)
@@ -541,27 +554,27 @@ class Bench:
                 fused = comm.ShardedLinearQ4_0(self.world, self.rank, m, n, k, exchange) \
                     if m <= 16 else None
 
-                def gemv(x=x, y=y, m=m):
-                    self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, sh.rows, k,
-                                  self.stream()), "lm_head shard")
+                def gemv(i, x=x, y=y, m=m):
+                    self.check(fn(x.data_ptr(), ws[i % len(ws)].data_ptr(), y.data_ptr(), m,
+                                  sh.rows, k, self.stream()), "lm_head shard")
 
                 def run_gemv():
-                    for _ in range(steps):
-                        gemv()
+                    for i in range(steps):
+                        gemv(i)
 
                 def run_nccl(y=y, recv=recv, count=count):
-                    for _ in range(steps):
-                        gemv()
+                    for i in range(steps):
+                        gemv(i)
                         nccl.all_gather(y.data_ptr(), recv.data_ptr(), count, self.stream())
 
                 def run_p2p(y=y, peer=peer):
                     for i in range(steps):
-                        gemv()
+                        gemv(i)
                         peer.all_gather(y.data_ptr(), i % 2, self.stream())
 
                 def run_fused(x=x, fused=fused):
                     for i in range(steps):
-                        fused(x.data_ptr(), w.data_ptr(), i % 2, self.stream())
+                        fused(x.data_ptr(), ws[i % len(ws)].data_ptr(), i % 2, self.stream())
 
                 row = {}
                 # the fused epilogue is the decode path (GEMV, <= 16 tokens a

@@ -204,6 +204,20 @@ class CudaContext:
         errors.check(lib().mote_cuda_memcpy_host_to_device(tensor.pointer, buf.ctypes.data,
                                                            buf.nbytes), "upload")
 
+    def linear_workspace_bytes(self, rows: int, n: int, k: int) -> int:
+        """mote_cuda_q4_0_linear_workspace_bytes for a shape, memoised (it
+        depends only on the shape and this context's device)."""
+        cache = self.__dict__.setdefault("_ws_need", {})
+        key = (rows, n, k)
+        need = cache.get(key)
+        if need is None:
+            out = ctypes.c_uint64(0)
+            errors.check(lib().mote_cuda_q4_0_linear_workspace_bytes(rows, n, k,
+                                                                     ctypes.byref(out)),
+                         "query linear workspace")
+            need = cache[key] = out.value
+        return need
+
     def linear_workspace(self, nbytes: int) -> tuple[int, int]:
         """A zeroed device workspace of at least ``nbytes`` owned by this
         context (for the split-K linear), grown on demand.  The kernels leave
@@ -258,6 +272,10 @@ class CudaContext:
 
     # -- ownership check used by every op (context.rs:150-176) --------------
     def storage(self, tensor: Tensor) -> CudaStorage:
+        st = tensor.storage
+        if (st.__class__ is CudaStorage and st.context is self.inner and tensor.byte_offset == 0
+                and tensor.desc.is_contiguous):
+            return st  # every check below passes (same context implies same device)
         if tensor.device != self.device:
             raise errors.DeviceMismatch(expected=self.device, actual=tensor.device)
         if tensor.byte_offset != 0:

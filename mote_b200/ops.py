@@ -112,10 +112,8 @@ def quantized_linear_q4_0(context: CudaContext, input: Tensor, weights: Tensor, 
     context.inner.select()
     if (input_dtype, output_dtype) == (DType.F16, DType.F16):
         # the split-K path, with the context's workspace
-        need = ctypes.c_uint64(0)
-        errors.check(lib().mote_cuda_q4_0_linear_workspace_bytes(rows, n, k, ctypes.byref(need)),
-                     "query linear workspace")
-        ws_ptr, ws_bytes = context.linear_workspace(need.value) if need.value else (None, 0)
+        need = context.linear_workspace_bytes(rows, n, k)
+        ws_ptr, ws_bytes = context.linear_workspace(need) if need else (None, 0)
         errors.check(lib().mote_cuda_quantized_linear_q4_0_f16_ws(
             in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k, ws_ptr, ws_bytes,
             context.stream), "launch Q4_0 linear kernel")

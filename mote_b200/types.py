@@ -10,6 +10,7 @@ from __future__ import annotations
 import enum
 import math
 from dataclasses import dataclass, field
+from functools import cached_property
 
 
 class DType(enum.Enum):
@@ -95,6 +96,9 @@ class Layout:
 
 @dataclass(frozen=True)
 class TensorDesc:
+    # Immutable, so the derived figures below are computed once per
+    # descriptor (cached in the instance dictionary, outside the fields that
+    # equality and hashing compare).
     shape: tuple[int, ...]
     encoding: Encoding
     layout: Layout = field(default_factory=Layout.contiguous)
@@ -113,15 +117,15 @@ class TensorDesc:
         if self.layout.strides is not None and len(self.layout.strides) != len(self.shape):
             raise TensorDescError("RankMismatch")
 
-    @property
+    @cached_property
     def rank(self) -> int:
         return len(self.shape)
 
-    @property
+    @cached_property
     def numel(self) -> int:
         return math.prod(self.shape)
 
-    @property
+    @cached_property
     def is_contiguous(self) -> bool:
         if self.layout.strides is None or 0 in self.shape:
             return True
@@ -132,7 +136,7 @@ class TensorDesc:
             expected *= dim
         return True
 
-    @property
+    @cached_property
     def required_span_bytes(self) -> int:
         """tensor_desc.rs:59-101: plain = span * size; quantized = rows * blocks * bytes."""
         if self.encoding.quantized is not None:
@@ -149,7 +153,7 @@ class TensorDesc:
             span = 1 + sum((d - 1) * s for d, s in zip(self.shape, self.layout.strides))
         return span * self.encoding.plain.size_bytes
 
-    @property
+    @cached_property
     def required_alignment(self) -> int:
         if self.encoding.quantized is not None:
             return self.encoding.quantized.alignment_bytes

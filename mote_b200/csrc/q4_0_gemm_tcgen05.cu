@@ -8,20 +8,21 @@
 // One CTA computes a tile of 128 features x 256 tokens.  The dequantized
 // weights are the MMA's A operand (M = 128 rows) and the activations its B
 // operand (N = 256), so every weight converted to f16 feeds 256 tokens:
-// * warp 8 (producer) streams activation tiles (64 k x 256 tokens, TMA with
-//   128-byte swizzle) and raw Q4_0 row slices (128 rows x 144 bytes = 8
+// * warp 16 (producer) streams activation tiles (64 k x 256 tokens, TMA
+//   with 128-byte swizzle) and raw Q4_0 row slices (128 rows x 144 bytes = 8
 //   blocks per row, TMA 2-D tile of bytes) into shared memory;
-// * warps 0-7 (converters) dequantize each 64-k slice of the raw rows into
-//   f16 (q - 8) * d -- correctly rounded, exactly what a dense f16 weight
-//   would hold -- written straight into the 128-byte-swizzled K-major
-//   layout the tensor core reads (warps 0-3 the even block of every slice,
-//   warps 4-7 the odd one: no divergence);
-// * warp 9 allocates 256 TMEM columns and one thread issues
+// * warps 0-15 (converters, two groups of 8 taking alternate 64-k slices)
+//   dequantize each slice of the raw rows into f16 (q - 8) * d -- correctly
+//   rounded, exactly what a dense f16 weight would hold -- written straight
+//   into the 128-byte-swizzled K-major layout the tensor core reads (in a
+//   group, warps 0-3 the even block of the slice, warps 4-7 the odd one: no
+//   divergence);
+// * warp 17 allocates the TMEM columns and one thread issues
 //   tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) per 16-k step,
 //   accumulating in f32 in TMEM; tcgen05.commit releases the operand stages;
-// * after the last k-slice the converter warps read the accumulator with
-//   tcgen05.ld (warp w owns TMEM lanes = features 32*(w%4).. and half of the
-//   token columns) and store it: for each token, a warp writes 32
+// * after the last k-slice the first converter group reads the accumulator
+//   with tcgen05.ld (warp w owns TMEM lanes = features 32*(w%4).. and half of
+//   the token columns) and stores it: for each token, a warp writes 32
 //   consecutive features.
 // Stages are tracked with mbarriers; every wait is bounded and an expired
 // wait aborts the whole CTA (which still frees its TMEM).  No TMA load uses
@@ -42,15 +43,25 @@ namespace gemm {
 constexpr int kFT = 128;                 // features per tile = A rows = TMEM lanes
 constexpr int kBK = 64;                  // k per operand stage (one 128-B f16 swizzle row)
 constexpr int kSuperK = 256;             // k per raw weight stage (8 blocks, 144 B per row)
-constexpr int kStages = 3;               // operand stages
-constexpr int kRawStages = 2;            // raw weight stages
+// Four operand stages (4 x 48 KB at TT = 256) keep three 64-k slices of
+// MMA work queued behind the one in flight, enough to cover the TMA
+// latency of the activation tiles; one raw stage (256 k) is refilled while
+// the converted stages ahead of it drain.  Three operand stages with two
+// raw stages ran at 931 TFLOP/s, four with one at 1008 (M=2048, K=4096,
+// N=14336, 8 converter warps).
+constexpr int kStages = 4;               // operand stages
+constexpr int kRawStages = 1;            // raw weight stages
 constexpr int kWBytes = kFT * kBK * 2;   // 16 KB converted weights per stage (A)
 constexpr int kRawRowBytes = 144;
 constexpr int kRawBytes = kFT * kRawRowBytes;  // 18 KB
-constexpr int kConvWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 10 * 32;
+// Converter warps form kConvGroups groups of 8; group g converts the 64-k
+// slices kb with kb % kConvGroups == g, so each group has kConvGroups MMA
+// slices of time per slice it converts.
+constexpr int kConvGroups = 2;
+constexpr int kConvWarps = 8 * kConvGroups;
+constexpr int kProducerWarp = kConvWarps;
+constexpr int kMmaWarp = kConvWarps + 1;
+constexpr int kThreads = (kConvWarps + 2) * 32;
 
 // Shared-memory layout for a token tile of TT (64, 128 or 256) tokens = the
 // MMA's N and the TMEM columns: activations TT x 64 k per stage (B).
@@ -278,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&x_full[s], 1);
-            mbar_init(&w_full[s], kConvWarps);
+            mbar_init(&w_full[s], 8);  // the 8 warps of the slice's group
             mbar_init(&empty[s], 1);
         }
         for (int r = 0; r < kRawStages; ++r) {
@@ -341,11 +352,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // converters: warp w converts the even (w < 4) or odd (w >= 4) block
-        // of every 64-k slice of weight row 32*(w%4) + lane
+        // converters: warp w of group g = w / 8 converts the even (w % 8 < 4)
+        // or odd block of the group's 64-k slices, weight row 32*(w%4) + lane
         const int row = 32 * (warp % 4) + lane;  // 0..127
         const int swz = row & 7;
-        const bool odd = warp >= 4;
+        const bool odd = (warp % 8) >= 4;
+        const int group = warp / 8;
         const std::uint32_t nsb = num_kb / (kSuperK / kBK);
         bool ok = true;
         for (std::uint32_t sb = 0; sb < nsb && ok; ++sb) {
@@ -373,21 +385,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
                                      smem_u32(&w_full[s]))
                                  : "memory");
-                    if (SUB == (kSuperK / kBK) - 1)
+                    // the group's last slice of this raw stage
+                    if (SUB + kConvGroups >= kSuperK / kBK)
                         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
                                          smem_u32(&raw_empty[r]))
                                      : "memory");
                 }
             };
-            slice(std::integral_constant<int, 0>{});
-            slice(std::integral_constant<int, 1>{});
-            slice(std::integral_constant<int, 2>{});
-            slice(std::integral_constant<int, 3>{});
+            static_assert(kConvGroups == 2 && kSuperK / kBK == 4, "slice assignment");
+            if (group == 0) {  // warp-uniform
+                slice(std::integral_constant<int, 0>{});
+                slice(std::integral_constant<int, 2>{});
+            } else {
+                slice(std::integral_constant<int, 1>{});
+                slice(std::integral_constant<int, 3>{});
+            }
         }
-        // epilogue: warp w reads TMEM lanes (features) 32*(w%4).. and token
-        // columns (TT/2)*(w/4)..; for each token the warp stores 32
-        // consecutive features
-        if (__all_sync(0xffffffffu, ok && wait_or_abort(accum, 0, abort_flag))) {
+        // epilogue (group 0): warp w reads TMEM lanes (features) 32*(w%4)..
+        // and token columns (TT/2)*(w/4)..; for each token the warp stores
+        // 32 consecutive features
+        if (group == 0 && __all_sync(0xffffffffu, ok && wait_or_abort(accum, 0, abort_flag))) {
             tc_fence_after();
             const int lane_base = 32 * (warp % 4);
             const int col_base = (TT / 2) * (warp / 4);

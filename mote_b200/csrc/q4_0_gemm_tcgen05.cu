@@ -63,14 +63,33 @@ constexpr int kProducerWarp = kConvWarps;
 constexpr int kMmaWarp = kConvWarps + 1;
 constexpr int kThreads = (kConvWarps + 2) * 32;
 
+// The converted weights (the MMA's A operand) live in tensor memory, next
+// to the accumulator, instead of shared memory: the converters write them
+// with tcgen05.st (a warp reaches exactly the 32 TMEM lanes = weight rows
+// it converts) and the MMA reads A from TMEM, which takes 32 KB per slice of
+// traffic off shared memory.
+constexpr bool kATmem = true;
+
+constexpr int pow2_at_least(int v) {
+    int p = 32;
+    while (p < v) p *= 2;
+    return p;
+}
+
 // Shared-memory layout for a token tile of TT (64, 128 or 256) tokens = the
-// MMA's N and the TMEM columns: activations TT x 64 k per stage (B).
+// MMA's N and the accumulator's TMEM columns: activations TT x 64 k per
+// stage (B).
 template <int TT>
 struct Layout {
     static constexpr int kXBytes = TT * kBK * 2;
     static constexpr int kOffX = 0;
     static constexpr int kOffW = kOffX + kStages * kXBytes;
-    static constexpr int kOffRaw = kOffW + kStages * kWBytes;
+    static constexpr int kOffRaw = kOffW + (kATmem ? 0 : kStages * kWBytes);
+    // TMEM: accumulator columns [0, TT), then A stage s at kAColBase + 32 s
+    // (64 k of f16 = 32 columns of 32 bits per lane)
+    static constexpr int kAColBase = TT;
+    static constexpr int kTmemCols = kATmem ? pow2_at_least(TT + kStages * 32) : TT;
+    static_assert(kTmemCols <= 512, "tensor memory");
     static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
     // barriers: x_full[S], w_full[S], empty[S], raw_full[R], raw_empty[R], accum
     static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
@@ -135,6 +154,22 @@ __device__ __forceinline__ void umma_f16(std::uint32_t tmem_d, std::uint64_t ade
         : "memory");
 }
 
+// Same with A read from tensor memory (128 lanes = rows, 8 columns of two
+// f16 = 16 k per step).
+__device__ __forceinline__ void umma_f16_ta(std::uint32_t tmem_d, std::uint32_t tmem_a,
+                                            std::uint64_t bdesc, std::uint32_t idesc,
+                                            std::uint32_t accumulate) {
+    const std::uint32_t mask = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+            tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask), "r"(mask), "r"(mask),
+        "r"(mask)
+        : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(std::uint32_t bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -188,10 +223,9 @@ __device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t 
 
 // One Q4_0 block -- scale bits `dbits`, quant words q[0..3] = bytes 0..15 --
 // to 32 f16 values (q - 8) * d (exact subtraction, one rounding in the
-// product), written as four 16-byte chunks of the 128-byte swizzled row at
-// `dst_row`, starting at element e0 (0 or 32).
+// product): o[j] holds elements 2j, 2j+1.
 __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::uint32_t (&q)[4],
-                                              std::uint32_t dst_row, int e0, int swz) {
+                                              std::uint32_t (&o)[16]) {
     const std::uint32_t d2 = dbits | (dbits << 16);
     std::uint32_t lo[8], hi[8];
 #pragma unroll
@@ -203,7 +237,6 @@ __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::ui
         hi[2 * i] = and_or(a, 0x00F000F0u, 0x54005400u);
         hi[2 * i + 1] = and_or(b, 0x00F000F0u, 0x54005400u);
     }
-    std::uint32_t o[16];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         std::uint32_t t;
@@ -212,7 +245,12 @@ __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::ui
         asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(hi[i]), "r"(0x54805480u));
         asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[8 + i]) : "r"(t), "r"(d2));
     }
-    // o[0..7]: elements 0..15, o[8..15]: elements 16..31, 8 elements per chunk
+}
+
+// The 32 converted values as four 16-byte chunks of the 128-byte swizzled
+// row at `dst_row`, starting at element e0 (0 or 32).
+__device__ __forceinline__ void store_block_swizzled(const std::uint32_t (&o)[16],
+                                                     std::uint32_t dst_row, int e0, int swz) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         const int chunk = (e0 / 8 + c) ^ swz;
@@ -222,6 +260,18 @@ __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::ui
     }
 }
 
+// The 32 converted values of this lane's row into 16 consecutive TMEM
+// columns of its lane (the warp's 32 lanes at once).
+__device__ __forceinline__ void store_block_tmem(const std::uint32_t (&o)[16], std::uint32_t taddr) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]),
+        "r"(o[8]), "r"(o[9]), "r"(o[10]), "r"(o[11]), "r"(o[12]), "r"(o[13]), "r"(o[14]),
+        "r"(o[15])
+        : "memory");
+}
+
 // Converts one Q4_0 block (PAR = 0: the even, 1: the odd block) of 64-k
 // slice SUB (0..3) of a 144-byte raw row (16-byte aligned at `raw_row`) into
 // the swizzled f16 row `dst_row`.  The slice spans bytes [36*SUB, 36*SUB +
@@ -229,7 +279,7 @@ __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::ui
 // apart, so a warp's loads are bank-conflict free) and byte permutes pick
 // the block out.
 template <int SUB, int PAR>
-__device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::uint32_t dst_row,
+__device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::uint32_t dst,
                                                    int swz) {
     constexpr int kStart = 36 * SUB;
     constexpr int kChunk0 = kStart / 16;
@@ -242,17 +292,24 @@ __device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::u
                      : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
                      : "r"(raw_row + chunk * 16));
     }
+    std::uint32_t o[16];
     if constexpr (PAR == 0) {
         // even block: scale = low half of word kW, quants start 2 bytes later
         std::uint32_t q0[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) q0[i] = prmt(w[kW + i], w[kW + i + 1], 0x5432u);
-        convert_block(w[kW] & 0xFFFFu, q0, dst_row, 0, swz);
+        convert_block(w[kW] & 0xFFFFu, q0, o);
     } else {
         // odd block: scale = high half of word kW+4, quants are words kW+5..kW+8
         const std::uint32_t q1[4] = {w[kW + 5], w[kW + 6], w[kW + 7], w[kW + 8]};
-        convert_block(w[kW + 4] >> 16, q1, dst_row, 32, swz);
+        convert_block(w[kW + 4] >> 16, q1, o);
     }
+    // dst: the TMEM address of the block's 16 columns, or the swizzled
+    // shared-memory row
+    if constexpr (kATmem)
+        store_block_tmem(o, dst);
+    else
+        store_block_swizzled(o, dst, 32 * PAR, swz);
 }
 
 template <int TT, bool OF32>
@@ -263,7 +320,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kOffX = L::kOffX, kOffW = L::kOffW, kOffRaw = L::kOffRaw, kOffBar = L::kOffBar;
     constexpr int kOffTmemSlot = L::kOffTmemSlot, kOffAbort = L::kOffAbort;
     constexpr int kXBytes = L::kXBytes;
-    constexpr int kTmemCols = TT;
     extern __shared__ std::uint8_t smem_raw[];
     // 1024-byte aligned base (SW128 atoms and TMA swizzle need it)
     const std::uint32_t raw_base = smem_u32(smem_raw);
@@ -285,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const std::uint32_t n0 = blockIdx.x * kFT;   // first feature (weight row)
     const std::uint32_t m0 = blockIdx.y * TT;    // first token
     const std::uint32_t num_kb = p.K / kBK;
+    constexpr int kTmemCols = L::kTmemCols;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -342,9 +399,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const std::uint32_t x_addr = base + kOffX + s * kXBytes;
 #pragma unroll
                 for (int k = 0; k < kBK / 16; ++k) {
-                    // +32 bytes per 16-element step inside the 128-byte swizzle row
-                    umma_f16(tmem_d, smem_desc_sw128(w_addr + k * 32),
-                             smem_desc_sw128(x_addr + k * 32), L::kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    // +32 bytes per 16-element step inside the 128-byte swizzle
+                    // row; A in TMEM: +8 columns (16 f16) per step
+                    if constexpr (kATmem)
+                        umma_f16_ta(tmem_d, tmem_d + L::kAColBase + s * 32 + k * 8,
+                                    smem_desc_sw128(x_addr + k * 32), L::kIdesc,
+                                    (kb | k) != 0 ? 1u : 0u);
+                    else
+                        umma_f16(tmem_d, smem_desc_sw128(w_addr + k * 32),
+                                 smem_desc_sw128(x_addr + k * 32), L::kIdesc,
+                                 (kb | k) != 0 ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&empty[s]));
             }
@@ -373,13 +437,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = __all_sync(0xffffffffu, wait_or_abort(&empty[s], ((kb / kStages) - 1) & 1u,
                                                                abort_flag));
                 if (!ok) return;  // warp-uniform
-                const std::uint32_t dst = base + kOffW + s * kWBytes + row * 128;
+                const std::uint32_t dst =
+                    kATmem ? tmem_d + (static_cast<std::uint32_t>(32 * (warp % 4)) << 16) +
+                                 static_cast<std::uint32_t>(L::kAColBase + s * 32 + (odd ? 16 : 0))
+                           : base + kOffW + s * kWBytes + row * 128;
                 if (odd)  // warp-uniform
                     convert_half_slice<SUB, 1>(raw_row, dst, swz);
                 else
                     convert_half_slice<SUB, 0>(raw_row, dst, swz);
-                // make the generic-proxy writes visible to the tensor core
-                fence_proxy_async_smem();
+                if constexpr (kATmem) {
+                    // the TMEM stores complete before the MMA warp is told
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                } else {
+                    // make the generic-proxy writes visible to the tensor core
+                    fence_proxy_async_smem();
+                }
                 __syncwarp();
                 if (lane == 0) {
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(

@@ -516,23 +516,22 @@ class Bench:
                                 "tflops": round(flops / ms / 1e9, 1)}
         return out
 
-    def lm_head_sharded(self) -> dict:
-        """Config 5 at N > 1: lm_head rows split over the ranks (strong
-        scaling); per step each rank runs the GEMV on its shard and the f16
-        logits are all-gathered: with NCCL (mote_cuda_comm_*), with the
-        peer-store kernel, and fused into the GEMV epilogue (stores into
-        every rank's [M, N] logits over NVLink + flag handshake).  Steps are
-        captured in CUDA graphs; times are the max over ranks; GB/s counts
-        the full 295.5 MB weight once per step.  A shard smaller than 2.5x
-        L2 (G >= 2) is rotated over copies, one per step, like the sweep."""
+    def sharded_linear(self, n: int, ms_list, seed: int, k: int = 4096) -> dict:
+        """A linear column-sharded over the ranks (strong scaling): per step
+        each rank runs the Q4_0 linear on its rows [rank * shard, ...) and the
+        f16 outputs are all-gathered -- with NCCL (mote_cuda_comm_*), with the
+        peer-store kernel, and (<= 16 tokens) fused into the GEMV epilogue
+        (stores into every rank's [M, N] output over NVLink + flag
+        handshake).  Steps are captured in CUDA graphs; times are the max over
+        ranks; GB/s counts the full weight once per step, TFLOP/s 2 M N K.  A
+        shard smaller than 2.5x L2 is rotated over copies, one per step."""
         torch = self.torch
         import torch.distributed as dist
 
         from mote_b200 import comm
 
-        k, n = 4096, 128256
         sh = comm.shard_rows(n, self.world, self.rank)
-        w0 = self.encode_q4_0(sh.rows, k, seed=700 + self.rank)
+        w0 = self.encode_q4_0(sh.rows, k, seed=seed + self.rank)
         ws = [w0] + [w0.clone() for _ in range(copies_for(w0.numel()) - 1)]
         fn = self.lib.mote_cuda_quantized_linear_q4_0_f16
 
@@ -542,10 +541,12 @@ class Bench:
             return out
 
         nccl = comm.NcclAllGather(self.world, self.rank, exchange)
-        result = {"shard_rows": sh.rows, "world": self.world, "weight_copies": len(ws)}
-        reps, steps = 10, max(8, len(ws))
+        result = {"n": n, "k": k, "shard_rows": sh.rows, "world": self.world,
+                  "weight_copies": len(ws)}
+        steps = max(8, len(ws))
         try:
-            for m in (1, 16, 64):
+            for m in ms_list:
+                reps = 10 if m <= 64 else 3
                 x = self.randn((m, k), 60 + m, torch.float16)
                 y = torch.empty((m, sh.rows), dtype=torch.float16, device=self.dev)
                 count = m * sh.rows
@@ -554,22 +555,22 @@ class Bench:
                 fused = comm.ShardedLinearQ4_0(self.world, self.rank, m, n, k, exchange) \
                     if m <= 16 else None
 
-                def gemv(i, x=x, y=y, m=m):
+                def linear(i, x=x, y=y, m=m):
                     self.check(fn(x.data_ptr(), ws[i % len(ws)].data_ptr(), y.data_ptr(), m,
-                                  sh.rows, k, self.stream()), "lm_head shard")
+                                  sh.rows, k, self.stream()), "linear shard")
 
                 def run_gemv():
                     for i in range(steps):
-                        gemv(i)
+                        linear(i)
 
                 def run_nccl(y=y, recv=recv, count=count):
                     for i in range(steps):
-                        gemv(i)
+                        linear(i)
                         nccl.all_gather(y.data_ptr(), recv.data_ptr(), count, self.stream())
 
                 def run_p2p(y=y, peer=peer):
                     for i in range(steps):
-                        gemv(i)
+                        linear(i)
                         peer.all_gather(y.data_ptr(), i % 2, self.stream())
 
                 def run_fused(x=x, fused=fused):
@@ -586,19 +587,65 @@ class Bench:
                     self.barrier()
                     g = self.graph(body)
                     self.barrier()
-                    ms = self.max_over_ranks(self.time_graph(g, reps, steps * kernels)) / steps
+                    t = self.max_over_ranks(self.time_graph(g, reps, steps * kernels)) / steps
                     del g
-                    row[f"{name}_us"] = round(ms * 1e3, 2)
-                    row[f"{name}_gbs"] = round(linear_bytes(m, n, k) / ms / 1e6, 1)
+                    row[f"{name}_us"] = round(t * 1e3, 2)
+                    if m > 64:
+                        row[f"{name}_tflops"] = round(2.0 * m * n * k / t / 1e9, 1)
+                    else:
+                        row[f"{name}_gbs"] = round(linear_bytes(m, n, k) / t / 1e6, 1)
                 result[f"m{m}"] = row
                 self.barrier()
                 peer.close(barrier=self.barrier)
                 if fused is not None:
                     fused.close(barrier=self.barrier)
+                del recv, y
         finally:
             torch.cuda.synchronize()
             nccl.close()
         return result
+
+    def norm_rope_row_split(self) -> dict:
+        """Config 2 at N > 1: the T = 512 tokens split by rows, T/G per rank,
+        no exchange (the tokens are independent); us per layer = max over
+        ranks, inputs rotated over copies holding >= 2.5x L2 per rank."""
+        torch = self.torch
+        t_all, hidden, qh, kh, hd = 512, 2048, 32, 8, 64
+        t = -(-t_all // self.world)
+        nbytes = (2 * t * hidden + 2 * t * qh * hd + 2 * t * kh * hd) * 2 + hidden * 2 + \
+            2 * t * (hd // 2) * 4
+        r = copies_for(nbytes)
+        pos = torch.arange(self.rank * t, self.rank * t + t, dtype=torch.int32, device=self.dev)
+        cos = torch.empty((t, hd // 2), dtype=torch.float32, device=self.dev)
+        sin = torch.empty_like(cos)
+        self.check(self.lib.mote_cuda_rope_cos_sin_f32(pos.data_ptr(), cos.data_ptr(),
+                                                       sin.data_ptr(), t, hd,
+                                                       ctypes.c_double(10000.0), self.stream()),
+                   "rope table")
+        gamma = self.randn((hidden,), 3, torch.float16, 0.1, 1.0)
+        sets = []
+        for i in range(r):
+            x = self.randn((t, hidden), 10 + i, torch.float16)
+            q = self.randn((t, qh, hd), 1000 + i, torch.float16)
+            kk = self.randn((t, kh, hd), 2000 + i, torch.float16)
+            sets.append((x, torch.empty_like(x), q, torch.empty_like(q), kk, torch.empty_like(kk),
+                         cos.clone(), sin.clone()))
+        fn = self.lib.mote_cuda_rms_norm_rope_f16
+
+        def run():
+            for (x, xo, q, qo, kk, ko, c, s) in sets:
+                self.check(fn(x.data_ptr(), gamma.data_ptr(), xo.data_ptr(), q.data_ptr(),
+                              qo.data_ptr(), kk.data_ptr(), ko.data_ptr(), c.data_ptr(),
+                              s.data_ptr(), t, hidden, qh, kh, hd, 0, ctypes.c_float(1e-6),
+                              self.stream()), "norm+rope")
+
+        self.barrier()
+        g = self.graph(run)
+        self.barrier()
+        ms = self.max_over_ranks(self.time_graph(g, 20, r)) / r
+        del g, sets
+        return {"tokens_per_rank": t, "us_per_layer": round(ms * 1e3, 3),
+                "gbs_total": round(nbytes * self.world / ms / 1e6, 1), "copies": r}
 
     # -- main -------------------------------------------------------------------
     def run(self) -> dict | None:
@@ -654,7 +701,13 @@ class Bench:
             extra["config5"] = self.config5()
         e2e = self.e2e(max(3, min(args.steps, 20)))
         if self.world > 1:
-            extra["lm_head_sharded"] = self.lm_head_sharded()
+            # the splits the data plane supports: lm_head and FFN up/gate by
+            # output columns (decode GEMV), the prefill GEMM by output columns
+            # (tcgen05), config 2 by token rows
+            extra["lm_head_sharded"] = self.sharded_linear(128256, (1, 16, 64), seed=700)
+            extra["ffn_up_sharded"] = self.sharded_linear(14336, (1, 16), seed=800)
+            extra["prefill_sharded"] = self.sharded_linear(14336, (2048,), seed=900)
+            extra["norm_rope_row_split"] = self.norm_rope_row_split()
         if self.rank == 0:
             cpu = cpu_baseline(budget_s=args.cpu_seconds)
             c2 = extra["config2_rmsnorm_rope_t512"]

@@ -505,9 +505,14 @@ class Bench:
         x = self.randn((m, k), 99, torch.float16)
         y = torch.empty((m, n), dtype=torch.float16, device=self.dev)
 
+        wsp = torch.zeros(max(self.workspace_bytes(m, n, k), 256), dtype=torch.uint8,
+                          device=self.dev)
+
         def runp():
-            self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, self.stream()),
-                       "prefill")
+            # the workspace entry (what mote_b200.ops calls): the partial last
+            # wave of tiles is split along K through the workspace
+            self.check(fn_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, wsp.data_ptr(),
+                             wsp.numel(), self.stream()), "prefill")
 
         g = self.graph(runp)
         ms = self.time_graph(g, 5, 1)

@@ -51,7 +51,6 @@ constexpr int kSuperK = 256;             // k per raw weight stage (8 blocks, 14
 // N=14336, 8 converter warps).
 constexpr int kStages = 4;               // operand stages
 constexpr int kRawStages = 1;            // raw weight stages
-constexpr int kWBytes = kFT * kBK * 2;   // 16 KB converted weights per stage (A)
 constexpr int kRawRowBytes = 144;
 constexpr int kRawBytes = kFT * kRawRowBytes;  // 18 KB
 // Converter warps form kConvGroups groups of 8; group g converts the 64-k
@@ -64,12 +63,10 @@ constexpr int kMmaWarp = kConvWarps + 1;
 constexpr int kThreads = (kConvWarps + 2) * 32;
 
 // The converted weights (the MMA's A operand) live in tensor memory, next
-// to the accumulator, instead of shared memory: the converters write them
-// with tcgen05.st (a warp reaches exactly the 32 TMEM lanes = weight rows
-// it converts) and the MMA reads A from TMEM, which takes 32 KB per slice of
-// traffic off shared memory.
-constexpr bool kATmem = true;
-
+// to the accumulator: the converters write them with tcgen05.st (a warp
+// reaches exactly the 32 TMEM lanes = weight rows it converts) and the MMA
+// reads A from TMEM.  Against A in shared memory this takes 32 KB per slice
+// of traffic off shared memory and the proxy fence off the converters.
 constexpr int pow2_at_least(int v) {
     int p = 32;
     while (p < v) p *= 2;
@@ -83,12 +80,11 @@ template <int TT>
 struct Layout {
     static constexpr int kXBytes = TT * kBK * 2;
     static constexpr int kOffX = 0;
-    static constexpr int kOffW = kOffX + kStages * kXBytes;
-    static constexpr int kOffRaw = kOffW + (kATmem ? 0 : kStages * kWBytes);
+    static constexpr int kOffRaw = kOffX + kStages * kXBytes;
     // TMEM: accumulator columns [0, TT), then A stage s at kAColBase + 32 s
     // (64 k of f16 = 32 columns of 32 bits per lane)
     static constexpr int kAColBase = TT;
-    static constexpr int kTmemCols = kATmem ? pow2_at_least(TT + kStages * 32) : TT;
+    static constexpr int kTmemCols = pow2_at_least(TT + kStages * 32);
     static_assert(kTmemCols <= 512, "tensor memory");
     static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
     // barriers: x_full[S], w_full[S], empty[S], raw_full[R], raw_empty[R], accum
@@ -103,10 +99,21 @@ struct Layout {
     static_assert(TT == 64 || TT == 128 || TT == 256, "token tile");
 };
 
+// Tiles are numbered feature-tile-fastest: tile t covers features
+// 128 * (t % tiles_n) and tokens TT * (t / tiles_n).  CTA b < full computes
+// tile b over all of K.  With a workspace, the tiles of a partial last wave
+// are split along K instead: CTA full + j computes part j % parts (K/parts
+// of K) of tile full + j / parts and stores its f32 accumulator to
+// part_buf[j] as [TT tokens][128 features]; q4_0_gemm_reduce_kernel adds
+// the parts in part order afterwards.
 struct Params {
     void* y;
     std::uint32_t M, N, K;
     std::uint64_t ldy;
+    std::uint32_t tiles_n;
+    std::uint32_t full;     // CTAs that compute a whole tile
+    std::uint32_t parts;    // K parts of a split tile (1: no split)
+    float* part_buf;
 };
 
 // ---- PTX wrappers ------------------------------------------------------------
@@ -139,23 +146,9 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, cta_group::1.
-__device__ __forceinline__ void umma_f16(std::uint32_t tmem_d, std::uint64_t adesc,
-                                         std::uint64_t bdesc, std::uint32_t idesc,
-                                         std::uint32_t accumulate) {
-    const std::uint32_t mask = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
-            tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask), "r"(mask), "r"(mask),
-        "r"(mask)
-        : "memory");
-}
-
-// Same with A read from tensor memory (128 lanes = rows, 8 columns of two
-// f16 = 16 k per step).
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, cta_group::1: A read
+// from tensor memory (128 lanes = rows, 8 columns of two f16 = 16 k per
+// step), B from shared memory.
 __device__ __forceinline__ void umma_f16_ta(std::uint32_t tmem_d, std::uint32_t tmem_a,
                                             std::uint64_t bdesc, std::uint32_t idesc,
                                             std::uint32_t accumulate) {
@@ -247,19 +240,6 @@ __device__ __forceinline__ void convert_block(std::uint32_t dbits, const std::ui
     }
 }
 
-// The 32 converted values as four 16-byte chunks of the 128-byte swizzled
-// row at `dst_row`, starting at element e0 (0 or 32).
-__device__ __forceinline__ void store_block_swizzled(const std::uint32_t (&o)[16],
-                                                     std::uint32_t dst_row, int e0, int swz) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const int chunk = (e0 / 8 + c) ^ swz;
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst_row + chunk * 16),
-                     "r"(o[4 * c]), "r"(o[4 * c + 1]), "r"(o[4 * c + 2]), "r"(o[4 * c + 3])
-                     : "memory");
-    }
-}
-
 // The 32 converted values of this lane's row into 16 consecutive TMEM
 // columns of its lane (the warp's 32 lanes at once).
 __device__ __forceinline__ void store_block_tmem(const std::uint32_t (&o)[16], std::uint32_t taddr) {
@@ -274,13 +254,12 @@ __device__ __forceinline__ void store_block_tmem(const std::uint32_t (&o)[16], s
 
 // Converts one Q4_0 block (PAR = 0: the even, 1: the odd block) of 64-k
 // slice SUB (0..3) of a 144-byte raw row (16-byte aligned at `raw_row`) into
-// the swizzled f16 row `dst_row`.  The slice spans bytes [36*SUB, 36*SUB +
+// the 16 TMEM columns at `taddr` (this lane's row).  The slice spans bytes [36*SUB, 36*SUB +
 // 36); three aligned 16-byte loads cover it (rows are 144 = 9 x 16 bytes
 // apart, so a warp's loads are bank-conflict free) and byte permutes pick
 // the block out.
 template <int SUB, int PAR>
-__device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::uint32_t dst,
-                                                   int swz) {
+__device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::uint32_t taddr) {
     constexpr int kStart = 36 * SUB;
     constexpr int kChunk0 = kStart / 16;
     constexpr int kW = (kStart % 16) / 4;  // first word of the slice within the 12 loaded
@@ -304,12 +283,7 @@ __device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::u
         const std::uint32_t q1[4] = {w[kW + 5], w[kW + 6], w[kW + 7], w[kW + 8]};
         convert_block(w[kW + 4] >> 16, q1, o);
     }
-    // dst: the TMEM address of the block's 16 columns, or the swizzled
-    // shared-memory row
-    if constexpr (kATmem)
-        store_block_tmem(o, dst);
-    else
-        store_block_swizzled(o, dst, 32 * PAR, swz);
+    store_block_tmem(o, taddr);
 }
 
 template <int TT, bool OF32>
@@ -317,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
                              const __grid_constant__ CUtensorMap map_w, const Params p) {
     using L = Layout<TT>;
-    constexpr int kOffX = L::kOffX, kOffW = L::kOffW, kOffRaw = L::kOffRaw, kOffBar = L::kOffBar;
+    constexpr int kOffX = L::kOffX, kOffRaw = L::kOffRaw, kOffBar = L::kOffBar;
     constexpr int kOffTmemSlot = L::kOffTmemSlot, kOffAbort = L::kOffAbort;
     constexpr int kXBytes = L::kXBytes;
     extern __shared__ std::uint8_t smem_raw[];
@@ -338,9 +312,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const std::uint32_t n0 = blockIdx.x * kFT;   // first feature (weight row)
-    const std::uint32_t m0 = blockIdx.y * TT;    // first token
-    const std::uint32_t num_kb = p.K / kBK;
+    // this CTA's tile and K range (in 64-k slices: [kb0, kb0 + num_kb))
+    const bool split = blockIdx.x >= p.full;
+    const std::uint32_t j = blockIdx.x - p.full;  // split CTAs only
+    const std::uint32_t tile = split ? p.full + j / p.parts : blockIdx.x;
+    const std::uint32_t n0 = (tile % p.tiles_n) * kFT;  // first feature (weight row)
+    const std::uint32_t m0 = (tile / p.tiles_n) * TT;   // first token
+    const std::uint32_t num_kb = split ? p.K / kBK / p.parts : p.K / kBK;
+    const std::uint32_t kb0 = split ? (j % p.parts) * num_kb : 0;
     constexpr int kTmemCols = L::kTmemCols;
 
     if (threadIdx.x == 0) {
@@ -378,12 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     mbar_arrive_expect_tx(&raw_full[r], kRawBytes);
                     tma_load_2d(base + kOffRaw + r * kRawBytes, &map_w,
-                                static_cast<int>(sb * kRawRowBytes), static_cast<int>(n0),
-                                smem_u32(&raw_full[r]));
+                                static_cast<int>((kb0 / (kSuperK / kBK) + sb) * kRawRowBytes),
+                                static_cast<int>(n0), smem_u32(&raw_full[r]));
                 }
                 mbar_arrive_expect_tx(&x_full[s], kXBytes);
-                tma_load_2d(base + kOffX + s * kXBytes, &map_x, static_cast<int>(kb * kBK),
-                            static_cast<int>(m0), smem_u32(&x_full[s]));
+                tma_load_2d(base + kOffX + s * kXBytes, &map_x,
+                            static_cast<int>((kb0 + kb) * kBK), static_cast<int>(m0),
+                            smem_u32(&x_full[s]));
             }
         }
         __syncwarp();  // reconverge before the block-wide barrier below
@@ -395,20 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_or_abort(&x_full[s], ph, abort_flag)) break;
                 if (!wait_or_abort(&w_full[s], ph, abort_flag)) break;
                 tc_fence_after();
-                const std::uint32_t w_addr = base + kOffW + s * kWBytes;
                 const std::uint32_t x_addr = base + kOffX + s * kXBytes;
 #pragma unroll
                 for (int k = 0; k < kBK / 16; ++k) {
-                    // +32 bytes per 16-element step inside the 128-byte swizzle
-                    // row; A in TMEM: +8 columns (16 f16) per step
-                    if constexpr (kATmem)
-                        umma_f16_ta(tmem_d, tmem_d + L::kAColBase + s * 32 + k * 8,
-                                    smem_desc_sw128(x_addr + k * 32), L::kIdesc,
-                                    (kb | k) != 0 ? 1u : 0u);
-                    else
-                        umma_f16(tmem_d, smem_desc_sw128(w_addr + k * 32),
-                                 smem_desc_sw128(x_addr + k * 32), L::kIdesc,
-                                 (kb | k) != 0 ? 1u : 0u);
+                    // B: +32 bytes per 16-element step inside the 128-byte
+                    // swizzle row; A in TMEM: +8 columns (16 f16) per step
+                    umma_f16_ta(tmem_d, tmem_d + L::kAColBase + s * 32 + k * 8,
+                                smem_desc_sw128(x_addr + k * 32), L::kIdesc,
+                                (kb | k) != 0 ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&empty[s]));
             }
@@ -419,7 +393,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // converters: warp w of group g = w / 8 converts the even (w % 8 < 4)
         // or odd block of the group's 64-k slices, weight row 32*(w%4) + lane
         const int row = 32 * (warp % 4) + lane;  // 0..127
-        const int swz = row & 7;
         const bool odd = (warp % 8) >= 4;
         const int group = warp / 8;
         const std::uint32_t nsb = num_kb / (kSuperK / kBK);
@@ -437,22 +410,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = __all_sync(0xffffffffu, wait_or_abort(&empty[s], ((kb / kStages) - 1) & 1u,
                                                                abort_flag));
                 if (!ok) return;  // warp-uniform
-                const std::uint32_t dst =
-                    kATmem ? tmem_d + (static_cast<std::uint32_t>(32 * (warp % 4)) << 16) +
-                                 static_cast<std::uint32_t>(L::kAColBase + s * 32 + (odd ? 16 : 0))
-                           : base + kOffW + s * kWBytes + row * 128;
+                // this warp's 32 TMEM lanes, the block's 16 columns of stage s
+                const std::uint32_t ta = tmem_d + (static_cast<std::uint32_t>(32 * (warp % 4)) << 16) +
+                                         static_cast<std::uint32_t>(L::kAColBase + s * 32 +
+                                                                    (odd ? 16 : 0));
                 if (odd)  // warp-uniform
-                    convert_half_slice<SUB, 1>(raw_row, dst, swz);
+                    convert_half_slice<SUB, 1>(raw_row, ta);
                 else
-                    convert_half_slice<SUB, 0>(raw_row, dst, swz);
-                if constexpr (kATmem) {
-                    // the TMEM stores complete before the MMA warp is told
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                    tc_fence_before();
-                } else {
-                    // make the generic-proxy writes visible to the tensor core
-                    fence_proxy_async_smem();
-                }
+                    convert_half_slice<SUB, 0>(raw_row, ta);
+                // the TMEM stores complete before the MMA warp is told
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
@@ -489,6 +457,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_32x32b_x32(tmem_d + (static_cast<std::uint32_t>(lane_base) << 16) +
                                        static_cast<std::uint32_t>(col_base + cb),
                                    v);
+                if (split) {
+                    // f32 part [token][feature] of split tile j / parts: for
+                    // each token the warp stores 32 consecutive features
+                    float* part = p.part_buf + static_cast<std::uint64_t>(j) * TT * kFT +
+                                  static_cast<std::uint32_t>(col_base + cb) * kFT + lane_base +
+                                  lane;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) part[i * kFT] = __uint_as_float(v[i]);
+                    continue;
+                }
                 const std::uint32_t mb = m0 + col_base + cb;
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
@@ -509,6 +487,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_d, kTmemCols);
+    }
+}
+
+// The split tiles: y[token][feature] = sum over parts, in part order, of
+// part_buf[(tile - full) * parts + part][token - m0][feature - n0].  One
+// thread per token and 4 consecutive features (reads and writes coalesced
+// along features).
+template <int TT, bool OF32>
+__global__ void __launch_bounds__(256) q4_0_gemm_reduce_kernel(const Params p,
+                                                              std::uint32_t split_tiles) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const std::uint64_t per_tile = static_cast<std::uint64_t>(TT) * (kFT / 4);
+    if (i >= per_tile * split_tiles) return;
+    const std::uint32_t st = static_cast<std::uint32_t>(i / per_tile);
+    const std::uint32_t rem = static_cast<std::uint32_t>(i % per_tile);
+    const std::uint32_t tok = rem / (kFT / 4);
+    const std::uint32_t f4 = (rem % (kFT / 4)) * 4;
+    const std::uint32_t tile = p.full + st;
+    const std::uint32_t n = (tile % p.tiles_n) * kFT + f4;
+    const std::uint32_t m = (tile / p.tiles_n) * TT + tok;
+    if (m >= p.M || n >= p.N) return;  // N % 16 == 0: a 4-feature group is all in or out
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (std::uint32_t q = 0; q < p.parts; ++q) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(
+            p.part_buf + (static_cast<std::uint64_t>(st) * p.parts + q) * TT * kFT +
+            static_cast<std::uint64_t>(tok) * kFT + f4));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    if constexpr (OF32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.y) + m * p.ldy + n) = acc;
+    } else {
+        __half2 h[2] = {__floats2half2_rn(acc.x, acc.y), __floats2half2_rn(acc.z, acc.w)};
+        *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + m * p.ldy + n) =
+            *reinterpret_cast<const uint2*>(h);
     }
 }
 
@@ -539,9 +556,50 @@ inline bool supported(const void* x, const void* w, const void* y, std::uint64_t
            reinterpret_cast<std::uintptr_t>(y) % 16 == 0 && (N * out_size) % 16 == 0;
 }
 
+// Split of the partial last wave: with T tiles on `slots` resident CTAs and
+// r = T mod slots tiles left for the last wave (at most half of it), each of
+// those r tiles is split along K into `parts` (a power of two dividing K/256
+// with r * parts <= slots) so the last wave fills the GPU; the parts meet in
+// the workspace.  Returns parts (1: no split) and the bytes it needs.
+struct SplitPlan {
+    std::uint32_t full = 0, parts = 1, split_tiles = 0;
+    std::uint64_t bytes = 0;
+};
+template <int TT>
+inline SplitPlan plan_split(std::uint64_t tiles, std::uint64_t K, std::uint64_t slots) {
+    SplitPlan sp;
+    sp.full = static_cast<std::uint32_t>(tiles);
+    if (slots == 0 || tiles <= slots) return sp;
+    const std::uint64_t r = tiles % slots;
+    if (r == 0 || 2 * r > slots) return sp;
+    std::uint64_t parts = 1;
+    while ((K / kSuperK) % (parts * 2) == 0 && r * parts * 2 <= slots) parts *= 2;
+    if (parts < 2) return sp;
+    sp.full = static_cast<std::uint32_t>(tiles - r);
+    sp.parts = static_cast<std::uint32_t>(parts);
+    sp.split_tiles = static_cast<std::uint32_t>(r);
+    sp.bytes = r * parts * TT * kFT * 4;
+    return sp;
+}
+
+// Resident CTAs per SM of a kernel (cached per device ordinal).
+template <typename Kernel>
+int ctas_per_sm(Kernel kernel, int smem, std::atomic<int> (&cache)[64], int dev) {
+    int v = cache[dev & 63].load(std::memory_order_relaxed);
+    if (v == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kThreads, smem) !=
+                cudaSuccess ||
+            v <= 0)
+            v = 1;
+        cache[dev & 63].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
 template <int TT, bool OF32>
 int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
-                std::uint64_t K, cudaStream_t stream) {
+                std::uint64_t K, cudaStream_t stream, void* workspace,
+                std::uint64_t workspace_bytes) {
     using L = Layout<TT>;
     auto encode = encode_fn();
     if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
@@ -581,22 +639,65 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
         if (e != cudaSuccess) return static_cast<int>(e);
         configured.fetch_or(bit);
     }
-    Params p{y, static_cast<std::uint32_t>(M), static_cast<std::uint32_t>(N),
-             static_cast<std::uint32_t>(K), N};
-    const dim3 grid(static_cast<unsigned>((N + kFT - 1) / kFT),
-                    static_cast<unsigned>((M + TT - 1) / TT));
+    const std::uint64_t tiles_n = (N + kFT - 1) / kFT;
+    const std::uint64_t tiles = tiles_n * ((M + TT - 1) / TT);
+    SplitPlan sp;
+    sp.full = static_cast<std::uint32_t>(tiles);
+    if (workspace != nullptr && reinterpret_cast<std::uintptr_t>(workspace) % 16 == 0) {
+        static std::atomic<int> occ[64];
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        const SplitPlan cand = plan_split<TT>(
+            tiles, K,
+            static_cast<std::uint64_t>(sms) * ctas_per_sm(kernel, L::kSmemBytes, occ, dev));
+        if (cand.parts > 1 && cand.bytes <= workspace_bytes) sp = cand;
+    }
+    Params p{y,
+             static_cast<std::uint32_t>(M),
+             static_cast<std::uint32_t>(N),
+             static_cast<std::uint32_t>(K),
+             N,
+             static_cast<std::uint32_t>(tiles_n),
+             sp.full,
+             sp.parts,
+             static_cast<float*>(workspace)};
+    const unsigned grid = sp.full + sp.split_tiles * sp.parts;
     kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(map_x, map_w, p);
-    return static_cast<int>(cudaGetLastError());
+    e = cudaGetLastError();
+    if (e != cudaSuccess || sp.parts == 1) return static_cast<int>(e);
+    const std::uint64_t threads = static_cast<std::uint64_t>(sp.split_tiles) * TT * (kFT / 4);
+    return launch_pdl(q4_0_gemm_reduce_kernel<TT, OF32>,
+                      dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), stream, p,
+                      sp.split_tiles);
+}
+
+// Workspace bytes the split of a partial last wave can use for this shape
+// (0: no split), for the widest token tile of the shape.
+inline std::uint64_t split_workspace_bytes(std::uint64_t M, std::uint64_t N, std::uint64_t K) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        sms = 148;
+    const std::uint64_t tiles_n = (N + kFT - 1) / kFT;
+    // M > 128 runs 256-token tiles, one CTA per SM; narrower tiles at most 2 per SM
+    if (M > 128) return plan_split<256>(tiles_n * ((M + 255) / 256), K, sms).bytes;
+    const std::uint64_t a = plan_split<128>(tiles_n * ((M + 127) / 128), K, 2ull * sms).bytes;
+    const std::uint64_t b = plan_split<128>(tiles_n * ((M + 127) / 128), K, sms).bytes;
+    return a > b ? a : b;
 }
 
 // Token tile: the narrowest of 64 / 128 / 256 that holds M (wider tiles
 // waste MMA columns on missing tokens), 256 beyond.
 template <bool OF32>
 int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
-           std::uint64_t K, cudaStream_t stream) {
-    if (M <= 64) return launch_tile<64, OF32>(x, w, y, M, N, K, stream);
-    if (M <= 128) return launch_tile<128, OF32>(x, w, y, M, N, K, stream);
-    return launch_tile<256, OF32>(x, w, y, M, N, K, stream);
+           std::uint64_t K, cudaStream_t stream, void* workspace = nullptr,
+           std::uint64_t workspace_bytes = 0) {
+    if (M <= 64)
+        return launch_tile<64, OF32>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+    if (M <= 128)
+        return launch_tile<128, OF32>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+    return launch_tile<256, OF32>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
 }
 
 }  // namespace gemm

@@ -1078,7 +1078,16 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     if constexpr (!XF32 && EPI == kEpiPlain) {
         if (M > static_cast<std::uint64_t>(kMaxXRows) && ldy == N &&
             gemm::supported(x, w, y, M, N, K, osz))
-            return gemm::launch<OF32>(x, w, y, M, N, K, stream);
+        {
+            // the workspace past the tile counters holds the split parts
+            void* parts = nullptr;
+            std::uint64_t parts_bytes = 0;
+            if (workspace != nullptr && workspace_bytes > kCounterBytes) {
+                parts = static_cast<std::uint8_t*>(workspace) + kCounterBytes;
+                parts_bytes = workspace_bytes - kCounterBytes;
+            }
+            return gemm::launch<OF32>(x, w, y, M, N, K, stream, parts, parts_bytes);
+        }
     }
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
@@ -1458,6 +1467,12 @@ extern "C" int mote_cuda_q4_0_linear_workspace_bytes(std::uint64_t rows,
         return mote::kSuccess;
     const std::uint64_t tiles = (output_features + 15) / 16;
     if (tiles <= kCounterTiles) *bytes = part_workspace_bytes(4, tiles, 2);
+    if (rows > static_cast<std::uint64_t>(kMaxXRows) && output_features % 16 == 0) {
+        // tcgen05 shapes: the K split of a partial last wave
+        const std::uint64_t split = mote::gemm::split_workspace_bytes(rows, output_features,
+                                                                      input_features);
+        if (split != 0 && kCounterBytes + split > *bytes) *bytes = kCounterBytes + split;
+    }
     return mote::kSuccess;
 }
 

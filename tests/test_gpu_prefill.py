@@ -99,3 +99,45 @@ def test_config5_prefill_full_size_sampled(ctx, oracle_lib):
     ref = checker.linear_f64(x[rows].astype(np.float32), dec)
     assert checker.rel_err_normwise(got[rows], ref) <= NORMWISE
     assert checker.rel_err_elementwise(got[rows], ref) <= ELEMENTWISE
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 10240, 2048), (128, 38400, 2048), (64, 39680, 1024),
+                                   (2048, 14336, 4096)])
+def test_prefill_split_last_wave(ctx, oracle_lib, m, n, k):
+    """Through the workspace entry the tiles of a partial last wave are split
+    along K (on 148 SMs: 12 tiles x 8 parts, 4 x 8, 14 x 4 and 8 x 16 here)
+    and their f32 parts added in part order by a second kernel: two calls
+    give identical outputs, which agree with the unsplit kernel (the plain
+    entry) and, on sampled rows, with a float64 accumulation."""
+    import ctypes
+
+    from mote_b200._native import lib
+
+    w = fx.q4_0_weights(oracle_lib, n, k, seed=900 + m)
+    x = fx.activations(m, k, seed=901 + m).astype(np.float16)
+    xt = ctx.from_bytes(plain((m, k), DType.F16), x)
+    wt = ctx.from_bytes(quantized((n, k)), w)
+    need = ctypes.c_uint64(0)
+    assert lib().mote_cuda_q4_0_linear_workspace_bytes(m, n, k, ctypes.byref(need)) == 0
+    ws = ctx.from_bytes(plain((need.value,), DType.U8), np.zeros(need.value, np.uint8))
+    nan = np.full(m * n, np.nan, np.float16)
+    outs = []
+    for split in (True, True, False):
+        yt = ctx.from_bytes(plain((m, n), DType.F16), nan)
+        if split:
+            st = lib().mote_cuda_quantized_linear_q4_0_f16_ws(
+                xt.pointer, wt.pointer, yt.pointer, m, n, k, ws.pointer, need.value, ctx.stream)
+        else:
+            st = lib().mote_cuda_quantized_linear_q4_0_f16(xt.pointer, wt.pointer, yt.pointer,
+                                                           m, n, k, ctx.stream)
+        assert st == 0
+        outs.append(np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32)
+                    .reshape(m, n))
+    assert ctx.device_status() == 0
+    assert np.array_equal(outs[0], outs[1]) and not np.isnan(outs[0]).any()
+    ok, bad = checker.within_reference_tolerance(outs[0], outs[2], 0.01, 0.002)
+    assert ok, bad
+    rows = np.random.default_rng(1).choice(m, min(m, 48), replace=False)
+    ref = checker.linear_f64(x[rows].astype(np.float32), checker.q4_0_dequant_np(w, n, k))
+    assert checker.rel_err_normwise(outs[0][rows], ref) <= NORMWISE
+    assert checker.rel_err_elementwise(outs[0][rows], ref) <= ELEMENTWISE

@@ -124,10 +124,12 @@ int mote_cuda_quantized_linear_q4_0_f32(const void* input, const void* weights, 
  * tokens at K = 4096) and N has at most 4096 row tiles, K is split over 2 or
  * 4 CTAs whose partial sums
  * meet in the workspace (added in a fixed order: results do not depend on
- * timing).  A null or too small workspace gives the unsplit kernel.  Calls
- * sharing a workspace must not overlap.  No reference counterpart; argument
- * rules as mote_cuda_quantized_linear_q4_0_f16, plus an unaligned workspace
- * -> 1. */
+ * timing).  On the tensor-core path (more than 16 tokens), the tiles of a
+ * partial last wave are split along K instead, their f32 parts stored past
+ * the counters and added in part order by a second kernel.  A null or too
+ * small workspace gives the unsplit kernels.  Calls sharing a workspace must
+ * not overlap.  No reference counterpart; argument rules as
+ * mote_cuda_quantized_linear_q4_0_f16, plus an unaligned workspace -> 1. */
 int mote_cuda_quantized_linear_q4_0_f16_ws(const void* input, const void* weights, void* output,
                                            uint64_t rows, uint64_t output_features,
                                            uint64_t input_features, void* workspace,
@@ -146,7 +148,8 @@ int mote_cuda_quantized_linear_q4_0_f16_noalloc(const void* input, const void* w
                                                 void* output, uint64_t rows,
                                                 uint64_t output_features, uint64_t input_features,
                                                 void* stream);
-/* Workspace bytes that allow the widest split for these sizes (0: none). */
+/* Workspace bytes that allow the widest split for these sizes, on the
+ * current device (0: none). */
 int mote_cuda_q4_0_linear_workspace_bytes(uint64_t rows, uint64_t output_features,
                                           uint64_t input_features, uint64_t* bytes);
 

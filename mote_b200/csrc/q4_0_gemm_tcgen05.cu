@@ -20,9 +20,9 @@
 // * warp 17 allocates the TMEM columns and one thread issues
 //   tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) per 16-k step,
 //   accumulating in f32 in TMEM; tcgen05.commit releases the operand stages;
-// * after the last k-slice the first converter group reads the accumulator
-//   with tcgen05.ld (warp w owns TMEM lanes = features 32*(w%4).. and half of
-//   the token columns) and stores it: for each token, a warp writes 32
+// * after the last k-slice the converter warps read the accumulator with
+//   tcgen05.ld (warp w owns TMEM lanes = features 32*(w%4).. and a slice of
+//   the token columns) and store it: for each token, a warp writes 32
 //   consecutive features.
 // Stages are tracked with mbarriers; every wait is bounded and an expired
 // wait aborts the whole CTA (which still frees its TMEM).  No TMA load uses
@@ -442,17 +442,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 slice(std::integral_constant<int, 3>{});
             }
         }
-        // epilogue (group 0): warp w reads TMEM lanes (features) 32*(w%4)..
-        // and token columns (TT/2)*(w/4)..; for each token the warp stores
-        // 32 consecutive features
-        if (group == 0 && __all_sync(0xffffffffu, ok && wait_or_abort(accum, 0, abort_flag))) {
+        // epilogue: warp w reads TMEM lanes (features) 32*(w%4).. and a
+        // slice of kCols token columns (all converter warps for TT >= 128,
+        // group 0 for TT = 64: a TMEM load takes 32 columns); for each token
+        // the warp stores 32 consecutive features
+        constexpr int kEpiWarps = TT >= 128 ? kConvWarps : 8;
+        constexpr int kCols = TT / (kEpiWarps / 4);
+        if (warp < kEpiWarps &&
+            __all_sync(0xffffffffu, ok && wait_or_abort(accum, 0, abort_flag))) {
             tc_fence_after();
             const int lane_base = 32 * (warp % 4);
-            const int col_base = (TT / 2) * (warp / 4);
+            const int col_base = kCols * (warp / 4);
             const std::uint32_t n = n0 + lane_base + lane;
             const bool n_ok = n < p.N;
 #pragma unroll 1
-            for (int cb = 0; cb < TT / 2; cb += 32) {
+            for (int cb = 0; cb < kCols; cb += 32) {
                 std::uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem_d + (static_cast<std::uint32_t>(lane_base) << 16) +
                                        static_cast<std::uint32_t>(col_base + cb),

@@ -22,8 +22,8 @@
  * Stream overlap: kernels are launched with programmatic dependent launch,
  * so a kernel may begin while earlier kernels of this library on the stream
  * are still running; each waits for its predecessor to complete before it
- * touches activations or outputs.  The Q4_0 linears start streaming their
- * WEIGHTS before that wait (and mote_cuda_rms_norm_rope_f16 reads gamma and
+ * touches activations or outputs.  The Q4_0 and Q8_0 linears start streaming
+ * their WEIGHTS before that wait (and mote_cuda_rms_norm_rope_f16 reads gamma and
  * the cos/sin rows before it), so such parameters must not be written by
  * this library's kernels still in flight on its stream (parameters written by
  * a copy, by mote_cuda_q4_0_encode_f32 or by any kernel not from this
@@ -116,6 +116,21 @@ int mote_cuda_quantized_linear_q4_0_f16_f32out(const void* input, const void* we
 int mote_cuda_quantized_linear_q4_0_f32(const void* input, const void* weights, void* output,
                                         uint64_t rows, uint64_t output_features,
                                         uint64_t input_features, void* stream);
+
+/* Q8_0 weights (ggml blocks of 34 bytes: little-endian f16 scale d, then 32
+ * signed bytes; value = q * d), f16 input, f32 accumulation, f16 or f32
+ * output: the device counterpart of mote-reference's quantized_linear_f32
+ * for Q8_0 (crates/mote-reference/src/quantized.rs:89-144, decode :191-195).
+ * No HIP counterpart (the HIP backend has a Q4_0 linear only); argument
+ * rules as mote_cuda_quantized_linear_q4_0_f16.  A decode kernel: more than
+ * 16 tokens run as consecutive launches of 16. */
+int mote_cuda_quantized_linear_q8_0_f16(const void* input, const void* weights, void* output,
+                                        uint64_t rows, uint64_t output_features,
+                                        uint64_t input_features, void* stream);
+int mote_cuda_quantized_linear_q8_0_f16_f32out(const void* input, const void* weights,
+                                               void* output, uint64_t rows,
+                                               uint64_t output_features, uint64_t input_features,
+                                               void* stream);
 
 /* The f16 linear with a caller workspace (256-byte aligned, zeroed once
  * before first use; its first 256 KiB hold per-tile counters that every call

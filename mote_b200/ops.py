@@ -128,6 +128,47 @@ def quantized_linear_q4_0_f16(context: CudaContext, input: Tensor, weights: Tens
     quantized_linear_q4_0(context, input, weights, output, DType.F16, DType.F16)
 
 
+_Q8_0_SYMBOLS = {
+    (DType.F16, DType.F16): "mote_cuda_quantized_linear_q8_0_f16",
+    (DType.F16, DType.F32): "mote_cuda_quantized_linear_q8_0_f16_f32out",
+}
+
+
+def quantized_linear_q8_0(context: CudaContext, input: Tensor, weights: Tensor, output: Tensor,
+                          output_dtype: DType = DType.F16) -> None:
+    """``output = input @ weights^T`` with Q8_0 weights [N, K] (34-byte
+    blocks: f16 scale, 32 signed bytes), f16 input, f32 accumulation and an
+    f16 or f32 output -- the device counterpart of mote-reference's
+    ``quantized_linear_f32`` for Q8_0.  Same validation as the Q4_0 op."""
+    symbol = _Q8_0_SYMBOLS.get((DType.F16, output_dtype))
+    if symbol is None:
+        raise errors.DTypeMismatch(tensor="output", expected=DType.F16, actual=output_dtype)
+    _plain(input, "input", DType.F16)
+    _rank(input, "input", 2)
+    enc = weights.desc.encoding
+    if enc.quantized is not QuantFormat.Q8_0:
+        raise errors.UnsupportedEncoding(actual=enc)
+    _rank(weights, "weights", 2)
+    _plain(output, "output", output_dtype)
+    _rank(output, "output", 2)
+    rows, k = input.shape
+    n, wk = weights.shape
+    if wk != k:
+        raise errors.ShapeMismatch(tensor="weights", expected=(n, k), actual=weights.shape)
+    _shape(output, "output", (rows, n))
+    in_s, w_s, out_s = (context.storage(t) for t in (input, weights, output))
+    _not_aliased(output, "output", input, "input")
+    _not_aliased(output, "output", weights, "weights")
+    if rows * n > U32_MAX:
+        raise errors.QuantizedLinearDimensionsTooLarge(rows=rows, output_features=n,
+                                                       input_features=k)
+    if rows * n == 0:
+        return
+    context.inner.select()
+    errors.check(getattr(lib(), symbol)(in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k,
+                                        context.stream), "launch Q8_0 linear kernel")
+
+
 def quantized_linear_q4_0_f32(context: CudaContext, input: Tensor, weights: Tensor,
                               output: Tensor) -> None:
     """f32 in, f32 out (device counterpart of ``quantized_linear_f32``)."""

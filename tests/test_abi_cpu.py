@@ -187,3 +187,12 @@ def test_fused_norm_argument_rules(lib):
     assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 2, 1, 24, 256, eps, STREAM) == 1  # hd % 16
     assert qkv(FAKE, FAKE, FAKE, FAKE + 2, FAKE, FAKE, 1, 2, 1, 64, 256, eps, STREAM) == 1
     assert qkv(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 2, 1, 64, 256, eps, STREAM) == 0
+
+
+def test_q8_0_argument_rules(lib):
+    for fn in (lib.mote_cuda_quantized_linear_q8_0_f16, lib.mote_cuda_quantized_linear_q8_0_f16_f32out):
+        assert fn(None, FAKE, FAKE, 1, 8, 32, STREAM) == 1       # null input
+        assert fn(FAKE, FAKE, FAKE, 1, 8, 33, STREAM) == 1       # K % 32
+        assert fn(FAKE, FAKE, FAKE, 1, 8, 32, None) == 1         # null stream
+        assert fn(FAKE, FAKE, FAKE, 0, 8, 32, STREAM) == 0       # empty: no launch
+        assert fn(FAKE, FAKE, FAKE, 1 << 20, 1 << 13, 32, STREAM) == 9  # rows*N > u32

@@ -521,6 +521,42 @@ class Bench:
                                 "tflops": round(flops / ms / 1e9, 1)}
         return out
 
+    def q8_0(self) -> dict:
+        """The Q8_0 linear (next after the Q4_0 path): lm_head K=4096,
+        N=128256 at M in {1, 16} (558 MB of weights, no rotation needed) and
+        N=14336 at M=1 over copies holding >= 2.5x L2.  Weights are random
+        signed bytes with a fixed small f16 scale (timing only; parity is in
+        tests/test_gpu_q8_0.py)."""
+        torch = self.torch
+        fn = self.lib.mote_cuda_quantized_linear_q8_0_f16
+        k = 4096
+        out = {}
+        for n, ms in ((128256, (1, 16)), (14336, (1,))):
+            nb = n * (k // 32) * 34
+            g0 = torch.Generator(device=self.dev).manual_seed(n)
+            base = torch.randint(0, 256, (nb,), generator=g0, dtype=torch.uint8, device=self.dev)
+            blocks = base.view(n * (k // 32), 34)
+            blocks[:, 0] = 0
+            blocks[:, 1] = 0x20  # f16 scale bits 0x2000
+            ws = [base] + [base.clone() for _ in range(copies_for(nb) - 1)]
+            for m in ms:
+                x = self.randn((m, k), 70 + m, torch.float16)
+                y = torch.empty((m, n), dtype=torch.float16, device=self.dev)
+
+                def run(x=x, y=y, m=m, n=n, ws=ws):
+                    for w in ws:
+                        self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k,
+                                      self.stream()), "q8_0 linear")
+
+                g = self.graph(run)
+                t = self.time_graph(g, 10, len(ws)) / len(ws)
+                del g
+                b = nb + m * k * 2 + m * n * 2
+                out[f"m{m}_n{n}"] = {"us": round(t * 1e3, 2), "gbs": round(b / t / 1e6, 1),
+                                     "weight_bytes": nb, "copies": len(ws)}
+            del ws, base
+        return out
+
     def sharded_linear(self, n: int, ms_list, seed: int, k: int = 4096) -> dict:
         """A linear column-sharded over the ranks (strong scaling): per step
         each rank runs the Q4_0 linear on its rows [rank * shard, ...) and the
@@ -704,6 +740,7 @@ class Bench:
             extra["config2_rmsnorm_rope_t512"] = self.config2()
             extra["config4_decoder_layer_m1"] = self.config4()
             extra["config5"] = self.config5()
+            extra["q8_0_linear"] = self.q8_0()
         e2e = self.e2e(max(3, min(args.steps, 20)))
         if self.world > 1:
             # the splits the data plane supports: lm_head and FFN up/gate by

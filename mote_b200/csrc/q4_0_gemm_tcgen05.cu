@@ -1,4 +1,6 @@
-// Prefill-shaped Q4_0 GEMM on the 5th-generation tensor cores (tcgen05/TMEM).
+// Prefill-shaped Q4_0 (and Q8_0) GEMM on the 5th-generation tensor cores
+// (tcgen05/TMEM).  The kernel is written for Q4_0; with Q8 = true the raw
+// stages hold 272-byte Q8_0 rows and convert_block_q8 does the conversion.
 //
 //   Y[M, N] = X[M, K] * W[N, K]^T,  X f16, W ggml Q4_0 (18-byte blocks), Y f16/f32,
 //   for M large enough that the contraction, not the weight stream, bounds
@@ -51,8 +53,13 @@ constexpr int kSuperK = 256;             // k per raw weight stage (8 blocks, 14
 // N=14336, 8 converter warps).
 constexpr int kStages = 4;               // operand stages
 constexpr int kRawStages = 1;            // raw weight stages
-constexpr int kRawRowBytes = 144;
-constexpr int kRawBytes = kFT * kRawRowBytes;  // 18 KB
+// Raw weight rows of a 256-k stage: 8 Q4_0 blocks (144 bytes) or 8 Q8_0
+// blocks (272 bytes; its TMA box counts 2-byte elements, a box edge being
+// at most 256 elements).
+template <bool Q8>
+constexpr int kRawRowBytes = Q8 ? 272 : 144;
+template <bool Q8>
+constexpr int kRawBytes = kFT * kRawRowBytes<Q8>;  // 34 KB or 18 KB
 // Converter warps form kConvGroups groups of 8; group g converts the 64-k
 // slices kb with kb % kConvGroups == g, so each group has kConvGroups MMA
 // slices of time per slice it converts.
@@ -76,7 +83,7 @@ constexpr int pow2_at_least(int v) {
 // Shared-memory layout for a token tile of TT (64, 128 or 256) tokens = the
 // MMA's N and the accumulator's TMEM columns: activations TT x 64 k per
 // stage (B).
-template <int TT>
+template <int TT, bool Q8>
 struct Layout {
     static constexpr int kXBytes = TT * kBK * 2;
     static constexpr int kOffX = 0;
@@ -86,7 +93,7 @@ struct Layout {
     static constexpr int kAColBase = TT;
     static constexpr int kTmemCols = pow2_at_least(TT + kStages * 32);
     static_assert(kTmemCols <= 512, "tensor memory");
-    static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
+    static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes<Q8>;
     // barriers: x_full[S], w_full[S], empty[S], raw_full[R], raw_empty[R], accum
     static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
@@ -286,12 +293,52 @@ __device__ __forceinline__ void convert_half_slice(std::uint32_t raw_row, std::u
     store_block_tmem(o, taddr);
 }
 
-template <int TT, bool OF32>
+// Converts Q8_0 block 2*SUB + PAR of a 272-byte raw row (8 blocks of 34
+// bytes: f16 scale, 32 signed bytes) into the 16 TMEM columns at `taddr`:
+// q exactly as f16 ((q ^ 0x80) under the exponent of 1024, minus 1152),
+// then q * d rounded once.  The block spans at most three 16-byte chunks.
+template <int SUB, int PAR>
+__device__ __forceinline__ void convert_block_q8(std::uint32_t raw_row, std::uint32_t taddr) {
+    constexpr int kOff = 34 * (2 * SUB + PAR);
+    constexpr int kChunk0 = kOff / 16;
+    constexpr int kO = kOff % 16;  // even: the scale's byte offset in the loaded words
+    std::uint32_t w[12];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int chunk = kChunk0 + c < 17 ? kChunk0 + c : 16;  // never past the row
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                     : "r"(raw_row + chunk * 16));
+    }
+    const std::uint32_t dbits = (kO % 4 == 0) ? (w[kO / 4] & 0xFFFFu) : (w[kO / 4] >> 16);
+    const std::uint32_t d2 = dbits | (dbits << 16);
+    std::uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        constexpr int kQ = kO + 2;  // first quant byte
+        std::uint32_t q;
+        if constexpr (kQ % 4 == 0)
+            q = w[kQ / 4 + i];
+        else
+            q = prmt(w[kQ / 4 + i], w[kQ / 4 + i + 1], 0x5432u);
+        const std::uint32_t v = q ^ 0x80808080u;  // q + 128 per byte
+        std::uint32_t lo, hi;
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(prmt(v, 0x64646464u, 0x4140u)), "r"(0x64806480u));
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(prmt(v, 0x64646464u, 0x4342u)), "r"(0x64806480u));
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[2 * i]) : "r"(lo), "r"(d2));
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[2 * i + 1]) : "r"(hi), "r"(d2));
+    }
+    store_block_tmem(o, taddr);
+}
+
+template <int TT, bool OF32, bool Q8>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
                              const __grid_constant__ CUtensorMap map_w, const Params p) {
-    using L = Layout<TT>;
+    using L = Layout<TT, Q8>;
     constexpr int kOffX = L::kOffX, kOffRaw = L::kOffRaw, kOffBar = L::kOffBar;
+    constexpr int kRawRow = kRawRowBytes<Q8>;
+    constexpr int kRaw = kRawBytes<Q8>;
     constexpr int kOffTmemSlot = L::kOffTmemSlot, kOffAbort = L::kOffAbort;
     constexpr int kXBytes = L::kXBytes;
     extern __shared__ std::uint8_t smem_raw[];
@@ -355,9 +402,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (sb >= kRawStages &&
                         !wait_or_abort(&raw_empty[r], ((sb / kRawStages) - 1) & 1u, abort_flag))
                         break;
-                    mbar_arrive_expect_tx(&raw_full[r], kRawBytes);
-                    tma_load_2d(base + kOffRaw + r * kRawBytes, &map_w,
-                                static_cast<int>((kb0 / (kSuperK / kBK) + sb) * kRawRowBytes),
+                    mbar_arrive_expect_tx(&raw_full[r], kRaw);
+                    // x in the map's elements: bytes (Q4_0) or 2-byte units (Q8_0)
+                    tma_load_2d(base + kOffRaw + r * kRaw, &map_w,
+                                static_cast<int>((kb0 / (kSuperK / kBK) + sb) * kRawRow /
+                                                 (Q8 ? 2 : 1)),
                                 static_cast<int>(n0), smem_u32(&raw_full[r]));
                 }
                 mbar_arrive_expect_tx(&x_full[s], kXBytes);
@@ -401,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int r = sb % kRawStages;
             ok = __all_sync(0xffffffffu, wait_or_abort(&raw_full[r], (sb / kRawStages) & 1u,
                                                        abort_flag));
-            const std::uint32_t raw_row = base + kOffRaw + r * kRawBytes + row * kRawRowBytes;
+            const std::uint32_t raw_row = base + kOffRaw + r * kRaw + row * kRawRow;
             auto slice = [&](auto sub_tag) {
                 constexpr int SUB = decltype(sub_tag)::value;
                 const std::uint32_t kb = sb * (kSuperK / kBK) + SUB;
@@ -414,10 +463,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const std::uint32_t ta = tmem_d + (static_cast<std::uint32_t>(32 * (warp % 4)) << 16) +
                                          static_cast<std::uint32_t>(L::kAColBase + s * 32 +
                                                                     (odd ? 16 : 0));
-                if (odd)  // warp-uniform
-                    convert_half_slice<SUB, 1>(raw_row, ta);
-                else
-                    convert_half_slice<SUB, 0>(raw_row, ta);
+                if constexpr (Q8) {
+                    if (odd)  // warp-uniform
+                        convert_block_q8<SUB, 1>(raw_row, ta);
+                    else
+                        convert_block_q8<SUB, 0>(raw_row, ta);
+                } else {
+                    if (odd)  // warp-uniform
+                        convert_half_slice<SUB, 1>(raw_row, ta);
+                    else
+                        convert_half_slice<SUB, 0>(raw_row, ta);
+                }
                 // the TMEM stores complete before the MMA warp is told
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
@@ -600,11 +656,11 @@ int ctas_per_sm(Kernel kernel, int smem, std::atomic<int> (&cache)[64], int dev)
     return v;
 }
 
-template <int TT, bool OF32>
+template <int TT, bool OF32, bool Q8>
 int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
                 std::uint64_t K, cudaStream_t stream, void* workspace,
                 std::uint64_t workspace_bytes) {
-    using L = Layout<TT>;
+    using L = Layout<TT, Q8>;
     auto encode = encode_fn();
     if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
     CUtensorMap map_x{}, map_w{};
@@ -620,18 +676,22 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
             return static_cast<int>(cudaErrorInvalidValue);
     }
     {
-        const std::uint64_t pitch = (K / 32) * 18;
-        const cuuint64_t dims[2] = {pitch, N};
+        // Q4_0 rows as bytes; Q8_0 rows as 2-byte units (a 272-byte box edge
+        // is over the 256-element limit); both pitches are multiples of 16
+        const std::uint64_t pitch = (K / 32) * (Q8 ? 34 : 18);
+        const std::uint64_t esize = Q8 ? 2 : 1;
+        const cuuint64_t dims[2] = {pitch / esize, N};
         const cuuint64_t strides[1] = {pitch};
-        const cuuint32_t box[2] = {kRawRowBytes, kFT};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRowBytes<Q8> / esize), kFT};
         const cuuint32_t estr[2] = {1, 1};
-        if (encode(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides,
+        if (encode(&map_w, Q8 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                   const_cast<void*>(w), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return static_cast<int>(cudaErrorInvalidValue);
     }
-    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32>;
+    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32, Q8>;
     static std::atomic<std::uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -693,15 +753,16 @@ inline std::uint64_t split_workspace_bytes(std::uint64_t M, std::uint64_t N, std
 
 // Token tile: the narrowest of 64 / 128 / 256 that holds M (wider tiles
 // waste MMA columns on missing tokens), 256 beyond.
-template <bool OF32>
+// Q8 selects Q8_0 weights instead of Q4_0.
+template <bool OF32, bool Q8 = false>
 int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
            std::uint64_t K, cudaStream_t stream, void* workspace = nullptr,
            std::uint64_t workspace_bytes = 0) {
     if (M <= 64)
-        return launch_tile<64, OF32>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+        return launch_tile<64, OF32, Q8>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
     if (M <= 128)
-        return launch_tile<128, OF32>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
-    return launch_tile<256, OF32>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+        return launch_tile<128, OF32, Q8>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+    return launch_tile<256, OF32, Q8>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
 }
 
 }  // namespace gemm

@@ -21,9 +21,10 @@
 //   subtraction of 1152 gives q;
 // * mma.sync.m16n8k16 (f16 x f16 -> f32) per 16-k step, with the 8 columns
 //   the tokens; each block's partial is scaled by its row's f32 d.
-// More than 16 tokens run as consecutive launches of up to 16.  Shapes the
-// fast path does not take (K % 256 != 0, unaligned pointers) run a plain
-// warp-per-row kernel.
+// More than 16 tokens run on the tcgen05 GEMM (q4_0_gemm_tcgen05.cu, Q8_0
+// conversion) when N % 16 == 0, K % 256 == 0 and the pointers are aligned,
+// else as consecutive launches of up to 16.  Shapes the fast path does not
+// take (K % 256 != 0, unaligned pointers) run a plain warp-per-row kernel.
 
 namespace mote {
 namespace q8 {
@@ -359,6 +360,9 @@ int run_linear8(const void* x, const void* w, void* y, std::uint64_t M, std::uin
     const std::size_t osz = OF32 ? 4 : 2;
     if (K == 0)  // every dot product is empty: zeros, as the reference
         return static_cast<int>(cudaMemsetAsync(y, 0, M * N * osz, stream));
+    // prefill-shaped problems: the tcgen05 GEMM with Q8_0 conversion
+    if (M > static_cast<std::uint64_t>(kMaxTokens) && gemm::supported(x, w, y, M, N, K, osz))
+        return gemm::launch<OF32, true>(x, w, y, M, N, K, stream);
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
     p.N = static_cast<std::uint32_t>(N);

@@ -894,6 +894,7 @@ def run_single_case(args) -> None:
     """One kernel, a few plain launches (no graph): the command ncu profiles.
 
     --only gemv       Q4_0 linear f16 -> f16, [--m, --n, --k]
+    --only q8_0       Q8_0 linear f16 -> f16, [--m, --n, --k]
     --only norm_rope  fused RMSNorm + RoPE at config-2 geometry
     """
     import torch
@@ -911,6 +912,21 @@ def run_single_case(args) -> None:
             b.check(b.lib.mote_cuda_quantized_linear_q4_0_f16(
                 x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "gemv")
         nbytes = linear_bytes(m, n, k)
+    elif args.only == "q8_0":
+        m, n, k = args.m, args.n, args.k
+        nb = n * (k // 32) * 34
+        g0 = torch.Generator(device=b.dev).manual_seed(1)
+        w = torch.randint(0, 256, (nb,), generator=g0, dtype=torch.uint8, device=b.dev)
+        blocks = w.view(n * (k // 32), 34)
+        blocks[:, 0] = 0
+        blocks[:, 1] = 0x20  # f16 scale bits 0x2000
+        x = b.randn((m, k), 2, torch.float16)
+        y = torch.empty((m, n), dtype=torch.float16, device=b.dev)
+
+        def launch():
+            b.check(b.lib.mote_cuda_quantized_linear_q8_0_f16(
+                x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "q8_0")
+        nbytes = nb + m * k * 2 + m * n * 2
     elif args.only == "norm_rope":
         t, hidden, qh, kh, hd = 512, 2048, 32, 8, 64
         pos = torch.arange(t, dtype=torch.int32, device=b.dev)
@@ -949,7 +965,7 @@ def run_single_case(args) -> None:
 
 def main() -> int:
     p = argparse.ArgumentParser()
-    p.add_argument("--only", default=None, help="profile one kernel: gemv | norm_rope")
+    p.add_argument("--only", default=None, help="profile one kernel: gemv | q8_0 | norm_rope")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=128256)
     p.add_argument("--k", type=int, default=4096)

@@ -561,7 +561,7 @@ class Bench:
         """A linear column-sharded over the ranks (strong scaling): per step
         each rank runs the Q4_0 linear on its rows [rank * shard, ...) and the
         f16 outputs are all-gathered -- with NCCL (mote_cuda_comm_*), with the
-        peer-store kernel, and (<= 16 tokens) fused into the GEMV epilogue
+        peer-store kernel, and fused into the GEMV or tcgen05 GEMM epilogue
         (stores into every rank's [M, N] output over NVLink + flag
         handshake).  Steps are captured in CUDA graphs; times are the max over
         ranks; GB/s counts the full weight once per step, TFLOP/s 2 M N K.  A
@@ -593,8 +593,7 @@ class Bench:
                 count = m * sh.rows
                 recv = torch.empty(self.world * count, dtype=torch.float16, device=self.dev)
                 peer = comm.PeerAllGather(self.world, self.rank, count, exchange)
-                fused = comm.ShardedLinearQ4_0(self.world, self.rank, m, n, k, exchange) \
-                    if m <= 16 else None
+                fused = comm.ShardedLinearQ4_0(self.world, self.rank, m, n, k, exchange)
 
                 def linear(i, x=x, y=y, m=m):
                     self.check(fn(x.data_ptr(), ws[i % len(ws)].data_ptr(), y.data_ptr(), m,
@@ -619,11 +618,10 @@ class Bench:
                         fused(x.data_ptr(), ws[i % len(ws)].data_ptr(), i % 2, self.stream())
 
                 row = {}
-                # the fused epilogue is the decode path (GEMV, <= 16 tokens a
-                # launch); larger M runs the tcgen05 GEMM and a separate gather
-                arms = [("gemv", run_gemv, 1), ("nccl", run_nccl, 1), ("p2p", run_p2p, 2)]
-                if m <= 16:
-                    arms.append(("fused", run_fused, 1))
+                # fused: the GEMV (<= 16 tokens) or the tcgen05 GEMM with the
+                # peer-store epilogue and the handshake, one kernel per step
+                arms = [("gemv", run_gemv, 1), ("nccl", run_nccl, 1), ("p2p", run_p2p, 2),
+                        ("fused", run_fused, 1)]
                 for name, body, kernels in arms:
                     self.barrier()
                     g = self.graph(body)
@@ -638,8 +636,7 @@ class Bench:
                 result[f"m{m}"] = row
                 self.barrier()
                 peer.close(barrier=self.barrier)
-                if fused is not None:
-                    fused.close(barrier=self.barrier)
+                fused.close(barrier=self.barrier)
                 del recv, y
         finally:
             torch.cuda.synchronize()

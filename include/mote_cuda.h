@@ -322,7 +322,10 @@ int mote_cuda_all_gather_p2p_f16(const void* send, void* const* recv_ptrs,
  * buffer [rows, total_features] at columns rank*shard.. (outputs: DEVICE
  * array of nranks pointers, peers mapped over CUDA IPC), then the flag
  * handshake of mote_cuda_all_gather_p2p_f16 runs at the end of the grid, so
- * when the launch completes every rank holds all columns.  shard % 16 == 0,
+ * when the launch completes every rank holds all columns.  More than 16
+ * tokens run on the tensor-core GEMM with the same epilogue and handshake
+ * (a rank whose shard has no real rows only joins the handshake).
+ * shard % 16 == 0,
  * total_features % 8 == 0, K % 256 == 0 and K > 0, 16-byte aligned input,
  * weights and output buffers; every rank
  * passes the same rows (rows == 0 returns 0 without a launch on all ranks).

@@ -121,7 +121,50 @@ struct Params {
     std::uint32_t full;     // CTAs that compute a whole tile
     std::uint32_t parts;    // K parts of a split tile (1: no split)
     float* part_buf;
+    // Column-sharded linear with the all-gather fused (PEERS kernels): this
+    // rank's f16 results go to every rank's [M, ldy] output at columns
+    // col0 + n, then the grid ends with the flag handshake (flag array per
+    // rank: [q] epoch of rank q, [nranks] arrival counter, [nranks + 1] own
+    // epoch).
+    __half* const* peer_y;
+    unsigned* const* peer_flags;
+    unsigned* own_flags;
+    std::uint64_t col0;
+    std::uint32_t rank;
+    std::uint32_t nranks;
 };
+
+// End of a PEERS grid, thread 0 of every CTA after a CTA barrier: one
+// cumulative system fence publishes the CTA's peer stores before its arrival
+// is counted; the last CTA advances this rank's epoch, stores it to every
+// rank's flags (fence + strong relaxed stores: a release pattern) and waits,
+// bounded, until every rank's epoch has arrived.
+__device__ __forceinline__ void peer_grid_handshake(const Params& p) {
+    __threadfence_system();
+    const unsigned arrived = atomicAdd(&p.own_flags[p.nranks], 1u);
+    if (arrived != gridDim.x - 1) return;
+    p.own_flags[p.nranks] = 0u;
+    const unsigned epoch = p.own_flags[p.nranks + 1] + 1u;
+    p.own_flags[p.nranks + 1] = epoch;
+    __threadfence_system();
+    for (std::uint32_t q = 0; q < p.nranks; ++q)
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q] + p.rank),
+                     "r"(epoch)
+                     : "memory");
+    const long long start = clock64();
+    for (std::uint32_t q = 0; q < p.nranks; ++q) {
+        for (;;) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.own_flags + q)
+                         : "memory");
+            if (static_cast<int>(v - epoch) >= 0) break;
+            if (clock64() - start > kWaitCycles) {
+                atomicOr(&g_device_status, kDevWaitTimeout);
+                return;
+            }
+        }
+    }
+}
 
 // ---- PTX wrappers ------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(std::uint32_t dst, const CUtensorMap* map, int x,
@@ -331,7 +374,7 @@ __device__ __forceinline__ void convert_block_q8(std::uint32_t raw_row, std::uin
     store_block_tmem(o, taddr);
 }
 
-template <int TT, bool OF32, bool Q8>
+template <int TT, bool OF32, bool Q8, bool PEERS>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
                              const __grid_constant__ CUtensorMap map_w, const Params p) {
@@ -528,15 +571,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                     continue;
                 }
                 const std::uint32_t mb = m0 + col_base + cb;
+                if constexpr (PEERS) {
+                    // every rank's output, columns col0 + n (over NVLink for the
+                    // peers), in 16-byte vectors: the warp's 32 features x 32
+                    // tokens are transposed through 2 KB of the (drained)
+                    // activation stages, then each lane stores 8 features of a
+                    // token per vector.  Real rows come in whole groups of 8
+                    // (shard % 16 == 0, total % 8 == 0).
+                    __half* tr = reinterpret_cast<__half*>(smem + kOffX) + warp * 32 * 32;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const std::uint32_t m = mb + i;
-                    if (n_ok && m < p.M) {
-                        if constexpr (OF32)
-                            static_cast<float*>(p.y)[m * p.ldy + n] = __uint_as_float(v[i]);
-                        else
-                            static_cast<__half*>(p.y)[m * p.ldy + n] =
-                                __float2half_rn(__uint_as_float(v[i]));
+                    for (int i = 0; i < 32; ++i) tr[i * 32 + lane] = __float2half_rn(__uint_as_float(v[i]));
+                    __syncwarp();
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const int c = lane + 32 * c4;
+                        const int i = c >> 2;          // token within the chunk
+                        const int f = (c & 3) * 8;     // first of 8 features
+                        const std::uint32_t nf = n0 + lane_base + f;
+                        if (mb + i < p.M && nf < p.N) {
+                            const uint4 vec = *reinterpret_cast<const uint4*>(tr + i * 32 + f);
+                            const std::uint64_t at =
+                                static_cast<std::uint64_t>(mb + i) * p.ldy + p.col0 + nf;
+                            for (std::uint32_t r = 0; r < p.nranks; ++r)
+                                *reinterpret_cast<uint4*>(p.peer_y[r] + at) = vec;
+                        }
+                    }
+                    __syncwarp();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const std::uint32_t m = mb + i;
+                        if (n_ok && m < p.M) {
+                            if constexpr (OF32)
+                                static_cast<float*>(p.y)[m * p.ldy + n] = __uint_as_float(v[i]);
+                            else
+                                static_cast<__half*>(p.y)[m * p.ldy + n] =
+                                    __float2half_rn(__uint_as_float(v[i]));
+                        }
                     }
                 }
             }
@@ -547,6 +618,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_d, kTmemCols);
+    }
+    if constexpr (PEERS) {
+        if (threadIdx.x == 0) peer_grid_handshake(p);
     }
 }
 
@@ -656,10 +730,20 @@ int ctas_per_sm(Kernel kernel, int smem, std::atomic<int> (&cache)[64], int dev)
     return v;
 }
 
-template <int TT, bool OF32, bool Q8>
+// Fused all-gather destinations of a column-sharded linear (PEERS).
+struct Peers {
+    __half* const* outputs;   // device array of nranks [M, ldy] f16 buffers
+    unsigned* const* flags;   // device array of the ranks' flag arrays
+    unsigned* own_flags;
+    std::uint64_t col0;       // this rank's first column
+    std::uint64_t ldy;        // total columns
+    std::uint32_t rank, nranks;
+};
+
+template <int TT, bool OF32, bool Q8, bool PEERS = false>
 int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
                 std::uint64_t K, cudaStream_t stream, void* workspace,
-                std::uint64_t workspace_bytes) {
+                std::uint64_t workspace_bytes, const Peers* peers = nullptr) {
     using L = Layout<TT, Q8>;
     auto encode = encode_fn();
     if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
@@ -691,7 +775,7 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return static_cast<int>(cudaErrorInvalidValue);
     }
-    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32, Q8>;
+    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32, Q8, PEERS>;
     static std::atomic<std::uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -707,7 +791,7 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
     const std::uint64_t tiles = tiles_n * ((M + TT - 1) / TT);
     SplitPlan sp;
     sp.full = static_cast<std::uint32_t>(tiles);
-    if (workspace != nullptr && reinterpret_cast<std::uintptr_t>(workspace) % 16 == 0) {
+    if (!PEERS && workspace != nullptr && reinterpret_cast<std::uintptr_t>(workspace) % 16 == 0) {
         static std::atomic<int> occ[64];
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -717,16 +801,27 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
             static_cast<std::uint64_t>(sms) * ctas_per_sm(kernel, L::kSmemBytes, occ, dev));
         if (cand.parts > 1 && cand.bytes <= workspace_bytes) sp = cand;
     }
-    Params p{y,
-             static_cast<std::uint32_t>(M),
-             static_cast<std::uint32_t>(N),
-             static_cast<std::uint32_t>(K),
-             N,
-             static_cast<std::uint32_t>(tiles_n),
-             sp.full,
-             sp.parts,
-             static_cast<float*>(workspace)};
-    const unsigned grid = sp.full + sp.split_tiles * sp.parts;
+    Params p{};
+    p.y = y;
+    p.M = static_cast<std::uint32_t>(M);
+    p.N = static_cast<std::uint32_t>(N);
+    p.K = static_cast<std::uint32_t>(K);
+    p.ldy = N;
+    p.tiles_n = static_cast<std::uint32_t>(tiles_n);
+    p.full = sp.full;
+    p.parts = sp.parts;
+    p.part_buf = static_cast<float*>(workspace);
+    if constexpr (PEERS) {
+        p.peer_y = peers->outputs;
+        p.peer_flags = peers->flags;
+        p.own_flags = peers->own_flags;
+        p.col0 = peers->col0;
+        p.ldy = peers->ldy;
+        p.rank = peers->rank;
+        p.nranks = peers->nranks;
+    }
+    unsigned grid = sp.full + sp.split_tiles * sp.parts;
+    if (PEERS && grid == 0) grid = 1;  // every rank joins the handshake
     kernel<<<grid, kThreads, L::kSmemBytes, stream>>>(map_x, map_w, p);
     e = cudaGetLastError();
     if (e != cudaSuccess || sp.parts == 1) return static_cast<int>(e);
@@ -753,6 +848,35 @@ inline std::uint64_t split_workspace_bytes(std::uint64_t M, std::uint64_t N, std
 
 // Token tile: the narrowest of 64 / 128 / 256 that holds M (wider tiles
 // waste MMA columns on missing tokens), 256 beyond.
+// A rank whose shard has no real rows still takes part in the handshake.
+__global__ void peer_handshake_only_kernel(const Params p) {
+    if (threadIdx.x == 0) peer_grid_handshake(p);
+}
+
+inline int launch_handshake_only(const Peers& peers, cudaStream_t stream) {
+    Params p{};
+    p.peer_flags = peers.flags;
+    p.own_flags = peers.own_flags;
+    p.rank = peers.rank;
+    p.nranks = peers.nranks;
+    peer_handshake_only_kernel<<<1, 32, 0, stream>>>(p);
+    return static_cast<int>(cudaGetLastError());
+}
+
+// The column-sharded Q4_0 linear with the all-gather fused into the
+// epilogue (see Peers), for more than 16 tokens: N = this rank's real rows.
+inline int launch_peers(const void* x, const void* w, std::uint64_t M, std::uint64_t N,
+                        std::uint64_t K, const Peers& peers, cudaStream_t stream) {
+    if (M <= 64)
+        return launch_tile<64, false, false, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
+                                                   &peers);
+    if (M <= 128)
+        return launch_tile<128, false, false, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
+                                                    &peers);
+    return launch_tile<256, false, false, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
+                                                &peers);
+}
+
 // Q8 selects Q8_0 weights instead of Q4_0.
 template <bool OF32, bool Q8 = false>
 int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,

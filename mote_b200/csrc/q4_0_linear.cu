@@ -1129,6 +1129,18 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
         fast = plan_gemv(M, K, XF32, EPI == kEpiPeers, tokens, nt, stages, ctas, p.x_rows,
                          p.x_stride, p.x_bytes);
     if (kFastOnly && !fast) return kInvalidValue;
+    if constexpr (EPI == kEpiPeers) {
+        // More than 16 tokens: the tcgen05 GEMM with the peer-store epilogue
+        // and one handshake per call on every rank (the token count is the
+        // same on every rank; a rank without real rows only joins the
+        // handshake).
+        if (M > static_cast<std::uint64_t>(kMaxXRows)) {
+            const gemm::Peers gp{p.peer_y, p.peer_flags, p.own_flags, p.col0, ldy,
+                                 p.rank,   p.nranks};
+            if (N == 0) return gemm::launch_handshake_only(gp, stream);
+            return gemm::launch_peers(x, w, M, N, K, gp, stream);
+        }
+    }
     p.parts = 1;
     // With a workspace, when the staged activations leave room for only one
     // CTA per SM, split K over 2 or 4 CTAs: each stages its part's columns

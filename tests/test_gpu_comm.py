@@ -5,7 +5,8 @@ linear + all-gather equals the plain GEMV bit for bit, and CUDA graphs
 replaying the peer kernels check that the device-side epoch advances); the
 two-rank test needs two GPUs and runs each rank as a spawned process: both
 ranks compute their shard of a Q4_0 linear with the GEMV kernel, gather it
-with NCCL and with peer stores and also run the fused linear + all-gather;
+with NCCL and with peer stores and also run the fused linear + all-gather
+(on the tcgen05 GEMM for 40 tokens, rank 1 with a ragged 488-row shard);
 rank 0 compares the logits with the CPU oracle (reference tolerance abs 0.01
 / rel 0.002 on the f16 outputs) and the two gather transports with each
 other (bit-identical).
@@ -77,7 +78,10 @@ def test_peer_world1_graph_replays(stream):
         g.close()
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 1000, 512), (5, 2048, 2048), (16, 296, 4096)])
+# 1-16 tokens: the GEMV with the peer epilogue; more (N % 16 == 0): the
+# tcgen05 GEMM with the peer epilogue against the plain tcgen05 GEMM
+@pytest.mark.parametrize("m,n,k", [(1, 1000, 512), (5, 2048, 2048), (16, 296, 4096),
+                                   (40, 1024, 512), (300, 2048, 1024)])
 def test_fused_world1_equals_plain_gemv(stream, oracle_lib, m, n, k):
     from tests import _fixtures as fx
 
@@ -195,7 +199,7 @@ def _rank_main(rank: int, world: int, port: int, m: int, n: int, k: int, out_dir
 
 @pytest.mark.timeout(300)
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("m", [1, 4])
+@pytest.mark.parametrize("m", [1, 4, 40])
 def test_two_rank_sharded_linear(tmp_path, m):
     import torch.multiprocessing as mp
 

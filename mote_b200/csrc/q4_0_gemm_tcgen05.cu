@@ -571,13 +571,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     continue;
                 }
                 const std::uint32_t mb = m0 + col_base + cb;
-                if constexpr (PEERS) {
-                    // every rank's output, columns col0 + n (over NVLink for the
-                    // peers), in 16-byte vectors: the warp's 32 features x 32
+                if constexpr (PEERS || !OF32) {
+                    // f16 out in 16-byte vectors: the warp's 32 features x 32
                     // tokens are transposed through 2 KB of the (drained)
                     // activation stages, then each lane stores 8 features of a
-                    // token per vector.  Real rows come in whole groups of 8
-                    // (shard % 16 == 0, total % 8 == 0).
+                    // token per vector -- to this GPU's output, or (PEERS) to
+                    // every rank's output at columns col0 + n, over NVLink for
+                    // the peers.  Rows come in whole groups of 8 (N % 16 == 0 on
+                    // the plain path; shard % 16 == 0 and total % 8 == 0 with
+                    // PEERS).
                     __half* tr = reinterpret_cast<__half*>(smem + kOffX) + warp * 32 * 32;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) tr[i * 32 + lane] = __float2half_rn(__uint_as_float(v[i]));
@@ -592,22 +594,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint4 vec = *reinterpret_cast<const uint4*>(tr + i * 32 + f);
                             const std::uint64_t at =
                                 static_cast<std::uint64_t>(mb + i) * p.ldy + p.col0 + nf;
-                            for (std::uint32_t r = 0; r < p.nranks; ++r)
-                                *reinterpret_cast<uint4*>(p.peer_y[r] + at) = vec;
+                            if constexpr (PEERS) {
+                                for (std::uint32_t r = 0; r < p.nranks; ++r)
+                                    *reinterpret_cast<uint4*>(p.peer_y[r] + at) = vec;
+                            } else {
+                                *reinterpret_cast<uint4*>(static_cast<__half*>(p.y) + at) = vec;
+                            }
                         }
                     }
                     __syncwarp();
-                } else {
+                } else {  // f32 out: for each token the warp stores 32 features
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const std::uint32_t m = mb + i;
-                        if (n_ok && m < p.M) {
-                            if constexpr (OF32)
-                                static_cast<float*>(p.y)[m * p.ldy + n] = __uint_as_float(v[i]);
-                            else
-                                static_cast<__half*>(p.y)[m * p.ldy + n] =
-                                    __float2half_rn(__uint_as_float(v[i]));
-                        }
+                        if (n_ok && m < p.M)
+                            static_cast<float*>(p.y)[m * p.ldy + n] = __uint_as_float(v[i]);
                     }
                 }
             }

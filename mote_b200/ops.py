@@ -86,7 +86,9 @@ def quantized_linear_q4_0(context: CudaContext, input: Tensor, weights: Tensor, 
     storage with either input.  Validated empty outputs return without a
     launch.
     """
-    symbol = _LINEAR_SYMBOLS.get((input_dtype, output_dtype))
+    f16 = input_dtype is DType.F16 and output_dtype is DType.F16  # the common case
+    symbol = _LINEAR_SYMBOLS[(DType.F16, DType.F16)] if f16 else \
+        _LINEAR_SYMBOLS.get((input_dtype, output_dtype))
     if symbol is None:
         raise errors.DTypeMismatch(tensor="output", expected=DType.F16, actual=output_dtype)
     _plain(input, "input", input_dtype)
@@ -110,13 +112,15 @@ def quantized_linear_q4_0(context: CudaContext, input: Tensor, weights: Tensor, 
     if rows * n == 0:
         return
     context.inner.select()
-    if (input_dtype, output_dtype) == (DType.F16, DType.F16):
-        # the split-K path, with the context's workspace
+    if f16:
+        # the workspace entry (split-K decode, split last wave on tcgen05)
         need = context.linear_workspace_bytes(rows, n, k)
         ws_ptr, ws_bytes = context.linear_workspace(need) if need else (None, 0)
-        errors.check(lib().mote_cuda_quantized_linear_q4_0_f16_ws(
+        st = lib().mote_cuda_quantized_linear_q4_0_f16_ws(
             in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k, ws_ptr, ws_bytes,
-            context.stream), "launch Q4_0 linear kernel")
+            context.inner.stream)
+        if st:
+            errors.check(st, "launch Q4_0 linear kernel")
         return
     errors.check(getattr(lib(), symbol)(in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k,
                                         context.stream), "launch Q4_0 linear kernel")

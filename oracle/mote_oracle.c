@@ -504,3 +504,97 @@ int oracle_rope_cos_sin_f64(const int32_t* positions, size_t tokens, size_t rota
     }
     return ORACLE_OK;
 }
+
+/* ------------------------------------------------------------------------ */
+/* K-quants: ggml's published dequantization (gguf 0.19.0, gguf/quants.py)   */
+/* ------------------------------------------------------------------------ */
+
+/* The 6-bit scale and min of sub-block j (0..7) from the 12 packed bytes:
+ * bytes 0-3 hold scales 0-3 (low 6 bits) and the top bits of scales 4-7,
+ * bytes 4-7 mins 0-3 and the top bits of mins 4-7, bytes 8-11 the low four
+ * bits of scales 4-7 (low nibble) and mins 4-7 (high nibble). */
+static void q4_k_scale_min(const uint8_t* s, int j, uint8_t* sc, uint8_t* m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+        *m = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+    }
+}
+
+/* Q4_K block (144 bytes): f16 d, f16 dmin, 12 scale bytes, 128 quant bytes.
+ * Quant byte l of 32-byte group c holds element 64c + l (low nibble) and
+ * element 64c + 32 + l (high nibble). */
+static void decode_q4_k_block(const uint8_t* b, float* y) {
+    const float d = oracle_f16_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    const float dmin = oracle_f16_to_f32((uint16_t)(b[2] | (b[3] << 8)));
+    const uint8_t* scales = b + 4;
+    const uint8_t* qs = b + 16;
+    for (int c = 0; c < 4; c++) {
+        uint8_t sc0, m0, sc1, m1;
+        q4_k_scale_min(scales, 2 * c, &sc0, &m0);
+        q4_k_scale_min(scales, 2 * c + 1, &sc1, &m1);
+        const float d0 = d * (float)sc0, dm0 = dmin * (float)m0;
+        const float d1 = d * (float)sc1, dm1 = dmin * (float)m1;
+        for (int l = 0; l < 32; l++) {
+            y[64 * c + l] = d0 * (float)(qs[32 * c + l] & 0x0F) - dm0;
+            y[64 * c + 32 + l] = d1 * (float)(qs[32 * c + l] >> 4) - dm1;
+        }
+    }
+}
+
+/* Q6_K block (210 bytes): 128 bytes of low nibbles, 64 bytes of 2-bit high
+ * parts, 16 int8 scales (one per 16 elements), f16 d.  In half h (128
+ * elements), element e takes nibble (e / 64) of low byte 64h + e % 64 and
+ * bit pair (e / 32) of high byte 32h + e % 32; q = that 6-bit value - 32. */
+static void decode_q6_k_block(const uint8_t* b, float* y) {
+    const uint8_t* ql = b;
+    const uint8_t* qh = b + 128;
+    const int8_t* sc = (const int8_t*)(b + 192);
+    const float d = oracle_f16_to_f32((uint16_t)(b[208] | (b[209] << 8)));
+    for (int h = 0; h < 2; h++) {
+        for (int e = 0; e < 128; e++) {
+            const uint8_t lo = (uint8_t)((ql[64 * h + (e % 64)] >> (4 * (e / 64))) & 0x0F);
+            const uint8_t hi = (uint8_t)((qh[32 * h + (e % 32)] >> (2 * (e / 32))) & 0x03);
+            const int q = (int)(lo | (hi << 4)) - 32;
+            const int idx = 128 * h + e;
+            y[idx] = (d * (float)sc[idx / 16]) * (float)q;
+        }
+    }
+}
+
+int oracle_kquant_dequantize_row(const uint8_t* bytes, size_t bytes_len, int format,
+                                 size_t row_elements, float* output) {
+    if (format != ORACLE_Q4_K && format != ORACLE_Q6_K) return ORACLE_QL_UNSUPPORTED_FORMAT;
+    if (row_elements % 256 != 0) return ORACLE_QL_ROW_MISALIGNED;
+    const size_t bb = oracle_block_bytes(format);
+    if (bytes_len != row_elements / 256 * bb) return ORACLE_QL_ROW_BYTE_LENGTH_MISMATCH;
+    for (size_t blk = 0; blk < row_elements / 256; blk++) {
+        if (format == ORACLE_Q4_K)
+            decode_q4_k_block(bytes + blk * bb, output + blk * 256);
+        else
+            decode_q6_k_block(bytes + blk * bb, output + blk * 256);
+    }
+    return ORACLE_OK;
+}
+
+int oracle_kquant_linear_f64(const float* input, const uint8_t* weights, int format, size_t rows,
+                             size_t n, size_t k, double* output) {
+    if (format != ORACLE_Q4_K && format != ORACLE_Q6_K) return ORACLE_QL_UNSUPPORTED_FORMAT;
+    if (k % 256 != 0) return ORACLE_QL_ROW_MISALIGNED;
+    const size_t row_bytes = k / 256 * oracle_block_bytes(format);
+    float* decoded = (float*)malloc((k ? k : 1) * sizeof(float));
+    if (!decoded) return ORACLE_ARGUMENT_INVALID;
+    for (size_t f = 0; f < n; f++) {
+        oracle_kquant_dequantize_row(weights + f * row_bytes, row_bytes, format, k, decoded);
+        for (size_t r = 0; r < rows; r++) {
+            const float* x = input + r * k;
+            double s = 0.0;
+            for (size_t i = 0; i < k; i++) s += (double)x[i] * (double)decoded[i];
+            output[r * n + f] = s;
+        }
+    }
+    free(decoded);
+    return ORACLE_OK;
+}

@@ -164,6 +164,27 @@ void oracle_swiglu_f64(const float* gate, const float* up, size_t n, float* outp
 int oracle_rope_cos_sin_f64(const int32_t* positions, size_t tokens, size_t rotary_dim,
                             double theta, float* cos_out, float* sin_out);
 
+/*
+ * K-quant super-blocks (Q4_K, Q6_K; 256 elements).  mote-reference rejects
+ * these formats (crates/mote-reference/src/quantized.rs:152-157) and only
+ * fixes their geometry (crates/mote-types/src/lib.rs:41-74), so these
+ * functions restate the published ggml algorithm as the gguf Python package,
+ * version 0.19.0, implements it (gguf/quants.py, Q4_K.dequantize_blocks and
+ * Q6_K.dequantize_blocks): every element is one f32 expression,
+ *   Q4_K: (d * sc) * q - (dmin * m),  q in 0..15, sc/m 6-bit per 32 elements;
+ *   Q6_K: (d * sc) * q,               q in -32..31, sc int8 per 16 elements.
+ * Parity is pinned by golden vectors that gguf 0.19.0 produced
+ * (tests/golden/kquant_golden.npz, made by tests/golden/make_kquant_golden.py).
+ */
+int oracle_kquant_dequantize_row(const uint8_t* bytes, size_t bytes_len, int format,
+                                 size_t row_elements, float* output);
+
+/* Y[rows, n] = X[rows, k] . W[n, k]^T with W decoded as above (f32 values)
+ * and every dot product accumulated in f64: the tolerance reference of the
+ * K-quant linear. */
+int oracle_kquant_linear_f64(const float* input, const uint8_t* weights, int format, size_t rows,
+                             size_t n, size_t k, double* output);
+
 #ifdef __cplusplus
 }
 #endif

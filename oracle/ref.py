@@ -98,6 +98,8 @@ def lib() -> ctypes.CDLL:
             "oracle_embedding_gather_f16": (I, [P, S, S, P, S, P, P]),
             "oracle_swiglu_f64": (None, [P, P, S, P]),
             "oracle_rope_cos_sin_f64": (I, [P, S, S, ctypes.c_double, P, P]),
+            "oracle_kquant_dequantize_row": (I, [P, S, I, S, P]),
+            "oracle_kquant_linear_f64": (I, [P, P, I, S, S, S, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(l, name)
@@ -187,6 +189,35 @@ def quantized_linear_f32(inp, weights, fmt: int, rows: int, output_features: int
                                                ctypes.byref(err))
     _check(st, err)
     return out
+
+
+# ------------------------------------------------------------- K-quants ----
+KQUANT_BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+
+
+def kquant_dequantize(weights, fmt: int, rows: int, k: int) -> np.ndarray:
+    """[rows, k] f32 values of a Q4_K / Q6_K matrix (ggml's dequantization
+    as gguf 0.19.0 states it; the reference itself rejects these formats)."""
+    w = _c(weights, np.uint8)
+    rb = k // 256 * KQUANT_BLOCK_BYTES.get(fmt, 0)
+    out = np.empty((rows, k), np.float32)
+    for r in range(rows):
+        st = lib().oracle_kquant_dequantize_row(_ptr(w[r * rb:(r + 1) * rb]), rb, fmt, k,
+                                                _ptr(out[r]))
+        if st != 0:
+            raise OracleError(st, _Err())
+    return out
+
+
+def kquant_linear_f64(inp, weights, fmt: int, rows: int, n: int, k: int) -> np.ndarray:
+    """Y = X . dequant(W)^T with f64 accumulation (tolerance reference)."""
+    x = _c(inp, np.float32)
+    w = _c(weights, np.uint8)
+    out = np.empty(rows * n, np.float64)
+    st = lib().oracle_kquant_linear_f64(_ptr(x), _ptr(w), fmt, rows, n, k, _ptr(out))
+    if st != 0:
+        raise OracleError(st, _Err())
+    return out.reshape(rows, n)
 
 
 def matmul_f32(lhs, rhs, m: int, n: int, k: int) -> np.ndarray:

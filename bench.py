@@ -557,6 +557,53 @@ class Bench:
             del ws, base
         return out
 
+    def kquant_weights(self, name: str, n: int, k: int, seed: int):
+        """Random K-quant super-blocks with small fixed f16 scales (timing only;
+        parity is in tests/test_gpu_kquant.py)."""
+        torch = self.torch
+        bb = 144 if name == "q4_k" else 210
+        nb = n * (k // 256) * bb
+        g0 = torch.Generator(device=self.dev).manual_seed(seed)
+        base = torch.randint(0, 256, (nb,), generator=g0, dtype=torch.uint8, device=self.dev)
+        blocks = base.view(n * (k // 256), bb)
+        if name == "q4_k":
+            blocks[:, 0:4] = torch.tensor([0, 0x08, 0, 0x08], dtype=torch.uint8, device=self.dev)
+        else:
+            blocks[:, 208:210] = torch.tensor([0, 0x10], dtype=torch.uint8, device=self.dev)
+        return base, nb
+
+    def kquant(self) -> dict:
+        """The K-quant linears: Q4_K (tensor-core decode kernel) at lm_head
+        K=4096, N=128256, M in {1, 16} (295.5 MB, no rotation needed) and
+        N=14336, M=1 over copies holding >= 2.5x L2; Q6_K (warp-per-row
+        kernel) at N=14336, M=1, rotated the same way."""
+        torch = self.torch
+        k = 4096
+        out = {}
+        for name, n, ms in (("q4_k", 128256, (1, 16)), ("q4_k", 14336, (1,)),
+                            ("q6_k", 14336, (1,))):
+            fn = getattr(self.lib, f"mote_cuda_quantized_linear_{name}_f16")
+            base, nb = self.kquant_weights(name, n, k, seed=n + len(name))
+            ws = [base] + [base.clone() for _ in range(copies_for(nb) - 1)]
+            for m in ms:
+                x = self.randn((m, k), 90 + m, torch.float16)
+                y = torch.empty((m, n), dtype=torch.float16, device=self.dev)
+
+                def run(x=x, y=y, m=m, n=n, ws=ws, fn=fn):
+                    for w in ws:
+                        self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k,
+                                      self.stream()), "k-quant linear")
+
+                g = self.graph(run)
+                t = self.time_graph(g, 10, len(ws)) / len(ws)
+                del g
+                b = nb + m * k * 2 + m * n * 2
+                out[f"{name}_m{m}_n{n}"] = {"us": round(t * 1e3, 2),
+                                            "gbs": round(b / t / 1e6, 1),
+                                            "weight_bytes": nb, "copies": len(ws)}
+            del ws, base
+        return out
+
     def sharded_linear(self, n: int, ms_list, seed: int, k: int = 4096) -> dict:
         """A linear column-sharded over the ranks (strong scaling): per step
         each rank runs the Q4_0 linear on its rows [rank * shard, ...) and the
@@ -738,6 +785,7 @@ class Bench:
             extra["config4_decoder_layer_m1"] = self.config4()
             extra["config5"] = self.config5()
             extra["q8_0_linear"] = self.q8_0()
+            extra["kquant_linear"] = self.kquant()
         e2e = self.e2e(max(3, min(args.steps, 20)))
         if self.world > 1:
             # the splits the data plane supports: lm_head and FFN up/gate by
@@ -892,6 +940,7 @@ def run_single_case(args) -> None:
 
     --only gemv       Q4_0 linear f16 -> f16, [--m, --n, --k]
     --only q8_0       Q8_0 linear f16 -> f16, [--m, --n, --k]
+    --only q4_k       Q4_K linear f16 -> f16, [--m, --n, --k]
     --only norm_rope  fused RMSNorm + RoPE at config-2 geometry
     """
     import torch
@@ -923,6 +972,16 @@ def run_single_case(args) -> None:
         def launch():
             b.check(b.lib.mote_cuda_quantized_linear_q8_0_f16(
                 x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "q8_0")
+        nbytes = nb + m * k * 2 + m * n * 2
+    elif args.only == "q4_k":
+        m, n, k = args.m, args.n, args.k
+        w, nb = b.kquant_weights("q4_k", n, k, seed=1)
+        x = b.randn((m, k), 2, torch.float16)
+        y = torch.empty((m, n), dtype=torch.float16, device=b.dev)
+
+        def launch():
+            b.check(b.lib.mote_cuda_quantized_linear_q4_k_f16(
+                x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "q4_k")
         nbytes = nb + m * k * 2 + m * n * 2
     elif args.only == "norm_rope":
         t, hidden, qh, kh, hd = 512, 2048, 32, 8, 64
@@ -962,7 +1021,7 @@ def run_single_case(args) -> None:
 
 def main() -> int:
     p = argparse.ArgumentParser()
-    p.add_argument("--only", default=None, help="profile one kernel: gemv | q8_0 | norm_rope")
+    p.add_argument("--only", default=None, help="profile one kernel: gemv | q8_0 | q4_k | norm_rope")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=128256)
     p.add_argument("--k", type=int, default=4096)

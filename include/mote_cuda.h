@@ -122,8 +122,9 @@ int mote_cuda_quantized_linear_q4_0_f32(const void* input, const void* weights, 
  * output: the device counterpart of mote-reference's quantized_linear_f32
  * for Q8_0 (crates/mote-reference/src/quantized.rs:89-144, decode :191-195).
  * No HIP counterpart (the HIP backend has a Q4_0 linear only); argument
- * rules as mote_cuda_quantized_linear_q4_0_f16.  A decode kernel: more than
- * 16 tokens run as consecutive launches of 16. */
+ * rules as mote_cuda_quantized_linear_q4_0_f16.  More than 16 tokens run on
+ * the tensor-core GEMM when N % 16 == 0, K % 256 == 0 and the pointers are
+ * 16-byte aligned, else as consecutive decode launches of up to 16. */
 int mote_cuda_quantized_linear_q8_0_f16(const void* input, const void* weights, void* output,
                                         uint64_t rows, uint64_t output_features,
                                         uint64_t input_features, void* stream);
@@ -131,6 +132,36 @@ int mote_cuda_quantized_linear_q8_0_f16_f32out(const void* input, const void* we
                                                void* output, uint64_t rows,
                                                uint64_t output_features, uint64_t input_features,
                                                void* stream);
+
+/* K-quant weights (ggml 256-element super-blocks): Q4_K (144 bytes: f16 d,
+ * f16 dmin, 12 bytes of packed 6-bit scales and mins, 128 bytes of nibbles;
+ * value = d*sc*q - dmin*m) and Q6_K (210 bytes: 128 bytes of low nibbles, 64
+ * of 2-bit high parts, 16 int8 scales, f16 d; value = d*sc*(q - 32)).  f16
+ * input [rows, K], f32 accumulation, f16 (or, for Q4_K, f32) output [rows,
+ * N].  No reference counterpart: mote-types fixes the geometry
+ * (crates/mote-types/src/lib.rs:41-74) and mote-reference rejects these
+ * formats (crates/mote-reference/src/quantized.rs:152-157).  K % 256 != 0 is
+ * an invalid value; other rules as mote_cuda_quantized_linear_q4_0_f16.
+ * Q4_K runs a tensor-core decode kernel for up to 16 tokens per launch
+ * (16-byte aligned input and weights), Q6_K a warp-per-row kernel. */
+int mote_cuda_quantized_linear_q4_k_f16(const void* input, const void* weights, void* output,
+                                        uint64_t rows, uint64_t output_features,
+                                        uint64_t input_features, void* stream);
+int mote_cuda_quantized_linear_q4_k_f16_f32out(const void* input, const void* weights,
+                                               void* output, uint64_t rows,
+                                               uint64_t output_features, uint64_t input_features,
+                                               void* stream);
+int mote_cuda_quantized_linear_q6_k_f16(const void* input, const void* weights, void* output,
+                                        uint64_t rows, uint64_t output_features,
+                                        uint64_t input_features, void* stream);
+
+/* Decodes a [rows, k] Q4_K (format 2) or Q6_K (format 3) matrix into f32
+ * values [rows, k], bit-identical to ggml's published decode (each element
+ * one separately rounded f32 expression).  Format ids follow mote-types'
+ * QuantFormat order (Q8_0, Q4_0, Q4_K, Q6_K).  A null pointer or stream,
+ * another format or k % 256 != 0 is an invalid value; empty succeeds. */
+int mote_cuda_kquant_dequantize_f32(int format, const void* weights, void* output, uint64_t rows,
+                                    uint64_t k, void* stream);
 
 /* The f16 linear with a caller workspace (256-byte aligned, zeroed once
  * before first use; its first 256 KiB hold per-tile counters that every call

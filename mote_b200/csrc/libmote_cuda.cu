@@ -5,6 +5,7 @@
 #include "q4_0_gemm_tcgen05.cu"
 #include "q4_0_linear.cu"
 #include "q8_0_linear.cu"
+#include "kquant_linear.cu"
 #include "layer_ops.cu"
 #include "q4_0_codec.cu"
 #include "comm.cu"

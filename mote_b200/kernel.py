@@ -103,6 +103,9 @@ _ARG_KINDS = {
     "mote_cuda_quantized_linear_q4_0_f32": "pppuuup",
     "mote_cuda_quantized_linear_q8_0_f16": "pppuuup",
     "mote_cuda_quantized_linear_q8_0_f16_f32out": "pppuuup",
+    "mote_cuda_quantized_linear_q4_k_f16": "pppuuup",
+    "mote_cuda_quantized_linear_q4_k_f16_f32out": "pppuuup",
+    "mote_cuda_quantized_linear_q6_k_f16": "pppuuup",
     "mote_cuda_q4_0_gate_up_swiglu_f16": "ppppuuup",
     "mote_cuda_quantized_linear_q4_0_f16_residual": "ppppuuup",
     "mote_cuda_quantized_linear_q4_0_f16_ws": "pppuuupup",
@@ -128,6 +131,9 @@ CUDA_KERNELS = {
     ("quantized_linear_q4_0", DType.F32): "mote_cuda_quantized_linear_q4_0_f32",
     ("quantized_linear_q8_0", DType.F16): "mote_cuda_quantized_linear_q8_0_f16",
     ("quantized_linear_q8_0_f32out", DType.F16): "mote_cuda_quantized_linear_q8_0_f16_f32out",
+    ("quantized_linear_q4_k", DType.F16): "mote_cuda_quantized_linear_q4_k_f16",
+    ("quantized_linear_q4_k_f32out", DType.F16): "mote_cuda_quantized_linear_q4_k_f16_f32out",
+    ("quantized_linear_q6_k", DType.F16): "mote_cuda_quantized_linear_q6_k_f16",
     ("gate_up_swiglu_q4_0", DType.F16): "mote_cuda_q4_0_gate_up_swiglu_f16",
     ("quantized_linear_q4_0_residual", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_residual",
     ("quantized_linear_q4_0_ws", DType.F16): "mote_cuda_quantized_linear_q4_0_f16_ws",

@@ -173,6 +173,69 @@ def quantized_linear_q8_0(context: CudaContext, input: Tensor, weights: Tensor, 
                                         context.stream), "launch Q8_0 linear kernel")
 
 
+_KQUANT_SYMBOLS = {
+    (QuantFormat.Q4_K, DType.F16): "mote_cuda_quantized_linear_q4_k_f16",
+    (QuantFormat.Q4_K, DType.F32): "mote_cuda_quantized_linear_q4_k_f16_f32out",
+    (QuantFormat.Q6_K, DType.F16): "mote_cuda_quantized_linear_q6_k_f16",
+}
+
+
+def quantized_linear_kquant(context: CudaContext, input: Tensor, weights: Tensor, output: Tensor,
+                            output_dtype: DType = DType.F16) -> None:
+    """``output = input @ weights^T`` with K-quant weights [N, K] (ggml Q4_K,
+    144-byte super-blocks, or Q6_K, 210 bytes, per 256 elements), f16 input,
+    f32 accumulation.  Q4_K writes f16 or f32, Q6_K f16.  mote-reference has
+    no K-quant linear (it rejects the formats, quantized.rs:152-157); the
+    checks are the Q4_0 op's, with K a multiple of 256."""
+    enc = weights.desc.encoding
+    fmt = enc.quantized
+    if fmt not in (QuantFormat.Q4_K, QuantFormat.Q6_K):
+        raise errors.UnsupportedEncoding(actual=enc)
+    symbol = _KQUANT_SYMBOLS.get((fmt, output_dtype))
+    if symbol is None:
+        raise errors.DTypeMismatch(tensor="output", expected=DType.F16, actual=output_dtype)
+    _plain(input, "input", DType.F16)
+    _rank(input, "input", 2)
+    _rank(weights, "weights", 2)
+    _plain(output, "output", output_dtype)
+    _rank(output, "output", 2)
+    rows, k = input.shape
+    n, wk = weights.shape
+    if wk != k:
+        raise errors.ShapeMismatch(tensor="weights", expected=(n, k), actual=weights.shape)
+    _shape(output, "output", (rows, n))
+    in_s, w_s, out_s = (context.storage(t) for t in (input, weights, output))
+    _not_aliased(output, "output", input, "input")
+    _not_aliased(output, "output", weights, "weights")
+    if rows * n > U32_MAX:
+        raise errors.QuantizedLinearDimensionsTooLarge(rows=rows, output_features=n,
+                                                       input_features=k)
+    if rows * n == 0:
+        return
+    context.inner.select()
+    errors.check(getattr(lib(), symbol)(in_s.pointer, w_s.pointer, out_s.pointer, rows, n, k,
+                                        context.stream), "launch K-quant linear kernel")
+
+
+def kquant_decode_f32(context: CudaContext, weights: Tensor, output: Tensor) -> None:
+    """Decodes a Q4_K / Q6_K matrix [N, K] into f32 values [N, K]."""
+    enc = weights.desc.encoding
+    fmt = enc.quantized
+    if fmt not in (QuantFormat.Q4_K, QuantFormat.Q6_K):
+        raise errors.UnsupportedEncoding(actual=enc)
+    _rank(weights, "weights", 2)
+    _plain(output, "output", DType.F32)
+    _shape(output, "output", weights.shape)
+    w_s, out_s = context.storage(weights), context.storage(output)
+    n, k = weights.shape
+    if n * k == 0:
+        return
+    context.inner.select()
+    code = 2 if fmt is QuantFormat.Q4_K else 3
+    errors.check(lib().mote_cuda_kquant_dequantize_f32(code, w_s.pointer, out_s.pointer, n, k,
+                                                       context.stream), "decode K-quant matrix")
+
+
 def quantized_linear_q4_0_f32(context: CudaContext, input: Tensor, weights: Tensor,
                               output: Tensor) -> None:
     """f32 in, f32 out (device counterpart of ``quantized_linear_f32``)."""

@@ -196,3 +196,21 @@ def test_q8_0_argument_rules(lib):
         assert fn(FAKE, FAKE, FAKE, 1, 8, 32, None) == 1         # null stream
         assert fn(FAKE, FAKE, FAKE, 0, 8, 32, STREAM) == 0       # empty: no launch
         assert fn(FAKE, FAKE, FAKE, 1 << 20, 1 << 13, 32, STREAM) == 9  # rows*N > u32
+
+
+def test_kquant_argument_rules(lib):
+    for fn in (lib.mote_cuda_quantized_linear_q4_k_f16,
+               lib.mote_cuda_quantized_linear_q4_k_f16_f32out,
+               lib.mote_cuda_quantized_linear_q6_k_f16):
+        assert fn(None, FAKE, FAKE, 1, 8, 256, STREAM) == 1      # null input
+        assert fn(FAKE, FAKE, FAKE, 1, 8, 288, STREAM) == 1      # K % 256 (a Q4_0-legal K)
+        assert fn(FAKE, FAKE, FAKE, 0, 8, 288, STREAM) == 1      # K % 256 checked before empty
+        assert fn(FAKE, FAKE, FAKE, 1, 8, 256, None) == 1        # null stream
+        assert fn(FAKE, FAKE, FAKE, 0, 8, 256, STREAM) == 0      # empty: no launch
+        assert fn(FAKE, FAKE, FAKE, 1 << 20, 1 << 13, 256, STREAM) == 9  # rows*N > u32
+    dq = lib.mote_cuda_kquant_dequantize_f32
+    assert dq(2, None, FAKE, 1, 256, STREAM) == 1
+    assert dq(1, FAKE, FAKE, 1, 256, STREAM) == 1                # Q4_0 is not a K-quant
+    assert dq(3, FAKE, FAKE, 1, 320, STREAM) == 1                # k % 256
+    assert dq(3, FAKE, FAKE, 1, 256, None) == 1
+    assert dq(2, FAKE, FAKE, 0, 256, STREAM) == 0

@@ -160,3 +160,48 @@ def test_kquant_linear_rejects_misaligned_k(ctx):
     f = lib().mote_cuda_quantized_linear_q4_k_f16
     assert f(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 16, 288,
              ctx.stream) == 1
+
+
+def test_gguf_weights_load_and_run(ctx, oracle_lib, tmp_path):
+    """A GGUF file (written by the gguf package) mapped by mote_b200.gguf_file,
+    its Q4_K, Q6_K and Q4_0 tensors copied to the device and run through the
+    linears; results against the oracle on the same bytes."""
+    gguf = pytest.importorskip("gguf")
+    from gguf import GGMLQuantizationType as T
+
+    from mote_b200.gguf_file import GGUFFile, load_tensors
+
+    n, k, m = 96, 1024, 3
+    w4k = kquant_weights("q4_k", n, k, seed=31).reshape(n, -1)
+    w6k = kquant_weights("q6_k", n, k, seed=32).reshape(n, -1)
+    w40 = np.empty((n, k // 32, 18), np.uint8)
+    rng = np.random.default_rng(33)
+    w40[:, :, 0:2] = rng.uniform(1e-3, 3e-3, (n, k // 32)).astype(np.float16).view(
+        np.uint8).reshape(n, k // 32, 2)
+    w40[:, :, 2:] = rng.integers(0, 256, (n, k // 32, 16), dtype=np.uint8)
+    w40 = w40.reshape(n, -1)
+    path = tmp_path / "w.gguf"
+    wr = gguf.GGUFWriter(str(path), "llama")
+    wr.add_tensor("blk.0.ffn_up.weight", w4k, raw_dtype=T.Q4_K)
+    wr.add_tensor("blk.0.ffn_down.weight", w6k, raw_dtype=T.Q6_K)
+    wr.add_tensor("blk.0.attn_q.weight", w40, raw_dtype=T.Q4_0)
+    wr.write_header_to_file()
+    wr.write_kv_data_to_file()
+    wr.write_tensors_to_file()
+    wr.close()
+    x = np.random.default_rng(34).normal(0, 1, (m, k)).astype(np.float16)
+    xt = ctx.from_bytes(plain((m, k), DType.F16), x)
+    with GGUFFile(path) as f:
+        dev = load_tensors(ctx, f)
+    for name, fmt_name, raw in (("blk.0.ffn_up.weight", "q4_k", w4k),
+                                ("blk.0.ffn_down.weight", "q6_k", w6k)):
+        yt = ctx.empty(plain((m, n), DType.F16))
+        ops.quantized_linear_kquant(ctx, xt, dev[name], yt)
+        got = np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(m, n)
+        check(oracle_lib, fmt_name, got, x, raw.reshape(-1), m, n, k)
+    yt = ctx.empty(plain((m, n), DType.F16))
+    ops.quantized_linear_q4_0_f16(ctx, xt, dev["blk.0.attn_q.weight"], yt)
+    got = np.frombuffer(ctx.read_bytes(yt), np.float16).astype(np.float32).reshape(m, n)
+    ref64 = checker.linear_f64(x.astype(np.float32), checker.q4_0_dequant_np(w40.reshape(-1), n, k))
+    assert checker.rel_err_normwise(got, ref64) <= BOUND
+    assert ctx.device_status() == 0

@@ -573,15 +573,14 @@ class Bench:
         return base, nb
 
     def kquant(self) -> dict:
-        """The K-quant linears: Q4_K (tensor-core decode kernel) at lm_head
-        K=4096, N=128256, M in {1, 16} (295.5 MB, no rotation needed) and
-        N=14336, M=1 over copies holding >= 2.5x L2; Q6_K (warp-per-row
-        kernel) at N=14336, M=1, rotated the same way."""
+        """The K-quant linears (tensor-core decode kernels): lm_head K=4096,
+        N=128256 at M in {1, 16} (Q4_K 295.5 MB, Q6_K 431 MB: no rotation
+        needed) and N=14336 at M=1 over copies holding >= 2.5x L2."""
         torch = self.torch
         k = 4096
         out = {}
         for name, n, ms in (("q4_k", 128256, (1, 16)), ("q4_k", 14336, (1,)),
-                            ("q6_k", 14336, (1,))):
+                            ("q6_k", 128256, (1, 16)), ("q6_k", 14336, (1,))):
             fn = getattr(self.lib, f"mote_cuda_quantized_linear_{name}_f16")
             base, nb = self.kquant_weights(name, n, k, seed=n + len(name))
             ws = [base] + [base.clone() for _ in range(copies_for(nb) - 1)]
@@ -941,6 +940,7 @@ def run_single_case(args) -> None:
     --only gemv       Q4_0 linear f16 -> f16, [--m, --n, --k]
     --only q8_0       Q8_0 linear f16 -> f16, [--m, --n, --k]
     --only q4_k       Q4_K linear f16 -> f16, [--m, --n, --k]
+    --only q6_k       Q6_K linear f16 -> f16, [--m, --n, --k]
     --only norm_rope  fused RMSNorm + RoPE at config-2 geometry
     """
     import torch
@@ -973,15 +973,15 @@ def run_single_case(args) -> None:
             b.check(b.lib.mote_cuda_quantized_linear_q8_0_f16(
                 x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "q8_0")
         nbytes = nb + m * k * 2 + m * n * 2
-    elif args.only == "q4_k":
+    elif args.only in ("q4_k", "q6_k"):
         m, n, k = args.m, args.n, args.k
-        w, nb = b.kquant_weights("q4_k", n, k, seed=1)
+        w, nb = b.kquant_weights(args.only, n, k, seed=1)
         x = b.randn((m, k), 2, torch.float16)
         y = torch.empty((m, n), dtype=torch.float16, device=b.dev)
+        fn = getattr(b.lib, f"mote_cuda_quantized_linear_{args.only}_f16")
 
         def launch():
-            b.check(b.lib.mote_cuda_quantized_linear_q4_k_f16(
-                x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "q4_k")
+            b.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), args.only)
         nbytes = nb + m * k * 2 + m * n * 2
     elif args.only == "norm_rope":
         t, hidden, qh, kh, hd = 512, 2048, 32, 8, 64
@@ -1021,7 +1021,7 @@ def run_single_case(args) -> None:
 
 def main() -> int:
     p = argparse.ArgumentParser()
-    p.add_argument("--only", default=None, help="profile one kernel: gemv | q8_0 | q4_k | norm_rope")
+    p.add_argument("--only", default=None, help="profile one kernel: gemv | q8_0 | q4_k | q6_k | norm_rope")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=128256)
     p.add_argument("--k", type=int, default=4096)

@@ -385,6 +385,271 @@ __global__ void __launch_bounds__(kThreads, 2) q4_k_gemv_kernel(const Params p) 
     }
 }
 
+// ---- Q6_K decode GEMV ------------------------------------------------------------
+// Q6_K super-blocks are 210 bytes, so inside a row they are only 2-byte
+// aligned.  With K % 2048 == 0 a row is a whole number of 16-byte chunks and
+// super-block u starts rem = (210 u) mod 16 bytes past a chunk boundary, the
+// same in every row.  A stage copies the 14 chunks (224 bytes) that cover the
+// block; the last block of a row has rem = 14, so its chunks end exactly at
+// the row's end and no copy leaves the matrix.  Blocks with rem = 2 mod 4
+// (odd u) have their quant words funnel-shifted out of two aligned words.
+// Step s (16 elements, one int8 scale) of a block: lane (g, t) takes elements
+// 16 s + 4t .. + 3, whose low nibbles are one word of ql and whose 2-bit high
+// parts are one word of qh; q - 32 becomes an exact f16 pair with one PRMT
+// and one f16x2 subtraction, each step is one MMA (C = 0), scaled by the
+// row's f32 d * sc into the accumulator.  The 16 x 16 products d * sc of a
+// stage are computed once per warp into a 1 KB scratch.
+constexpr int kQ6Bytes = 210;
+constexpr int kQ6Row = 240;                           // smem row stride: rows 28 banks apart
+constexpr int kQ6RowChunks = 14;
+constexpr int kQ6Stage = kTileRows * kQ6Row;          // 3840
+constexpr int kQ6Chunks = kTileRows * kQ6RowChunks;   // 224
+constexpr int kQ6ChunksPerLane = kQ6Chunks / 32;      // 7
+constexpr int kQ6ScaleBytes = kTileRows * 16 * 4;     // d * sc of one stage, per warp
+
+__host__ __device__ constexpr int q6_smem_bytes(int x_bytes, int nt, int stages) {
+    return x_bytes + kWarps * stages * kQ6Stage + kWarps * kQ6ScaleBytes + red_bytes(nt);
+}
+
+__device__ __forceinline__ int lds8s(std::uint32_t addr) {
+    int v;
+    asm volatile("ld.shared.s8 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void sts128f(std::uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+__device__ __forceinline__ float4 lds128f(std::uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+// The 4 bytes at addr: addr is word-aligned, or (MIS) 2 bytes past a word.
+template <bool MIS>
+__device__ __forceinline__ std::uint32_t ldw(std::uint32_t addr) {
+    if constexpr (MIS)
+        return prmt(lds32(addr - 2), lds32(addr + 2), 0x5432u);
+    else
+        return lds32(addr);
+}
+
+template <int NT, bool OF32, int STAGES>
+__global__ void __launch_bounds__(kThreads, 2) q6_k_gemv_kernel(const Params p) {
+    extern __shared__ __align__(1024) std::uint8_t smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    std::uint8_t* xs = smem;
+    std::uint8_t* ring = smem + p.x_bytes + warp * STAGES * kQ6Stage;
+    const std::uint32_t dsc_s =
+        smem_u32(smem + p.x_bytes + kWarps * STAGES * kQ6Stage + warp * kQ6ScaleBytes);
+    float* red = reinterpret_cast<float*>(smem + p.x_bytes + kWarps * STAGES * kQ6Stage +
+                                          kWarps * kQ6ScaleBytes);
+
+    const std::uint32_t sh = p.split_shift;
+    const std::uint32_t split = 1u << sh;
+    const std::uint32_t grp = static_cast<std::uint32_t>(warp) >> sh;
+    const std::uint32_t wig = static_cast<std::uint32_t>(warp) & (split - 1);
+    const std::uint32_t first = blockIdx.x + grp * gridDim.x;
+    const std::uint32_t stride = gridDim.x * (kWarps >> sh);
+    const std::uint32_t my_tiles = p.tiles > first ? (p.tiles - first + stride - 1) / stride : 0;
+    const std::uint32_t u0 = (p.units * wig) >> sh;
+    const std::uint32_t u1 = (p.units * (wig + 1)) >> sh;
+    const std::uint32_t spt = u1 - u0;
+    const std::uint32_t total = my_tiles * spt;
+    const std::uint64_t policy = l2_evict_first_policy();
+
+    // chunk c = lane + 32 j: row c / 14, column chunk c % 14
+    std::uint32_t dst_off[kQ6ChunksPerLane];
+    std::uint32_t chunk_row[kQ6ChunksPerLane];
+#pragma unroll
+    for (int j = 0; j < kQ6ChunksPerLane; ++j) {
+        const int c = lane + 32 * j;
+        chunk_row[j] = static_cast<std::uint32_t>(c / kQ6RowChunks);
+        dst_off[j] = chunk_row[j] * kQ6Row + (c % kQ6RowChunks) * 16;
+    }
+    const std::uint32_t ring_s = smem_u32(ring);
+    std::uint32_t iss_n = 0, iss_tl = 0, iss_u = 0, iss_slot = 0;
+    const std::uint8_t* src[kQ6ChunksPerLane];  // row start + column chunk
+    auto seek_tile = [&](std::uint32_t tl) {
+        const std::uint64_t row0 = static_cast<std::uint64_t>(first + tl * stride) * kTileRows;
+#pragma unroll
+        for (int j = 0; j < kQ6ChunksPerLane; ++j) {
+            const std::uint64_t r = min(row0 + chunk_row[j], static_cast<std::uint64_t>(p.N - 1));
+            src[j] = p.w + r * p.pitch + ((lane + 32 * j) % kQ6RowChunks) * 16;
+        }
+    };
+    if (total > 0) seek_tile(0);
+    auto issue = [&]() {
+        if (iss_n < total) {
+            const std::uint32_t slot_s = ring_s + iss_slot * kQ6Stage;
+            const std::uint32_t boff = ((u0 + iss_u) * kQ6Bytes) & ~15u;
+#pragma unroll
+            for (int j = 0; j < kQ6ChunksPerLane; ++j)
+                cp_async_16(slot_s + dst_off[j], src[j] + boff, policy);
+            if (++iss_u == spt) {
+                iss_u = 0;
+                if (iss_n + 1 < total) seek_tile(++iss_tl);
+            }
+        }
+        ++iss_n;
+        iss_slot = iss_slot + 1 == STAGES ? 0 : iss_slot + 1;
+        cp_async_commit();
+    };
+    for (int s = 0; s + 1 < STAGES; ++s) issue();
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // stage the activation rows (unpermuted) and one all-zero row
+    {
+        const std::uint32_t vec_per_row = static_cast<std::uint32_t>(p.K / 8);
+        const std::uint32_t nvec = p.M * vec_per_row;
+        for (std::uint32_t i = threadIdx.x; i < nvec; i += kThreads) {
+            const std::uint32_t m = i / vec_per_row;
+            const std::uint32_t v = i - m * vec_per_row;
+            const uint4 val = __ldg(reinterpret_cast<const uint4*>(p.x + m * p.K) + v);
+            *reinterpret_cast<uint4*>(xs + m * p.x_stride + 16 * v) = val;
+        }
+        for (std::uint32_t i = threadIdx.x; i < p.x_stride / 16; i += kThreads)
+            *reinterpret_cast<uint4*>(xs + p.M * p.x_stride + 16 * i) = make_uint4(0u, 0u, 0u, 0u);
+        __syncthreads();
+    }
+
+    std::uint32_t xsel[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const std::uint32_t m = nt * 8 + g;
+        xsel[nt] = smem_u32(xs) + (m < p.M ? m : p.M) * p.x_stride + 8 * t;
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    constexpr std::uint32_t kR8 = 8 * kQ6Row;
+    std::uint32_t slot = 0;
+
+    // one super-block of the stage in `slot_s`, block base 2 bytes past a
+    // word when MIS
+    auto block = [&](auto mis, std::uint32_t slot_s, std::uint32_t u, std::uint32_t rem) {
+        constexpr bool MIS = decltype(mis)::value;
+        // d * sc of the stage: lane L takes row L / 2, scale groups 8 (L % 2) ..
+        {
+            const std::uint32_t r = static_cast<std::uint32_t>(lane) >> 1;
+            const std::uint32_t s0 = 8u * (lane & 1);
+            const std::uint32_t rb = slot_s + r * kQ6Row + rem;
+            const float d = half_bits_to_float(lds16(rb + 208));
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = d * static_cast<float>(lds8s(rb + 192 + s0 + i));
+            sts128f(dsc_s + (r * 16 + s0) * 4, v[0], v[1], v[2], v[3]);
+            sts128f(dsc_s + (r * 16 + s0 + 4) * 4, v[4], v[5], v[6], v[7]);
+        }
+        __syncwarp();
+        const std::uint32_t qa = slot_s + g * kQ6Row + rem + 4 * t;  // row g, word t
+        q4::static_for<0, 2>([&](auto hh) {
+            constexpr int h = decltype(hh)::value;
+            std::uint32_t L[4][2], H[2][2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                L[i][0] = ldw<MIS>(qa + 64 * h + 16 * i);
+                L[i][1] = ldw<MIS>(qa + kR8 + 64 * h + 16 * i);
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                H[i][0] = ldw<MIS>(qa + 128 + 32 * h + 16 * i);
+                H[i][1] = ldw<MIS>(qa + kR8 + 128 + 32 * h + 16 * i);
+            }
+            q4::static_for<0, 2>([&](auto qq) {
+                constexpr int quad = decltype(qq)::value;  // steps 4 quad .. + 3 of this half
+                const float4 sg = lds128f(dsc_s + (g * 16 + 8 * h + 4 * quad) * 4);
+                const float4 sh8 = lds128f(dsc_s + ((g + 8) * 16 + 8 * h + 4 * quad) * 4);
+                const float dsg[4] = {sg.x, sg.y, sg.z, sg.w};
+                const float dsh[4] = {sh8.x, sh8.y, sh8.z, sh8.w};
+                q4::static_for<0, 4>([&](auto ss) {
+                    constexpr int s8 = 4 * quad + decltype(ss)::value;  // step within the half
+                    constexpr int n = s8 / 4, qi = s8 % 4, j = s8 / 2, hi = s8 % 2;
+                    std::uint32_t p01[2], p23[2];
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const std::uint32_t a = n ? (L[qi][r] >> 4) : L[qi][r];
+                        const std::uint32_t b = H[hi][r];
+                        const std::uint32_t bs = j == 0 ? (b << 4) : j == 1 ? (b << 2)
+                                               : j == 2 ? b : (b >> 2);
+                        const std::uint32_t q = and_or(a, 0x0F0F0F0Fu, bs & 0x30303030u);
+                        p01[r] = hsub2_u32(prmt(q, 0x64646464u, 0x4140u), 0x64206420u);
+                        p23[r] = hsub2_u32(prmt(q, 0x64646464u, 0x4342u), 0x64206420u);
+                    }
+                    constexpr int s = 8 * h + s8;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const uint2 xb = lds64(xsel[nt] + (256u * u + 16 * s) * 2);
+                        float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma_16816(tmp, p01[0], p01[1], p23[0], p23[1], xb.x, xb.y, tmp);
+                        const int k4 = decltype(ss)::value;
+                        acc[nt][0] = fmaf(dsg[k4], tmp[0], acc[nt][0]);
+                        acc[nt][1] = fmaf(dsg[k4], tmp[1], acc[nt][1]);
+                        acc[nt][2] = fmaf(dsh[k4], tmp[2], acc[nt][2]);
+                        acc[nt][3] = fmaf(dsh[k4], tmp[3], acc[nt][3]);
+                    }
+                });
+            });
+        });
+        __syncwarp();  // the scratch and the slot are rewritten next
+    };
+
+    for (std::uint32_t tl = 0; tl < my_tiles; ++tl) {
+        for (std::uint32_t st = 0; st < spt; ++st) {
+            issue();
+            cp_async_wait<STAGES - 1>();
+            __syncwarp();
+            const std::uint32_t u = u0 + st;
+            const std::uint32_t rem = (u * kQ6Bytes) & 15u;
+            const std::uint32_t slot_s = ring_s + slot * kQ6Stage;
+            if (rem & 2u)
+                block(std::true_type{}, slot_s, u, rem);
+            else
+                block(std::false_type{}, slot_s, u, rem);
+            slot = slot + 1 == STAGES ? 0 : slot + 1;
+        }
+        const std::uint32_t tile = first + tl * stride;
+        if (split == 1) {
+            store_tile<NT, OF32>(p, tile, g, t, acc);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+            continue;
+        }
+        float* gred = red + grp * 2 * split * (NT * 4 * 32);
+        float* mine = gred + ((tl & 1u) * split + wig) * (NT * 4 * 32);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                mine[(nt * 4 + i) * 32 + lane] = acc[nt][i];
+                acc[nt][i] = 0.f;
+            }
+        q4::named_barrier_sync(1 + static_cast<int>(grp), static_cast<int>(split) * 32);
+        if ((tl & (split - 1)) == wig) {
+            float sum[NT][4];
+            const float* base = gred + (tl & 1u) * split * (NT * 4 * 32);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sum[nt][i] = 0.f;
+            for (std::uint32_t wi = 0; wi < split; ++wi)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        sum[nt][i] += base[wi * (NT * 4 * 32) + (nt * 4 + i) * 32 + lane];
+            store_tile<NT, OF32>(p, tile, g, t, sum);
+        }
+    }
+}
+
 // ---- element decode shared by the generic linear and the dequantizer --------
 // Sub-block j (32 elements, 0..7) of a super-block, f32, each element one
 // separately rounded expression (no contraction), as the published decode.
@@ -499,9 +764,9 @@ __global__ void __launch_bounds__(256) kquant_dequantize_kernel(const std::uint8
 }
 
 // ---- host ----------------------------------------------------------------------
-template <int NT, bool OF32, int STAGES>
+template <int FMT, int NT, bool OF32, int STAGES>
 int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
-    auto kernel = q4_k_gemv_kernel<NT, OF32, STAGES>;
+    auto kernel = FMT == kQ4K ? q4_k_gemv_kernel<NT, OF32, STAGES> : q6_k_gemv_kernel<NT, OF32, STAGES>;
     static std::atomic<std::uint64_t> configured{0};
     const int st = q4::ensure_smem_attribute(kernel, q4::kMaxSmem, configured);
     if (st != kSuccess) return st;
@@ -511,7 +776,8 @@ int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
     cfg.gridDim = dim3(min((p.tiles + groups - 1) / groups, cap));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes =
-        smem_bytes(static_cast<int>(p.x_bytes), static_cast<int>(p.s_bytes), NT, STAGES);
+        FMT == kQ4K ? smem_bytes(static_cast<int>(p.x_bytes), static_cast<int>(p.s_bytes), NT, STAGES)
+                    : q6_smem_bytes(static_cast<int>(p.x_bytes), NT, STAGES);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -521,18 +787,18 @@ int launch_gemv(const Params& p, int ctas_per_sm, cudaStream_t stream) {
     return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, p));
 }
 
-template <bool OF32>
+template <int FMT, bool OF32>
 int launch_gemv_config(const Params& p, int stages, int ctas, bool two, cudaStream_t stream) {
     switch (stages) {
         case 4:
-            return two ? launch_gemv<2, OF32, 4>(p, ctas, stream)
-                       : launch_gemv<1, OF32, 4>(p, ctas, stream);
+            return two ? launch_gemv<FMT, 2, OF32, 4>(p, ctas, stream)
+                       : launch_gemv<FMT, 1, OF32, 4>(p, ctas, stream);
         case 3:
-            return two ? launch_gemv<2, OF32, 3>(p, ctas, stream)
-                       : launch_gemv<1, OF32, 3>(p, ctas, stream);
+            return two ? launch_gemv<FMT, 2, OF32, 3>(p, ctas, stream)
+                       : launch_gemv<FMT, 1, OF32, 3>(p, ctas, stream);
         default:
-            return two ? launch_gemv<2, OF32, 2>(p, ctas, stream)
-                       : launch_gemv<1, OF32, 2>(p, ctas, stream);
+            return two ? launch_gemv<FMT, 2, OF32, 2>(p, ctas, stream)
+                       : launch_gemv<FMT, 1, OF32, 2>(p, ctas, stream);
     }
 }
 
@@ -547,7 +813,8 @@ int run_linear(const void* x, const void* w, void* y, std::uint64_t M, std::uint
     p.pitch = (K / 256) * block_bytes(FMT);
     p.units = static_cast<std::uint32_t>(K / 256);
     p.tiles = static_cast<std::uint32_t>((N + kTileRows - 1) / kTileRows);
-    const bool fast = FMT == kQ4K && K <= (1ull << 20) &&
+    // Q6_K rows are whole 16-byte chunks only when K % 2048 == 0
+    const bool fast = (FMT == kQ4K || K % 2048 == 0) && K <= (1ull << 20) &&
                       reinterpret_cast<std::uintptr_t>(x) % 16 == 0 &&
                       reinterpret_cast<std::uintptr_t>(w) % 16 == 0;
     // tokens per launch, ring depth and CTAs per SM: two CTAs per SM with
@@ -564,14 +831,16 @@ int run_linear(const void* x, const void* w, void* y, std::uint64_t M, std::uint
             const int nt = m > 8 ? 2 : 1;
             constexpr int kOptions[5][2] = {{2, 4}, {2, 3}, {2, 2}, {1, 4}, {1, 2}};
             for (const auto& opt : kOptions) {
-                const int bytes = smem_bytes(static_cast<int>(xb), static_cast<int>(sb), nt, opt[1]);
+                const int bytes = FMT == kQ4K
+                                      ? smem_bytes(static_cast<int>(xb), static_cast<int>(sb), nt, opt[1])
+                                      : q6_smem_bytes(static_cast<int>(xb), nt, opt[1]);
                 if (bytes <= q4::kMaxSmem &&
                     opt[0] * (bytes + q4::kSmemReservedPerCta) <= q4::kSmemPerSm) {
                     tokens = m;
                     ctas = opt[0];
                     stages = opt[1];
                     p.x_bytes = xb;
-                    p.s_bytes = sb;
+                    p.s_bytes = FMT == kQ4K ? sb : 0u;
                     break;
                 }
             }
@@ -588,7 +857,7 @@ int run_linear(const void* x, const void* w, void* y, std::uint64_t M, std::uint
         p.y = static_cast<std::uint8_t*>(y) + m0 * N * osz;
         int st;
         if (tokens) {
-            st = launch_gemv_config<OF32>(p, stages, ctas, mc > 8, stream);
+            st = launch_gemv_config<FMT, OF32>(p, stages, ctas, mc > 8, stream);
         } else {
             const dim3 grid(static_cast<unsigned>((N + 3) / 4),
                             static_cast<unsigned>((mc + kGenericTokens - 1) / kGenericTokens));

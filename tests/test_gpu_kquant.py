@@ -10,8 +10,8 @@ tests/test_oracle_kquants.py):
   float64 accumulation of the exactly decoded weights, as the Q4_0 decode
   path.  The Q4_K tensor-core kernel (1-16 tokens per launch, K % 256 == 0,
   16-byte aligned pointers), its split-K groups, ragged N, chunked launches
-  beyond 16 tokens, the f32 output, the warp-per-row kernel (unaligned input,
-  and every Q6_K call) are covered.
+  beyond 16 tokens, the f32 output, the Q6_K tensor-core kernel (K % 2048
+  == 0) and the warp-per-row kernel (unaligned input, other K) are covered.
 """
 from __future__ import annotations
 
@@ -149,8 +149,11 @@ def test_q4_k_unaligned_input_runs_the_generic_kernel(ctx, oracle_lib):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 2048, 2048), (5, 300, 4096), (17, 40, 256),
-                                   (1, 1000, 8192)])
+                                   (1, 1000, 8192), (16, 100, 6144), (9, 2048, 4096),
+                                   (3, 50, 2304), (12, 4096, 2048), (2, 16032, 4096)])
 def test_q6_k_linear_matches_oracle(ctx, oracle_lib, m, n, k):
+    """K % 2048 == 0 with aligned pointers: the tensor-core Q6_K kernel (odd
+    super-blocks 2 bytes off a word); other K: the warp-per-row kernel."""
     w = kquant_weights("q6_k", n, k, seed=3 * n + k)
     x = np.random.default_rng(m + 100).normal(0, 1, (m, k)).astype(np.float16)
     check(oracle_lib, "q6_k", run(ctx, "q6_k", x, w, m, n, k), x, w, m, n, k)

@@ -24,7 +24,8 @@
 // a group, four consecutive elements per nibble plane, so the activations
 // stay unpermuted (the MMA k positions {2t, 2t+1, 2t+8, 2t+9} take elements
 // 4t..4t+3 of each 16-element step; B is one 8-byte load).
-// Other shapes, and Q6_K, run a warp-per-row kernel with f32 accumulation.
+// The Q6_K GEMV (K % 2048 == 0) is described above its kernel; other shapes
+// run a warp-per-row kernel with f32 accumulation.
 
 namespace mote {
 namespace kq {

@@ -575,7 +575,8 @@ class Bench:
     def kquant(self) -> dict:
         """The K-quant linears (tensor-core decode kernels): lm_head K=4096,
         N=128256 at M in {1, 16} (Q4_K 295.5 MB, Q6_K 431 MB: no rotation
-        needed) and N=14336 at M=1 over copies holding >= 2.5x L2."""
+        needed) and N=14336 at M=1 over copies holding >= 2.5x L2; and the
+        Q4_K prefill M=2048, N=14336 on the tcgen05 GEMM (TFLOP/s)."""
         torch = self.torch
         k = 4096
         out = {}
@@ -601,6 +602,22 @@ class Bench:
                                             "gbs": round(b / t / 1e6, 1),
                                             "weight_bytes": nb, "copies": len(ws)}
             del ws, base
+        # Q4_K prefill on the tcgen05 GEMM (Q4_K converter): M=2048, N=14336
+        m, n = 2048, 14336
+        w, nb = self.kquant_weights("q4_k", n, k, seed=5)
+        x = self.randn((m, k), 95, torch.float16)
+        y = torch.empty((m, n), dtype=torch.float16, device=self.dev)
+        fn = self.lib.mote_cuda_quantized_linear_q4_k_f16
+
+        def runp():
+            self.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, self.stream()),
+                       "q4_k prefill")
+
+        g = self.graph(runp)
+        t = self.time_graph(g, 10, 1)
+        del g
+        out["q4_k_prefill_m2048_n14336"] = {"us": round(t * 1e3, 1),
+                                             "tflops": round(2 * m * n * k / t / 1e9, 1)}
         return out
 
     def sharded_linear(self, n: int, ms_list, seed: int, k: int = 4096) -> dict:

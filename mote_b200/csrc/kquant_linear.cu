@@ -399,14 +399,16 @@ __global__ void __launch_bounds__(kThreads, 2) q4_k_gemv_kernel(const Params p) 
 // parts are one word of qh; q - 32 becomes an exact f16 pair with one PRMT
 // and one f16x2 subtraction, each step is one MMA (C = 0), scaled by the
 // row's f32 d * sc into the accumulator.  The 16 x 16 products d * sc of a
-// stage are computed once per warp into a 1 KB scratch.
+// stage are computed once per warp into a scratch whose 80-byte rows put the
+// eight row groups' 16-byte reads in distinct banks.
 constexpr int kQ6Bytes = 210;
 constexpr int kQ6Row = 240;                           // smem row stride: rows 28 banks apart
 constexpr int kQ6RowChunks = 14;
 constexpr int kQ6Stage = kTileRows * kQ6Row;          // 3840
 constexpr int kQ6Chunks = kTileRows * kQ6RowChunks;   // 224
 constexpr int kQ6ChunksPerLane = kQ6Chunks / 32;      // 7
-constexpr int kQ6ScaleBytes = kTileRows * 16 * 4;     // d * sc of one stage, per warp
+constexpr int kQ6ScaleStride = 20;                    // floats per row: rows 20 banks apart
+constexpr int kQ6ScaleBytes = kTileRows * kQ6ScaleStride * 4;  // d * sc of one stage, per warp
 
 __host__ __device__ constexpr int q6_smem_bytes(int x_bytes, int nt, int stages) {
     return x_bytes + kWarps * stages * kQ6Stage + kWarps * kQ6ScaleBytes + red_bytes(nt);
@@ -546,8 +548,8 @@ __global__ void __launch_bounds__(kThreads, 2) q6_k_gemv_kernel(const Params p) 
             float v[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = d * static_cast<float>(lds8s(rb + 192 + s0 + i));
-            sts128f(dsc_s + (r * 16 + s0) * 4, v[0], v[1], v[2], v[3]);
-            sts128f(dsc_s + (r * 16 + s0 + 4) * 4, v[4], v[5], v[6], v[7]);
+            sts128f(dsc_s + (r * kQ6ScaleStride + s0) * 4, v[0], v[1], v[2], v[3]);
+            sts128f(dsc_s + (r * kQ6ScaleStride + s0 + 4) * 4, v[4], v[5], v[6], v[7]);
         }
         __syncwarp();
         const std::uint32_t qa = slot_s + g * kQ6Row + rem + 4 * t;  // row g, word t
@@ -566,8 +568,9 @@ __global__ void __launch_bounds__(kThreads, 2) q6_k_gemv_kernel(const Params p) 
             }
             q4::static_for<0, 2>([&](auto qq) {
                 constexpr int quad = decltype(qq)::value;  // steps 4 quad .. + 3 of this half
-                const float4 sg = lds128f(dsc_s + (g * 16 + 8 * h + 4 * quad) * 4);
-                const float4 sh8 = lds128f(dsc_s + ((g + 8) * 16 + 8 * h + 4 * quad) * 4);
+                const float4 sg = lds128f(dsc_s + (g * kQ6ScaleStride + 8 * h + 4 * quad) * 4);
+                const float4 sh8 =
+                    lds128f(dsc_s + ((g + 8) * kQ6ScaleStride + 8 * h + 4 * quad) * 4);
                 const float dsg[4] = {sg.x, sg.y, sg.z, sg.w};
                 const float dsh[4] = {sh8.x, sh8.y, sh8.z, sh8.w};
                 q4::static_for<0, 4>([&](auto ss) {
@@ -807,6 +810,10 @@ template <int FMT, bool OF32>
 int run_linear(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
                std::uint64_t K, cudaStream_t stream) {
     const std::size_t osz = OF32 ? 4 : 2;
+    // prefill-shaped Q4_K: the tcgen05 GEMM with the Q4_K converter
+    if constexpr (FMT == kQ4K)
+        if (M > static_cast<std::uint64_t>(kMaxTokens) && gemm::supported(x, w, y, M, N, K, osz))
+            return gemm::launch<OF32, gemm::kWQ4_K>(x, w, y, M, N, K, stream);
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
     p.N = static_cast<std::uint32_t>(N);

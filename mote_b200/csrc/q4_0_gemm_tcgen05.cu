@@ -1,6 +1,8 @@
-// Prefill-shaped Q4_0 (and Q8_0) GEMM on the 5th-generation tensor cores
-// (tcgen05/TMEM).  The kernel is written for Q4_0; with Q8 = true the raw
-// stages hold 272-byte Q8_0 rows and convert_block_q8 does the conversion.
+// Prefill-shaped Q4_0 (and Q8_0, Q4_K) GEMM on the 5th-generation tensor
+// cores (tcgen05/TMEM).  The kernel is written for Q4_0; the weight format WF
+// selects the raw rows and the converter: Q8_0 stages hold 272-byte rows
+// (convert_block_q8), Q4_K stages one 144-byte super-block per row -- the
+// Q4_0 geometry -- (convert_slice_q4k).
 //
 //   Y[M, N] = X[M, K] * W[N, K]^T,  X f16, W ggml Q4_0 (18-byte blocks), Y f16/f32,
 //   for M large enough that the contraction, not the weight stream, bounds
@@ -56,10 +58,13 @@ constexpr int kRawStages = 1;            // raw weight stages
 // Raw weight rows of a 256-k stage: 8 Q4_0 blocks (144 bytes) or 8 Q8_0
 // blocks (272 bytes; its TMA box counts 2-byte elements, a box edge being
 // at most 256 elements).
-template <bool Q8>
-constexpr int kRawRowBytes = Q8 ? 272 : 144;
-template <bool Q8>
-constexpr int kRawBytes = kFT * kRawRowBytes<Q8>;  // 34 KB or 18 KB
+constexpr int kWQ4_0 = 0;  // weight formats of the converter
+constexpr int kWQ8_0 = 1;
+constexpr int kWQ4_K = 2;
+template <int WF>
+constexpr int kRawRowBytes = WF == kWQ8_0 ? 272 : 144;
+template <int WF>
+constexpr int kRawBytes = kFT * kRawRowBytes<WF>;  // 34 KB or 18 KB
 // Converter warps form kConvGroups groups of 8; group g converts the 64-k
 // slices kb with kb % kConvGroups == g, so each group has kConvGroups MMA
 // slices of time per slice it converts.
@@ -83,7 +88,7 @@ constexpr int pow2_at_least(int v) {
 // Shared-memory layout for a token tile of TT (64, 128 or 256) tokens = the
 // MMA's N and the accumulator's TMEM columns: activations TT x 64 k per
 // stage (B).
-template <int TT, bool Q8>
+template <int TT, int WF>
 struct Layout {
     static constexpr int kXBytes = TT * kBK * 2;
     static constexpr int kOffX = 0;
@@ -93,7 +98,7 @@ struct Layout {
     static constexpr int kAColBase = TT;
     static constexpr int kTmemCols = pow2_at_least(TT + kStages * 32);
     static_assert(kTmemCols <= 512, "tensor memory");
-    static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes<Q8>;
+    static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes<WF>;
     // barriers: x_full[S], w_full[S], empty[S], raw_full[R], raw_empty[R], accum
     static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
@@ -374,14 +379,76 @@ __device__ __forceinline__ void convert_block_q8(std::uint32_t raw_row, std::uin
     store_block_tmem(o, taddr);
 }
 
-template <int TT, bool OF32, bool Q8, bool PEERS>
+// Q4_K slice SUB of a 144-byte super-block row (16-byte aligned at
+// `raw_row`: f16 d, f16 dmin, 12 bytes of 6-bit scales and mins, 128 quant
+// bytes): quant bytes [32 SUB, 32 SUB + 32) hold sub-block 2 SUB in their low
+// nibbles (PAR = 0) and 2 SUB + 1 in their high nibbles (PAR = 1).  Each value
+// is (d * sc) * q - dmin * m in f32 -- the product is exact, so this is the
+// published decode's f32 value -- rounded once to f16, into the 16 TMEM
+// columns at `taddr`.
+template <int SUB, int PAR>
+__device__ __forceinline__ void convert_slice_q4k(std::uint32_t raw_row, std::uint32_t taddr) {
+    constexpr int J = 2 * SUB + PAR;  // sub-block
+    std::uint32_t h[4], w[8];
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+                 : "r"(raw_row));
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                     : "r"(raw_row + 16 + 32 * SUB + 16 * c));
+    // scale byte i of the 12 is byte i % 4 of h[1 + i / 4]
+    auto sbyte = [&](int i) { return (h[1 + i / 4] >> (8 * (i % 4))) & 0xFFu; };
+    std::uint32_t sc, m;
+    if constexpr (J < 4) {
+        sc = sbyte(J) & 63u;
+        m = sbyte(J + 4) & 63u;
+    } else {
+        sc = (sbyte(J + 4) & 0x0Fu) | ((sbyte(J - 4) >> 6) << 4);
+        m = (sbyte(J + 4) >> 4) | ((sbyte(J) >> 6) << 4);
+    }
+    const float ds = half_bits_to_float(h[0] & 0xFFFFu) * static_cast<float>(sc);
+    const float ndm = -(half_bits_to_float(h[0] >> 16) * static_cast<float>(m));
+    std::uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const std::uint32_t a = prmt(w[i], 0u, 0x4140u);  // bytes 4i, 4i+1
+        const std::uint32_t b = prmt(w[i], 0u, 0x4342u);  // bytes 4i+2, 4i+3
+        std::uint32_t qa, qb;                             // exact f16 pairs of q
+        if constexpr (PAR == 0) {
+            asm("sub.rn.f16x2 %0, %1, %2;"
+                : "=r"(qa)
+                : "r"(and_or(a, 0x000F000Fu, 0x64006400u)), "r"(0x64006400u));
+            asm("sub.rn.f16x2 %0, %1, %2;"
+                : "=r"(qb)
+                : "r"(and_or(b, 0x000F000Fu, 0x64006400u)), "r"(0x64006400u));
+        } else {
+            asm("sub.rn.f16x2 %0, %1, %2;"
+                : "=r"(qa)
+                : "r"(and_or(a, 0x00F000F0u, 0x54005400u)), "r"(0x54005400u));
+            asm("sub.rn.f16x2 %0, %1, %2;"
+                : "=r"(qb)
+                : "r"(and_or(b, 0x00F000F0u, 0x54005400u)), "r"(0x54005400u));
+        }
+        const float v0 = fmaf(ds, half_bits_to_float(qa & 0xFFFFu), ndm);
+        const float v1 = fmaf(ds, half_bits_to_float(qa >> 16), ndm);
+        const float v2 = fmaf(ds, half_bits_to_float(qb & 0xFFFFu), ndm);
+        const float v3 = fmaf(ds, half_bits_to_float(qb >> 16), ndm);
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o[2 * i]) : "f"(v1), "f"(v0));
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o[2 * i + 1]) : "f"(v3), "f"(v2));
+    }
+    store_block_tmem(o, taddr);
+}
+
+template <int TT, bool OF32, int WF, bool PEERS>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
                              const __grid_constant__ CUtensorMap map_w, const Params p) {
-    using L = Layout<TT, Q8>;
+    using L = Layout<TT, WF>;
     constexpr int kOffX = L::kOffX, kOffRaw = L::kOffRaw, kOffBar = L::kOffBar;
-    constexpr int kRawRow = kRawRowBytes<Q8>;
-    constexpr int kRaw = kRawBytes<Q8>;
+    constexpr int kRawRow = kRawRowBytes<WF>;
+    constexpr int kRaw = kRawBytes<WF>;
     constexpr int kOffTmemSlot = L::kOffTmemSlot, kOffAbort = L::kOffAbort;
     constexpr int kXBytes = L::kXBytes;
     extern __shared__ std::uint8_t smem_raw[];
@@ -449,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // x in the map's elements: bytes (Q4_0) or 2-byte units (Q8_0)
                     tma_load_2d(base + kOffRaw + r * kRaw, &map_w,
                                 static_cast<int>((kb0 / (kSuperK / kBK) + sb) * kRawRow /
-                                                 (Q8 ? 2 : 1)),
+                                                 (WF == kWQ8_0 ? 2 : 1)),
                                 static_cast<int>(n0), smem_u32(&raw_full[r]));
                 }
                 mbar_arrive_expect_tx(&x_full[s], kXBytes);
@@ -506,11 +573,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const std::uint32_t ta = tmem_d + (static_cast<std::uint32_t>(32 * (warp % 4)) << 16) +
                                          static_cast<std::uint32_t>(L::kAColBase + s * 32 +
                                                                     (odd ? 16 : 0));
-                if constexpr (Q8) {
+                if constexpr (WF == kWQ8_0) {
                     if (odd)  // warp-uniform
                         convert_block_q8<SUB, 1>(raw_row, ta);
                     else
                         convert_block_q8<SUB, 0>(raw_row, ta);
+                } else if constexpr (WF == kWQ4_K) {
+                    if (odd)  // warp-uniform
+                        convert_slice_q4k<SUB, 1>(raw_row, ta);
+                    else
+                        convert_slice_q4k<SUB, 0>(raw_row, ta);
                 } else {
                     if (odd)  // warp-uniform
                         convert_half_slice<SUB, 1>(raw_row, ta);
@@ -741,11 +813,11 @@ struct Peers {
     std::uint32_t rank, nranks;
 };
 
-template <int TT, bool OF32, bool Q8, bool PEERS = false>
+template <int TT, bool OF32, int WF, bool PEERS = false>
 int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
                 std::uint64_t K, cudaStream_t stream, void* workspace,
                 std::uint64_t workspace_bytes, const Peers* peers = nullptr) {
-    using L = Layout<TT, Q8>;
+    using L = Layout<TT, WF>;
     auto encode = encode_fn();
     if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
     CUtensorMap map_x{}, map_w{};
@@ -761,22 +833,23 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
             return static_cast<int>(cudaErrorInvalidValue);
     }
     {
-        // Q4_0 rows as bytes; Q8_0 rows as 2-byte units (a 272-byte box edge
-        // is over the 256-element limit); both pitches are multiples of 16
-        const std::uint64_t pitch = (K / 32) * (Q8 ? 34 : 18);
-        const std::uint64_t esize = Q8 ? 2 : 1;
+        // Q4_0 and Q4_K rows as bytes (both 144 bytes per 256 k); Q8_0 rows
+        // as 2-byte units (a 272-byte box edge is over the 256-element
+        // limit); all pitches are multiples of 16
+        const std::uint64_t pitch = (K / 32) * (WF == kWQ8_0 ? 34 : 18);
+        const std::uint64_t esize = WF == kWQ8_0 ? 2 : 1;
         const cuuint64_t dims[2] = {pitch / esize, N};
         const cuuint64_t strides[1] = {pitch};
-        const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRowBytes<Q8> / esize), kFT};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRowBytes<WF> / esize), kFT};
         const cuuint32_t estr[2] = {1, 1};
-        if (encode(&map_w, Q8 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+        if (encode(&map_w, WF == kWQ8_0 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                    const_cast<void*>(w), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return static_cast<int>(cudaErrorInvalidValue);
     }
-    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32, Q8, PEERS>;
+    auto kernel = q4_0_gemm_tcgen05_kernel<TT, OF32, WF, PEERS>;
     static std::atomic<std::uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -869,25 +942,25 @@ inline int launch_handshake_only(const Peers& peers, cudaStream_t stream) {
 inline int launch_peers(const void* x, const void* w, std::uint64_t M, std::uint64_t N,
                         std::uint64_t K, const Peers& peers, cudaStream_t stream) {
     if (M <= 64)
-        return launch_tile<64, false, false, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
+        return launch_tile<64, false, kWQ4_0, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
                                                    &peers);
     if (M <= 128)
-        return launch_tile<128, false, false, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
+        return launch_tile<128, false, kWQ4_0, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
                                                     &peers);
-    return launch_tile<256, false, false, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
+    return launch_tile<256, false, kWQ4_0, true>(x, w, nullptr, M, N, K, stream, nullptr, 0,
                                                 &peers);
 }
 
-// Q8 selects Q8_0 weights instead of Q4_0.
-template <bool OF32, bool Q8 = false>
+// WF selects the weight format: kWQ4_0, kWQ8_0 or kWQ4_K.
+template <bool OF32, int WF = kWQ4_0>
 int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
            std::uint64_t K, cudaStream_t stream, void* workspace = nullptr,
            std::uint64_t workspace_bytes = 0) {
     if (M <= 64)
-        return launch_tile<64, OF32, Q8>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+        return launch_tile<64, OF32, WF>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
     if (M <= 128)
-        return launch_tile<128, OF32, Q8>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
-    return launch_tile<256, OF32, Q8>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+        return launch_tile<128, OF32, WF>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
+    return launch_tile<256, OF32, WF>(x, w, y, M, N, K, stream, workspace, workspace_bytes);
 }
 
 }  // namespace gemm

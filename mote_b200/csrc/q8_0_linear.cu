@@ -362,7 +362,7 @@ int run_linear8(const void* x, const void* w, void* y, std::uint64_t M, std::uin
         return static_cast<int>(cudaMemsetAsync(y, 0, M * N * osz, stream));
     // prefill-shaped problems: the tcgen05 GEMM with Q8_0 conversion
     if (M > static_cast<std::uint64_t>(kMaxTokens) && gemm::supported(x, w, y, M, N, K, osz))
-        return gemm::launch<OF32, true>(x, w, y, M, N, K, stream);
+        return gemm::launch<OF32, gemm::kWQ8_0>(x, w, y, M, N, K, stream);
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
     p.N = static_cast<std::uint32_t>(N);

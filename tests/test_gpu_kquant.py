@@ -10,7 +10,8 @@ tests/test_oracle_kquants.py):
   float64 accumulation of the exactly decoded weights, as the Q4_0 decode
   path.  The Q4_K tensor-core kernel (1-16 tokens per launch, K % 256 == 0,
   16-byte aligned pointers), its split-K groups, ragged N, chunked launches
-  beyond 16 tokens, the f32 output, the Q6_K tensor-core kernel (K % 2048
+  beyond 16 tokens, the tcgen05 prefill path (more than 16 tokens, N % 16 ==
+  0; element-wise 2e-3), the f32 output, the Q6_K tensor-core kernel (K % 2048
   == 0) and the warp-per-row kernel (unaligned input, other K) are covered.
 """
 from __future__ import annotations
@@ -94,11 +95,45 @@ def run(ctx, name, x, w, m, n, k, out_dtype=DType.F16):
     return got
 
 
+def tensor_core_path(name, m, n, k):
+    """More than 16 Q4_K tokens with N % 16 == 0 and K % 256 == 0 run on the
+    tcgen05 GEMM, which rounds each weight's f32 value to f16 once
+    (<= 2^-11 relative): element-wise bound 2e-3 there, as for the Q4_0 and
+    Q8_0 prefill paths."""
+    return name == "q4_k" and m > 16 and n % 16 == 0 and k % 256 == 0
+
+
 def check(oracle_lib, name, got, x, w, m, n, k):
     x32 = x.astype(np.float16).astype(np.float32)
     ref64 = oracle_lib.kquant_linear_f64(x32, w, FMT[name][2], m, n, k)
     assert checker.rel_err_normwise(got, ref64) <= BOUND
-    assert checker.rel_err_elementwise(got, ref64) <= BOUND
+    elementwise = 2e-3 if tensor_core_path(name, m, n, k) else BOUND
+    assert checker.rel_err_elementwise(got, ref64) <= elementwise
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 256, 256), (64, 4096, 4096), (200, 528, 1024),
+                                   (129, 16, 768), (300, 2048, 2048), (40, 2048, 2048)])
+def test_q4_k_prefill_tensor_cores(ctx, oracle_lib, m, n, k):
+    """More than 16 tokens on the tcgen05 GEMM with the Q4_K converter (one
+    144-byte super-block per raw row, each value (d*sc)*q - dmin*m in f32
+    rounded once to f16); ragged M."""
+    w = kquant_weights("q4_k", n, k, seed=60 + m)
+    x = np.random.default_rng(61 + m).normal(0, 1, (m, k)).astype(np.float16)
+    check(oracle_lib, "q4_k", run(ctx, "q4_k", x, w, m, n, k), x, w, m, n, k)
+
+
+def test_q4_k_prefill_full_size_sampled(ctx, oracle_lib):
+    """M=2048, K=4096, N=14336 on the tensor cores; 64 sampled rows x all N
+    against float64 over the oracle's decoded weights."""
+    m, n, k = 2048, 14336, 4096
+    w = kquant_weights("q4_k", n, k, seed=77)
+    x = np.random.default_rng(78).normal(0, 1, (m, k)).astype(np.float16)
+    got = run(ctx, "q4_k", x, w, m, n, k)
+    rows = np.random.default_rng(0).choice(m, 64, replace=False)
+    dec = oracle_lib.kquant_dequantize(w, FMT["q4_k"][2], n, k).astype(np.float64)
+    ref64 = x[rows].astype(np.float64) @ dec.T
+    assert checker.rel_err_normwise(got[rows], ref64) <= BOUND
+    assert checker.rel_err_elementwise(got[rows], ref64) <= 2e-3
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 9, 16, 17, 40])

@@ -576,7 +576,7 @@ class Bench:
         """The K-quant linears (tensor-core decode kernels): lm_head K=4096,
         N=128256 at M in {1, 16} (Q4_K 295.5 MB, Q6_K 431 MB: no rotation
         needed) and N=14336 at M=1 over copies holding >= 2.5x L2; and the
-        Q4_K prefill M=2048, N=14336 on the tcgen05 GEMM (TFLOP/s)."""
+        Q4_K and Q6_K prefill M=2048, N=14336 on the tcgen05 GEMM (TFLOP/s)."""
         torch = self.torch
         k = 4096
         out = {}
@@ -617,6 +617,19 @@ class Bench:
         t = self.time_graph(g, 10, 1)
         del g
         out["q4_k_prefill_m2048_n14336"] = {"us": round(t * 1e3, 1),
+                                             "tflops": round(2 * m * n * k / t / 1e9, 1)}
+        del w
+        w6, _ = self.kquant_weights("q6_k", n, k, seed=6)
+        fn6 = self.lib.mote_cuda_quantized_linear_q6_k_f16
+
+        def runp6():
+            self.check(fn6(x.data_ptr(), w6.data_ptr(), y.data_ptr(), m, n, k, self.stream()),
+                       "q6_k prefill")
+
+        g = self.graph(runp6)
+        t = self.time_graph(g, 10, 1)
+        del g
+        out["q6_k_prefill_m2048_n14336"] = {"us": round(t * 1e3, 1),
                                              "tflops": round(2 * m * n * k / t / 1e9, 1)}
         return out
 

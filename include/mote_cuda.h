@@ -144,8 +144,9 @@ int mote_cuda_quantized_linear_q8_0_f16_f32out(const void* input, const void* we
  * an invalid value; other rules as mote_cuda_quantized_linear_q4_0_f16.
  * Tensor-core decode kernels run up to 16 tokens per launch when the input
  * and weights are 16-byte aligned (Q6_K also needs K % 2048 == 0); more
- * than 16 Q4_K tokens with N % 16 == 0 run on the tcgen05 GEMM (weights
- * rounded to f16 once); other shapes run a warp-per-row kernel. */
+ * than 16 tokens with N % 16 == 0 (and, for Q6_K, K % 2048 == 0) run on
+ * the tcgen05 GEMM (weights rounded to f16 once); other shapes run a
+ * warp-per-row kernel. */
 int mote_cuda_quantized_linear_q4_k_f16(const void* input, const void* weights, void* output,
                                         uint64_t rows, uint64_t output_features,
                                         uint64_t input_features, void* stream);

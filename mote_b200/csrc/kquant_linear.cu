@@ -810,10 +810,12 @@ template <int FMT, bool OF32>
 int run_linear(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
                std::uint64_t K, cudaStream_t stream) {
     const std::size_t osz = OF32 ? 4 : 2;
-    // prefill-shaped Q4_K: the tcgen05 GEMM with the Q4_K converter
-    if constexpr (FMT == kQ4K)
-        if (M > static_cast<std::uint64_t>(kMaxTokens) && gemm::supported(x, w, y, M, N, K, osz))
-            return gemm::launch<OF32, gemm::kWQ4_K>(x, w, y, M, N, K, stream);
+    // prefill-shaped problems: the tcgen05 GEMM with the format's converter
+    // (Q6_K windows need rows of whole 16-byte chunks: K % 2048 == 0)
+    if (M > static_cast<std::uint64_t>(kMaxTokens) && (FMT == kQ4K || K % 2048 == 0) &&
+        gemm::supported(x, w, y, M, N, K, osz))
+        return gemm::launch<OF32, FMT == kQ4K ? gemm::kWQ4_K : gemm::kWQ6_K>(x, w, y, M, N, K,
+                                                                          stream);
     Params p{};
     p.w = static_cast<const std::uint8_t*>(w);
     p.N = static_cast<std::uint32_t>(N);

@@ -1,8 +1,9 @@
-// Prefill-shaped Q4_0 (and Q8_0, Q4_K) GEMM on the 5th-generation tensor
-// cores (tcgen05/TMEM).  The kernel is written for Q4_0; the weight format WF
-// selects the raw rows and the converter: Q8_0 stages hold 272-byte rows
-// (convert_block_q8), Q4_K stages one 144-byte super-block per row -- the
-// Q4_0 geometry -- (convert_slice_q4k).
+// Prefill-shaped Q4_0 (and Q8_0, Q4_K, Q6_K) GEMM on the 5th-generation
+// tensor cores (tcgen05/TMEM).  The kernel is written for Q4_0; the weight
+// format WF selects the raw rows and the converter: Q8_0 stages hold 272-byte
+// rows (convert_block_q8), Q4_K stages one 144-byte super-block per row --
+// the Q4_0 geometry -- (convert_slice_q4k), Q6_K a 240-byte window around
+// each 210-byte super-block (convert_slice_q6k).
 //
 //   Y[M, N] = X[M, K] * W[N, K]^T,  X f16, W ggml Q4_0 (18-byte blocks), Y f16/f32,
 //   for M large enough that the contraction, not the weight stream, bounds
@@ -61,8 +62,15 @@ constexpr int kRawStages = 1;            // raw weight stages
 constexpr int kWQ4_0 = 0;  // weight formats of the converter
 constexpr int kWQ8_0 = 1;
 constexpr int kWQ4_K = 2;
+constexpr int kWQ6_K = 3;
+// Q6_K: a 16-byte-aligned 240-byte window that covers one 210-byte
+// super-block (K % 2048 == 0 keeps every row a whole number of 16-byte
+// chunks; the block starts 2 * (u mod 8) bytes into the window).  224 bytes
+// would cover it, but 240-byte rows (60 words) cut the bank conflicts of the
+// converters' per-row loads from 8-way to 4-way; the window of a row's last
+// block reaches 16 bytes past the row, which the TMA fills with zeros.
 template <int WF>
-constexpr int kRawRowBytes = WF == kWQ8_0 ? 272 : 144;
+constexpr int kRawRowBytes = WF == kWQ8_0 ? 272 : WF == kWQ6_K ? 240 : 144;
 template <int WF>
 constexpr int kRawBytes = kFT * kRawRowBytes<WF>;  // 34 KB or 18 KB
 // Converter warps form kConvGroups groups of 8; group g converts the 64-k
@@ -441,6 +449,59 @@ __device__ __forceinline__ void convert_slice_q4k(std::uint32_t raw_row, std::ui
     store_block_tmem(o, taddr);
 }
 
+// Q6_K slice SUB of a 210-byte super-block at `blk` (2-byte aligned: 128
+// bytes of low nibbles, 64 of 2-bit high parts, 16 int8 scales, f16 d).
+// Elements 64 SUB + 32 PAR + l (l = 0..31) sit in half h = SUB / 2: low
+// nibble (SUB % 2) of ql byte 64h + 32 PAR + l, bit pair 2 (SUB % 2) + PAR of
+// qh byte 32h + l, scale 4 SUB + 2 PAR + l / 16.  Each value is
+// (d * sc) * (q - 32) in f32 as the published decode (d * sc exact, one
+// rounding in the product), rounded once to f16 into the 16 TMEM columns at
+// `taddr`.  Words are read as 2-byte halves (the block is only 2-byte
+// aligned).
+__device__ __forceinline__ std::uint32_t lds_word2(std::uint32_t addr) {
+    std::uint16_t lo, hi;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(lo) : "r"(addr));
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hi) : "r"(addr + 2));
+    return static_cast<std::uint32_t>(lo) | (static_cast<std::uint32_t>(hi) << 16);
+}
+
+template <int SUB, int PAR>
+__device__ __forceinline__ void convert_slice_q6k(std::uint32_t blk, std::uint32_t taddr) {
+    constexpr int h = SUB / 2;
+    constexpr int n = SUB % 2;              // nibble of ql
+    constexpr int j = 2 * (SUB % 2) + PAR;  // bit pair of qh
+    constexpr int kSc = 4 * SUB + 2 * PAR;  // scales of elements 0..15 and 16..31
+    std::uint16_t dbits;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(dbits) : "r"(blk + 208));
+    const float d = half_bits_to_float(dbits);
+    const std::uint32_t scw = lds_word2(blk + 192 + kSc);  // two int8 scales, low half
+    const float ds0 = d * static_cast<float>(static_cast<std::int8_t>(scw & 0xFFu));
+    const float ds1 = d * static_cast<float>(static_cast<std::int8_t>((scw >> 8) & 0xFFu));
+    std::uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const std::uint32_t L = lds_word2(blk + 64 * h + 32 * PAR + 4 * i);
+        const std::uint32_t H = lds_word2(blk + 128 + 32 * h + 4 * i);
+        const std::uint32_t q =
+            ((L >> (4 * n)) & 0x0F0F0F0Fu) | (((H >> (2 * j)) & 0x03030303u) << 4);
+        std::uint32_t qa, qb;  // exact f16 pairs of q - 32
+        asm("sub.rn.f16x2 %0, %1, %2;"
+            : "=r"(qa)
+            : "r"(prmt(q, 0x64646464u, 0x4140u)), "r"(0x64206420u));
+        asm("sub.rn.f16x2 %0, %1, %2;"
+            : "=r"(qb)
+            : "r"(prmt(q, 0x64646464u, 0x4342u)), "r"(0x64206420u));
+        const float ds = i < 4 ? ds0 : ds1;  // elements 4i..4i+3
+        const float v0 = __fmul_rn(ds, half_bits_to_float(qa & 0xFFFFu));
+        const float v1 = __fmul_rn(ds, half_bits_to_float(qa >> 16));
+        const float v2 = __fmul_rn(ds, half_bits_to_float(qb & 0xFFFFu));
+        const float v3 = __fmul_rn(ds, half_bits_to_float(qb >> 16));
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o[2 * i]) : "f"(v1), "f"(v0));
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o[2 * i + 1]) : "f"(v3), "f"(v2));
+    }
+    store_block_tmem(o, taddr);
+}
+
 template <int TT, bool OF32, int WF, bool PEERS>
 __global__ void __launch_bounds__(kThreads, 1)
     q4_0_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_x,
@@ -513,11 +574,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         !wait_or_abort(&raw_empty[r], ((sb / kRawStages) - 1) & 1u, abort_flag))
                         break;
                     mbar_arrive_expect_tx(&raw_full[r], kRaw);
-                    // x in the map's elements: bytes (Q4_0) or 2-byte units (Q8_0)
-                    tma_load_2d(base + kOffRaw + r * kRaw, &map_w,
-                                static_cast<int>((kb0 / (kSuperK / kBK) + sb) * kRawRow /
-                                                 (WF == kWQ8_0 ? 2 : 1)),
-                                static_cast<int>(n0), smem_u32(&raw_full[r]));
+                    // x in the map's elements: bytes (Q4_0, Q4_K) or 2-byte
+                    // units (Q8_0; Q6_K from the window's aligned start)
+                    const std::uint32_t u = kb0 / (kSuperK / kBK) + sb;
+                    const int rx = WF == kWQ6_K  ? static_cast<int>(((u * 210u) & ~15u) / 2)
+                                   : WF == kWQ8_0 ? static_cast<int>(u * kRawRow / 2)
+                                                  : static_cast<int>(u * kRawRow);
+                    tma_load_2d(base + kOffRaw + r * kRaw, &map_w, rx, static_cast<int>(n0),
+                                smem_u32(&raw_full[r]));
                 }
                 mbar_arrive_expect_tx(&x_full[s], kXBytes);
                 tma_load_2d(base + kOffX + s * kXBytes, &map_x,
@@ -583,6 +647,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         convert_slice_q4k<SUB, 1>(raw_row, ta);
                     else
                         convert_slice_q4k<SUB, 0>(raw_row, ta);
+                } else if constexpr (WF == kWQ6_K) {
+                    // the super-block's offset in its window
+                    const std::uint32_t rem = ((kb0 / (kSuperK / kBK) + sb) * 210u) & 15u;
+                    if (odd)  // warp-uniform
+                        convert_slice_q6k<SUB, 1>(raw_row + rem, ta);
+                    else
+                        convert_slice_q6k<SUB, 0>(raw_row + rem, ta);
                 } else {
                     if (odd)  // warp-uniform
                         convert_half_slice<SUB, 1>(raw_row, ta);
@@ -836,13 +907,14 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
         // Q4_0 and Q4_K rows as bytes (both 144 bytes per 256 k); Q8_0 rows
         // as 2-byte units (a 272-byte box edge is over the 256-element
         // limit); all pitches are multiples of 16
-        const std::uint64_t pitch = (K / 32) * (WF == kWQ8_0 ? 34 : 18);
-        const std::uint64_t esize = WF == kWQ8_0 ? 2 : 1;
+        const std::uint64_t pitch =
+            WF == kWQ6_K ? (K / 256) * 210 : (K / 32) * (WF == kWQ8_0 ? 34 : 18);
+        const std::uint64_t esize = WF == kWQ8_0 || WF == kWQ6_K ? 2 : 1;
         const cuuint64_t dims[2] = {pitch / esize, N};
         const cuuint64_t strides[1] = {pitch};
         const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRawRowBytes<WF> / esize), kFT};
         const cuuint32_t estr[2] = {1, 1};
-        if (encode(&map_w, WF == kWQ8_0 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+        if (encode(&map_w, esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                    const_cast<void*>(w), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -951,7 +1023,8 @@ inline int launch_peers(const void* x, const void* w, std::uint64_t M, std::uint
                                                 &peers);
 }
 
-// WF selects the weight format: kWQ4_0, kWQ8_0 or kWQ4_K.
+// WF selects the weight format: kWQ4_0, kWQ8_0, kWQ4_K or kWQ6_K (which
+// also needs K % 2048 == 0).
 template <bool OF32, int WF = kWQ4_0>
 int launch(const void* x, const void* w, void* y, std::uint64_t M, std::uint64_t N,
            std::uint64_t K, cudaStream_t stream, void* workspace = nullptr,

@@ -11,7 +11,7 @@ tests/test_oracle_kquants.py):
   path.  The Q4_K tensor-core kernel (1-16 tokens per launch, K % 256 == 0,
   16-byte aligned pointers), its split-K groups, ragged N, chunked launches
   beyond 16 tokens, the tcgen05 prefill path (more than 16 tokens, N % 16 ==
-  0; element-wise 2e-3), the f32 output, the Q6_K tensor-core kernel (K % 2048
+  0, and K % 2048 == 0 for Q6_K; element-wise 2e-3), the f32 output, the Q6_K tensor-core kernel (K % 2048
   == 0) and the warp-per-row kernel (unaligned input, other K) are covered.
 """
 from __future__ import annotations
@@ -96,11 +96,11 @@ def run(ctx, name, x, w, m, n, k, out_dtype=DType.F16):
 
 
 def tensor_core_path(name, m, n, k):
-    """More than 16 Q4_K tokens with N % 16 == 0 and K % 256 == 0 run on the
-    tcgen05 GEMM, which rounds each weight's f32 value to f16 once
-    (<= 2^-11 relative): element-wise bound 2e-3 there, as for the Q4_0 and
-    Q8_0 prefill paths."""
-    return name == "q4_k" and m > 16 and n % 16 == 0 and k % 256 == 0
+    """More than 16 tokens with N % 16 == 0 and K % 256 == 0 (Q4_K) or
+    K % 2048 == 0 (Q6_K) run on the tcgen05 GEMM, which rounds each weight's
+    f32 value to f16 once (<= 2^-11 relative): element-wise bound 2e-3
+    there, as for the Q4_0 and Q8_0 prefill paths."""
+    return m > 16 and n % 16 == 0 and k % (256 if name == "q4_k" else 2048) == 0
 
 
 def check(oracle_lib, name, got, x, w, m, n, k):
@@ -120,6 +120,17 @@ def test_q4_k_prefill_tensor_cores(ctx, oracle_lib, m, n, k):
     w = kquant_weights("q4_k", n, k, seed=60 + m)
     x = np.random.default_rng(61 + m).normal(0, 1, (m, k)).astype(np.float16)
     check(oracle_lib, "q4_k", run(ctx, "q4_k", x, w, m, n, k), x, w, m, n, k)
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 256, 2048), (64, 4096, 4096), (200, 528, 2048),
+                                   (129, 16, 6144), (300, 2048, 2048), (40, 96, 16384)])
+def test_q6_k_prefill_tensor_cores(ctx, oracle_lib, m, n, k):
+    """More than 16 tokens with K % 2048 == 0 on the tcgen05 GEMM with the Q6_K
+    converter (240-byte TMA windows, each value (d*sc)*(q-32) in f32 rounded
+    once to f16); ragged M, every window offset."""
+    w = kquant_weights("q6_k", n, k, seed=80 + m)
+    x = np.random.default_rng(81 + m).normal(0, 1, (m, k)).astype(np.float16)
+    check(oracle_lib, "q6_k", run(ctx, "q6_k", x, w, m, n, k), x, w, m, n, k)
 
 
 def test_q4_k_prefill_full_size_sampled(ctx, oracle_lib):

@@ -21,9 +21,11 @@
 // * y += d * acc - dmin * mins, f32.
 // Quant byte l of 32-byte group c holds elements 64c + l (low nibble) and
 // 64c + 32 + l (high nibble): lane (g, t) takes word t of each 16-byte half of
-// a group, four consecutive elements per nibble plane, so the activations
-// stay unpermuted (the MMA k positions {2t, 2t+1, 2t+8, 2t+9} take elements
-// 4t..4t+3 of each 16-element step; B is one 8-byte load).
+// a group, four consecutive elements per nibble plane.  A LOP3 on the word
+// (and on the word >> 8) gives the pairs of elements (4t, 4t+2) and (4t+1,
+// 4t+3), so the activations are staged with elements 1 and 2 of every group
+// of four swapped and B stays one 8-byte load (the MMA k positions {2t, 2t+1,
+// 2t+8, 2t+9} take elements 4t, 4t+2, 4t+1, 4t+3 of each 16-element step).
 // The Q6_K GEMV (K % 2048 == 0) is described above its kernel; other shapes
 // run a warp-per-row kernel with f32 accumulation.
 
@@ -207,8 +209,9 @@ __global__ void __launch_bounds__(kThreads, 2) q4_k_gemv_kernel(const Params p) 
     pdl_launch_dependents();
     pdl_wait();
 
-    // stage the activation rows (unpermuted), the per-32-element sums of
-    // each row as f16 (hi, lo) pairs, and an all-zero row of each
+    // stage the activation rows (elements 1 and 2 of every group of four
+    // swapped), the per-32-element sums of each row as f16 (hi, lo) pairs,
+    // and an all-zero row of each
     {
         const std::uint32_t vec_per_row = static_cast<std::uint32_t>(p.K / 8);  // % 32 == 0
         const std::uint32_t nvec = p.M * vec_per_row;
@@ -221,7 +224,10 @@ __global__ void __launch_bounds__(kThreads, 2) q4_k_gemv_kernel(const Params p) 
                 m = i / vec_per_row;
                 v = i - m * vec_per_row;
                 const uint4 val = __ldg(reinterpret_cast<const uint4*>(p.x + m * p.K) + v);
-                *reinterpret_cast<uint4*>(xs + m * p.x_stride + 16 * v) = val;
+                // elements 1 and 2 of every group of four swapped
+                const uint4 pv = make_uint4(prmt(val.x, val.y, 0x5410u), prmt(val.x, val.y, 0x7632u),
+                                            prmt(val.z, val.w, 0x5410u), prmt(val.z, val.w, 0x7632u));
+                *reinterpret_cast<uint4*>(xs + m * p.x_stride + 16 * v) = pv;
                 const std::uint32_t wv[4] = {val.x, val.y, val.z, val.w};
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
@@ -316,8 +322,8 @@ __global__ void __launch_bounds__(kThreads, 2) q4_k_gemv_kernel(const Params p) 
                     std::uint32_t lo[4], hi[4];  // a0..a3 of the low / high plane
 #pragma unroll
                     for (int r = 0; r < 2; ++r) {
-                        const std::uint32_t wa = prmt(w[h][r], 0u, 0x4140u);  // bytes 0, 1
-                        const std::uint32_t wb = prmt(w[h][r], 0u, 0x4342u);  // bytes 2, 3
+                        const std::uint32_t wa = w[h][r];       // bytes 0, 2
+                        const std::uint32_t wb = w[h][r] >> 8;  // bytes 1, 3
                         const std::uint32_t sl = r ? slh : slg, cl = r ? clh : clg;
                         const std::uint32_t su = r ? shh : shg, cu = r ? chh : chg;
                         lo[r] = hfma2_u32(and_or(wa, 0x000F000Fu, 0x64006400u), sl, cl);

@@ -633,6 +633,37 @@ class Bench:
                                              "tflops": round(2 * m * n * k / t / 1e9, 1)}
         return out
 
+    def dense_matmul(self) -> dict:
+        """The dense f16 x f16 -> f32 matmul through cuBLASLt (the HIP
+        backend's hipBLASLt matmul; its bench uses M=N=K in 256..2048):
+        TFLOP/s at M=N=K in {1024, 2048, 4096} with a 32 MiB workspace."""
+        torch = self.torch
+        h = ctypes.c_void_p()
+        self.check(self.lib.mote_cuda_blaslt_create(ctypes.byref(h)), "blaslt create")
+        ws = torch.empty(32 << 20, dtype=torch.uint8, device=self.dev)
+        out = {}
+        try:
+            for s_ in (1024, 2048, 4096):
+                a = self.randn((s_, s_), 11, torch.float16)
+                b = self.randn((s_, s_), 12, torch.float16)
+                c = torch.empty((s_, s_), dtype=torch.float32, device=self.dev)
+
+                def run(a=a, b=b, c=c, s_=s_):
+                    self.check(self.lib.mote_cuda_blaslt_matmul_f16_f32(
+                        h, s_, s_, s_, a.data_ptr(), b.data_ptr(), c.data_ptr(), ws.data_ptr(),
+                        ws.numel(), self.stream()), "blaslt matmul")
+
+                run()  # tunes the shape outside the graph
+                torch.cuda.synchronize()
+                g = self.graph(run)
+                t = self.time_graph(g, 20, 1)
+                del g
+                out[f"mnk{s_}"] = {"us": round(t * 1e3, 1),
+                                   "tflops": round(2 * s_ ** 3 / t / 1e9, 1)}
+        finally:
+            self.lib.mote_cuda_blaslt_destroy(h)
+        return out
+
     def sharded_linear(self, n: int, ms_list, seed: int, k: int = 4096) -> dict:
         """A linear column-sharded over the ranks (strong scaling): per step
         each rank runs the Q4_0 linear on its rows [rank * shard, ...) and the
@@ -815,6 +846,7 @@ class Bench:
             extra["config5"] = self.config5()
             extra["q8_0_linear"] = self.q8_0()
             extra["kquant_linear"] = self.kquant()
+            extra["dense_matmul_f16_f32"] = self.dense_matmul()
         e2e = self.e2e(max(3, min(args.steps, 20)))
         if self.world > 1:
             # the splits the data plane supports: lm_head and FFN up/gate by

@@ -158,6 +158,26 @@ int mote_cuda_quantized_linear_q6_k_f16(const void* input, const void* weights, 
                                         uint64_t rows, uint64_t output_features,
                                         uint64_t input_features, void* stream);
 
+/* Dense row-major matmul through cuBLASLt: the counterpart of the HIP
+ * backend's hipBLASLt shim (crates/mote-backend-hip/src/hipblaslt_shim.cpp:
+ * 326-408; mote_hipblaslt_create / _destroy / _last_error /
+ * _matmul_f16_f32), same arguments and status rules.  create: a context in
+ * *output (-1 for a null output or when cuBLASLt cannot be loaded, else the
+ * library status).  last_error: the message of the context's last failed
+ * call ("" after a success).  matmul: output[m, n] f32 = lhs[m, k] f16 x
+ * rhs[k, n] f16, f32 accumulation, on `stream`; null pointers (stream and
+ * workspace included) return -1; library failures the cuBLAS status; CUDA
+ * failures -1000 - code.  The first call for a new (m, n, k) times the
+ * library's candidate algorithms on the stream (it synchronizes; make it
+ * before any stream capture) and caches the fastest.  m or n == 0 succeeds
+ * without a launch; k == 0 writes zeros.  cuBLASLt is loaded with dlopen. */
+int mote_cuda_blaslt_create(void** output);
+void mote_cuda_blaslt_destroy(void* context);
+const char* mote_cuda_blaslt_last_error(void* context);
+int mote_cuda_blaslt_matmul_f16_f32(void* context, uint64_t m, uint64_t n, uint64_t k,
+                                    const void* lhs, const void* rhs, void* output,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* Decodes a [rows, k] Q4_K (format 2) or Q6_K (format 3) matrix into f32
  * values [rows, k], bit-identical to ggml's published decode (each element
  * one separately rounded f32 expression).  Format ids follow mote-types'

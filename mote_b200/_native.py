@@ -56,6 +56,10 @@ SIGNATURES: dict[str, tuple] = {
     "mote_cuda_quantized_linear_q4_k_f16_f32out": (I, [P, P, P, U64, U64, U64, P]),
     "mote_cuda_quantized_linear_q6_k_f16": (I, [P, P, P, U64, U64, U64, P]),
     "mote_cuda_kquant_dequantize_f32": (I, [I, P, P, U64, U64, P]),
+    "mote_cuda_blaslt_create": (I, [ctypes.POINTER(P)]),
+    "mote_cuda_blaslt_destroy": (None, [P]),
+    "mote_cuda_blaslt_last_error": (ctypes.c_char_p, [P]),
+    "mote_cuda_blaslt_matmul_f16_f32": (I, [P, U64, U64, U64, P, P, P, P, SZ, P]),
     "mote_cuda_quantized_linear_q4_0_f16_ws": (I, [P, P, P, U64, U64, U64, P, U64, P]),
     "mote_cuda_q4_0_linear_workspace_bytes": (I, [U64, U64, U64, ctypes.POINTER(U64)]),
     "mote_cuda_quantized_linear_q4_0_f16_noalloc": (I, [P, P, P, U64, U64, U64, P]),

@@ -55,6 +55,10 @@ class _ContextInner:
         if self.stream:
             lib().mote_cuda_set_device(self.ordinal)
             lib().mote_cuda_stream_synchronize(self.stream)
+            state = getattr(self, "blas_state", None)
+            if state is not None:
+                lib().mote_cuda_blaslt_destroy(state[0])
+                self.blas_state = None
             lib().mote_cuda_stream_destroy(self.stream)
             self.stream = None
 
@@ -203,6 +207,24 @@ class CudaContext:
         self.sync()
         errors.check(lib().mote_cuda_memcpy_host_to_device(tensor.pointer, buf.ctypes.data,
                                                            buf.nbytes), "upload")
+
+    # the dense-matmul library context and its workspace (context.rs:11, 42:
+    # 32 MiB, as the HIP backend), made on first use
+    BLAS_WORKSPACE_BYTES = 32 * 1024 * 1024
+
+    def blas(self) -> tuple[int, int, int]:
+        """(cuBLASLt context, workspace pointer, workspace bytes)."""
+        state = getattr(self.inner, "blas_state", None)
+        if state is None:
+            self.inner.select()
+            handle = ctypes.c_void_p()
+            st = lib().mote_cuda_blaslt_create(ctypes.byref(handle))
+            if st != 0:
+                raise errors.BlasLt(operation="create", status=int(st),
+                                    message="cuBLASLt could not be started")
+            ws = CudaStorage(self.inner, self.BLAS_WORKSPACE_BYTES)
+            state = self.inner.blas_state = (handle.value, ws)
+        return state[0], state[1].pointer, state[1].size_bytes
 
     def linear_workspace_bytes(self, rows: int, n: int, k: int) -> int:
         """mote_cuda_q4_0_linear_workspace_bytes for a shape, memoised (it

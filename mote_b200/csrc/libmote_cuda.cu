@@ -9,3 +9,4 @@
 #include "layer_ops.cu"
 #include "q4_0_codec.cu"
 #include "comm.cu"
+#include "dense_matmul.cu"

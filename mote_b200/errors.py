@@ -97,6 +97,15 @@ class InvalidEpsilon(CudaError):
     pass
 
 
+class BlasLt(CudaError):
+    """``HipError::BlasLt`` (error.rs:14-19): the dense-matmul library call
+    failed; ``message`` is the context's last-error text."""
+
+
+class MatmulDimensionsTooLarge(CudaError):
+    """``HipError::MatmulDimensionsTooLarge`` (error.rs:79-80)."""
+
+
 class IndexOutOfRange(CudaError):
     """An embedding id was outside [0, vocab) (no reference counterpart)."""
 

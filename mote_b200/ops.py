@@ -236,6 +236,36 @@ def kquant_decode_f32(context: CudaContext, weights: Tensor, output: Tensor) -> 
                                                        context.stream), "decode K-quant matrix")
 
 
+def matmul_f16_f32(context: CudaContext, lhs: Tensor, rhs: Tensor, output: Tensor) -> None:
+    """``output[m, n] = lhs[m, k] @ rhs[k, n]``: row-major f16 inputs, f32
+    accumulation and output, through cuBLASLt (the HIP backend's
+    ``matmul_f16_f32``, crates/mote-backend-hip/src/matmul.rs:11-113, same
+    checks).  The first call of a new (m, n, k) tunes and caches an
+    algorithm, synchronizing the stream: make it before any graph capture."""
+    for t, name, dt in ((lhs, "lhs", DType.F16), (rhs, "rhs", DType.F16),
+                        (output, "output", DType.F32)):
+        _plain(t, name, dt)
+        _rank(t, name, 2)
+    m, k = lhs.shape
+    rk, n = rhs.shape
+    if rk != k:
+        raise errors.ShapeMismatch(tensor="rhs", expected=(k, n), actual=rhs.shape)
+    _shape(output, "output", (m, n))
+    if m * n == 0:
+        return
+    if max(m, n, k) > 0x7FFFFFFFFFFFFFFF:
+        raise errors.MatmulDimensionsTooLarge(m=m, n=n, k=k)
+    l_s, r_s, o_s = (context.storage(t) for t in (lhs, rhs, output))
+    handle, ws, ws_bytes = context.blas()
+    context.inner.select()
+    st = lib().mote_cuda_blaslt_matmul_f16_f32(handle, m, n, k, l_s.pointer, r_s.pointer,
+                                                o_s.pointer, ws, ws_bytes, context.stream)
+    if st != 0:
+        msg = lib().mote_cuda_blaslt_last_error(handle)
+        raise errors.BlasLt(operation="matmul", status=int(st),
+                            message=(msg or b"").decode(errors="replace"))
+
+
 def quantized_linear_q4_0_f32(context: CudaContext, input: Tensor, weights: Tensor,
                               output: Tensor) -> None:
     """f32 in, f32 out (device counterpart of ``quantized_linear_f32``)."""

@@ -214,3 +214,12 @@ def test_kquant_argument_rules(lib):
     assert dq(3, FAKE, FAKE, 1, 320, STREAM) == 1                # k % 256
     assert dq(3, FAKE, FAKE, 1, 256, None) == 1
     assert dq(2, FAKE, FAKE, 0, 256, STREAM) == 0
+
+
+def test_blaslt_argument_rules(lib):
+    # null context / output: -1 before any library call (hipblaslt_shim.cpp:326-408)
+    assert lib.mote_cuda_blaslt_create(None) == -1
+    assert lib.mote_cuda_blaslt_matmul_f16_f32(None, 1, 1, 1, FAKE, FAKE, FAKE, FAKE, 64,
+                                               STREAM) == -1
+    assert lib.mote_cuda_blaslt_last_error(None) is None
+    lib.mote_cuda_blaslt_destroy(None)

@@ -456,8 +456,8 @@ __device__ __forceinline__ void convert_slice_q4k(std::uint32_t raw_row, std::ui
 // qh byte 32h + l, scale 4 SUB + 2 PAR + l / 16.  Each value is
 // (d * sc) * (q - 32) in f32 as the published decode (d * sc exact, one
 // rounding in the product), rounded once to f16 into the 16 TMEM columns at
-// `taddr`.  Words are read as 2-byte halves (the block is only 2-byte
-// aligned).
+// `taddr`.  The block is only 2-byte aligned: odd blocks (MIS) take their
+// words from aligned neighbours.
 __device__ __forceinline__ std::uint32_t lds_word2(std::uint32_t addr) {
     std::uint16_t lo, hi;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(lo) : "r"(addr));
@@ -465,7 +465,24 @@ __device__ __forceinline__ std::uint32_t lds_word2(std::uint32_t addr) {
     return static_cast<std::uint32_t>(lo) | (static_cast<std::uint32_t>(hi) << 16);
 }
 
-template <int SUB, int PAR>
+// 8 consecutive words at `addr`, which is word-aligned, or (MIS) 2 bytes
+// past a word: then 9 aligned words are loaded and each output word is a
+// PRMT of two neighbours.
+template <bool MIS>
+__device__ __forceinline__ void lds_words8(std::uint32_t addr, std::uint32_t (&w)[8]) {
+    if constexpr (MIS) {
+        std::uint32_t a[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) a[i] = lds32(addr - 2 + 4 * i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = prmt(a[i], a[i + 1], 0x5432u);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = lds32(addr + 4 * i);
+    }
+}
+
+template <int SUB, int PAR, bool MIS>
 __device__ __forceinline__ void convert_slice_q6k(std::uint32_t blk, std::uint32_t taddr) {
     constexpr int h = SUB / 2;
     constexpr int n = SUB % 2;              // nibble of ql
@@ -477,11 +494,14 @@ __device__ __forceinline__ void convert_slice_q6k(std::uint32_t blk, std::uint32
     const std::uint32_t scw = lds_word2(blk + 192 + kSc);  // two int8 scales, low half
     const float ds0 = d * static_cast<float>(static_cast<std::int8_t>(scw & 0xFFu));
     const float ds1 = d * static_cast<float>(static_cast<std::int8_t>((scw >> 8) & 0xFFu));
+    std::uint32_t Lw[8], Hw[8];
+    lds_words8<MIS>(blk + 64 * h + 32 * PAR, Lw);
+    lds_words8<MIS>(blk + 128 + 32 * h, Hw);
     std::uint32_t o[16];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const std::uint32_t L = lds_word2(blk + 64 * h + 32 * PAR + 4 * i);
-        const std::uint32_t H = lds_word2(blk + 128 + 32 * h + 4 * i);
+        const std::uint32_t L = Lw[i];
+        const std::uint32_t H = Hw[i];
         const std::uint32_t q =
             ((L >> (4 * n)) & 0x0F0F0F0Fu) | (((H >> (2 * j)) & 0x03030303u) << 4);
         std::uint32_t qa, qb;  // exact f16 pairs of q - 32
@@ -650,10 +670,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else if constexpr (WF == kWQ6_K) {
                     // the super-block's offset in its window
                     const std::uint32_t rem = ((kb0 / (kSuperK / kBK) + sb) * 210u) & 15u;
-                    if (odd)  // warp-uniform
-                        convert_slice_q6k<SUB, 1>(raw_row + rem, ta);
-                    else
-                        convert_slice_q6k<SUB, 0>(raw_row + rem, ta);
+                    if (rem & 2u) {  // warp-uniform, as `odd`
+                        if (odd)
+                            convert_slice_q6k<SUB, 1, true>(raw_row + rem, ta);
+                        else
+                            convert_slice_q6k<SUB, 0, true>(raw_row + rem, ta);
+                    } else {
+                        if (odd)
+                            convert_slice_q6k<SUB, 1, false>(raw_row + rem, ta);
+                        else
+                            convert_slice_q6k<SUB, 0, false>(raw_row + rem, ta);
+                    }
                 } else {
                     if (odd)  // warp-uniform
                         convert_half_slice<SUB, 1>(raw_row, ta);

@@ -866,15 +866,7 @@ class Bench:
                 "scaling": "weak", "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (seeded N(0,0.02) weights Q4_0-encoded on device, "
                         "N(0,1) f16 activations)",
-                "config": {
-                    "workload": "config3 batch-decode sweep: Q4_0 linear M in {1,2,4,8,16} x "
-                                "N in {4096,11008,14336}, K=4096, f16 act, f32 acc, f16 out "
-                                "(mote_cuda_quantized_linear_q4_0_f16_ws, one workspace)",
-                    "weight_copies_per_n": {str(n): len(self.sweep_w[n]) for n in SWEEP_N},
-                    "l2": "inputs larger than L2: each case rotates over copies holding "
-                          ">= 2.5x L2 (126 MB)",
-                    "parallelism": f"replicas x{self.world}" if self.world > 1 else "single GPU",
-                    "timing": "CUDA graph per step, CUDA events, max over ranks"},
+                "config": sweep_config(self.world),
                 "roofline": {
                     "bound": "hbm", "achieved": round(achieved, 1),
                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -918,79 +910,115 @@ def traffic_ratio():
 
 
 # --------------------------------------------------------------------------
-def cpu_sample(k: int = SWEEP_K, rows: int = 512):
+CPU_SAMPLE_ROWS = 512
+
+
+def sweep_config(world: int) -> dict:
+    """The `config` of the headline line, shared by both arms."""
+    return {
+        "workload": "config3 batch-decode sweep: Q4_0 linear M in {1,2,4,8,16} x "
+                    "N in {4096,11008,14336}, K=4096, f16 act, f32 acc, f16 out "
+                    "(mote_cuda_quantized_linear_q4_0_f16_ws, one workspace)",
+        "weight_copies_per_n": {str(n): copies_for(q4_bytes(n, SWEEP_K)) for n in SWEEP_N},
+        "l2": "inputs larger than L2: each case rotates over copies holding "
+              ">= 2.5x L2 (126 MB)",
+        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+        "timing": "CUDA graph per step, CUDA events, max over ranks"}
+
+
+def cpu_sample(k: int = SWEEP_K, rows: int = CPU_SAMPLE_ROWS):
     """A bounded slice of the config-3 sweep for the CPU oracle: the first
-    `rows` output features of the N=4096 matrix, for every M of the sweep."""
+    `rows` output features of each of the three N's matrices (seeded
+    N(0, 0.02) weights, Q4_0-encoded) and the f16-valued activations of
+    every M of the sweep.  The slice has every case of the sweep, each with
+    the same number of rows, so per-row work (a K=4096 decode and M dot
+    products) is weighted as in the full sweep."""
     import numpy as np
 
     from oracle import ref
 
     rng = np.random.default_rng(4096)
-    w = ref.q4_0_quantize(rng.normal(0, 0.02, (rows, k)).astype(np.float32), rows, k)
+    ws = {}
+    for n in SWEEP_N:
+        ws[n] = ref.q4_0_quantize(rng.normal(0, 0.02, (rows, k)).astype(np.float32), rows, k)
     xs = {m: rng.normal(0, 1, (m, k)).astype(np.float16).astype(np.float32) for m in SWEEP_M}
-    return w, xs
+    return ws, xs
+
+
+def cpu_sample_bytes(k: int = SWEEP_K, rows: int = CPU_SAMPLE_ROWS) -> int:
+    """Algorithmic bytes of one pass over the sample (weights once per call,
+    x and y), the headline's byte count restricted to the sampled rows."""
+    return sum(linear_bytes(m, rows, k) for m in SWEEP_M for _ in SWEEP_N)
+
+
+def cpu_pass(ws, xs, threads: int, k: int = SWEEP_K, rows: int = CPU_SAMPLE_ROWS) -> None:
+    from oracle import ref
+
+    for m in SWEEP_M:
+        for n in SWEEP_N:
+            ref.quantized_linear_f32(xs[m], ws[n], ref.Q4_0, m, rows, k, threads=threads)
+
+
+def cpu_sample_text(rows: int, threads: int, passes: int | None = None) -> str:
+    head = f"{passes} passes of " if passes is not None else "per step: "
+    return (f"{head}the 15 config-3 cases (M in {{1,2,4,8,16}} x N in {{4096,11008,14336}}, "
+            f"K=4096), each on the first {rows} output features of its N, through "
+            f"quantized_linear_f32 (mote-reference crates/mote-reference/src/quantized.rs:89-144 "
+            f"restated in C, oracle/), {threads} thread(s)")
 
 
 def cpu_baseline(budget_s: float = 10.0, threads: int = 1) -> dict:
+    """The reference's CPU path, single-threaded as mote-reference's
+    quantized_linear_f32 is (crates/mote-reference/src/quantized.rs:127-142),
+    timed on this host over a bounded sample of the sweep."""
     from oracle import ref
 
     ref.build()
-    rows, k = 512, SWEEP_K
-    w, xs = cpu_sample(k, rows)
-    per_pass = sum(linear_bytes(m, rows, k) for m in SWEEP_M)
+    ws, xs = cpu_sample()
+    per_pass = cpu_sample_bytes()
+    cpu_pass(ws, xs, threads)  # warm-up
     passes = 0
     t0 = time.perf_counter()
     while True:
-        for m in SWEEP_M:
-            ref.quantized_linear_f32(xs[m], w, ref.Q4_0, m, rows, k, threads=threads)
+        cpu_pass(ws, xs, threads)
         passes += 1
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
     return {"value": round(per_pass * passes / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
-            "kind": "port",
-            "sample": f"mote-reference quantized_linear_f32 restated in C (oracle/), "
-                      f"{passes} passes of M in {{1,2,4,8,16}} x first {rows} rows of the "
-                      f"N=4096, K=4096 config-3 matrix ({budget_s:.0f} s budget), "
-                      f"{threads} thread(s)"}
+            "kind": "port" if threads == 1 else "ours",
+            "sample": cpu_sample_text(CPU_SAMPLE_ROWS, threads, passes)}
 
 
 def run_reference(args) -> None:
-    """Reference arm: the oracle (mote-reference restated in C; the Rust crate
-    cannot be built here) on the host cores with all threads, on the same
-    metric, in bounded per-step samples."""
+    """Reference arm: mote-reference's CPU linear (restated in C in oracle/;
+    the Rust crate cannot be built here), single-threaded as the reference
+    is, on the same metric and config as our arm, each step one pass over a
+    bounded sample of the sweep (every case, the first rows of each N)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import ref
 
-    threads = ref.host_threads()
-    rows, k = 512, SWEEP_K
-    w, xs = cpu_sample(k, rows)
-    per_step = sum(linear_bytes(m, rows, k) for m in SWEEP_M)
-
-    def step():
-        for m in SWEEP_M:
-            ref.quantized_linear_f32(xs[m], w, ref.Q4_0, m, rows, k, threads=threads)
-
+    ref.build()
+    threads = 1
+    ws, xs = cpu_sample()
+    per_step = cpu_sample_bytes()
     for _ in range(args.warmup):
-        step()
+        cpu_pass(ws, xs, threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        cpu_pass(ws, xs, threads)
     dt = time.perf_counter() - t0
     value = per_step * args.steps / dt / 1e9
-    sample = (f"per step: M in {{1,2,4,8,16}} x first {rows} rows of the N=4096, K=4096 "
-              f"config-3 Q4_0 matrix through quantized_linear_f32 (C restatement of "
-              f"mote-reference), {threads} threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config3 batch-decode sweep (row sample)", "sample_rows": rows},
+        "config": sweep_config(args.gpus),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": cpu_sample_text(CPU_SAMPLE_ROWS, threads)},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)

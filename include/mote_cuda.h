@@ -196,7 +196,7 @@ int mote_cuda_kquant_dequantize_f32(int format, const void* weights, void* outpu
  * timing).  On the tensor-core path (more than 16 tokens), the tiles of a
  * partial last wave are split along K instead, their f32 parts stored past
  * the counters and added in part order by a second kernel.  A null or too
- * small workspace gives the unsplit kernels.  Calls sharing a workspace must
+ * small workspace gives the unsplit kernels (for either split).  Calls sharing a workspace must
  * not overlap.  No reference counterpart; argument rules as
  * mote_cuda_quantized_linear_q4_0_f16, plus an unaligned workspace -> 1. */
 int mote_cuda_quantized_linear_q4_0_f16_ws(const void* input, const void* weights, void* output,
@@ -206,13 +206,20 @@ int mote_cuda_quantized_linear_q4_0_f16_ws(const void* input, const void* weight
 /* mote_cuda_quantized_linear_q4_0_f16_ws without a workspace argument, for
  * callers that cannot allocate or pass one (a kernel reached through
  * mote-kernel's KernelImpl::launch gets only its opaque argument words).  No
- * reference counterpart.  The split-K scratch is a static 8 MiB device
- * array per device, zero at load and left zero by every call; no memory is
- * allocated.  A request whose split needs more scratch returns 10200 before
- * anything is enqueued.  Calls on the same device must not overlap (one
- * scratch per device, shared by all streams).  The first call on a device
- * looks up the scratch address and must be made before any stream capture
- * that includes this entry point. */
+ * reference counterpart.  The split scratch is a static 8 MiB device array
+ * per device, zero at load and left zero by every call; no memory is
+ * allocated.  Limits:
+ *  - decode shapes (at most 16 tokens per launch): a request whose K split
+ *    over CTAs needs more than the scratch returns 10200 before anything is
+ *    enqueued -- even where the unsplit kernel would have run;
+ *  - prefill shapes (more than 16 tokens, the tensor-core GEMM): a partial
+ *    last wave whose K split needs more than the scratch runs unsplit;
+ *  - device ordinals of 64 and above return 1;
+ *  - calls on the same device must not overlap (one scratch per device,
+ *    shared by all streams);
+ *  - the first call on a device from a CUDA context (again after a
+ *    cudaDeviceReset) looks up the scratch address and must be made before
+ *    any stream capture that includes this entry point. */
 int mote_cuda_quantized_linear_q4_0_f16_noalloc(const void* input, const void* weights,
                                                 void* output, uint64_t rows,
                                                 uint64_t output_features, uint64_t input_features,

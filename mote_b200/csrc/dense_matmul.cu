@@ -80,6 +80,7 @@ struct Plan {
     cublasLtMatmulDesc_t op = nullptr;
     cublasLtMatrixLayout_t rhs = nullptr, lhs = nullptr, out = nullptr;
     cublasLtMatmulAlgo_t algo{};
+    std::size_t ws_need = 0;  // workspace the chosen algorithm needs
     ~Plan() {
         const Api& a = api();
         if (rhs) a.layout_destroy(rhs);
@@ -91,7 +92,9 @@ struct Plan {
 
 struct Context {
     cublasLtHandle_t handle = nullptr;
-    std::map<std::array<std::uint64_t, 3>, std::unique_ptr<Plan>> plans;
+    // plans per (m, n, k, pointer alignment); a plan tuned under a larger
+    // workspace limit than a later call offers is tuned again
+    std::map<std::array<std::uint64_t, 4>, std::unique_ptr<Plan>> plans;
     std::string last_error;
     ~Context() {
         plans.clear();
@@ -116,6 +119,14 @@ inline cublasStatus_t enqueue(const Context& c, const Plan& plan, const void* lh
                         plan.out, out, plan.out, &plan.algo, ws, ws_bytes, s);
 }
 
+// Largest power of two (at most 256) dividing every operand address.
+inline std::uint64_t operand_alignment(const void* lhs, const void* rhs, const void* out) {
+    const std::uintptr_t bits = reinterpret_cast<std::uintptr_t>(lhs) |
+                                reinterpret_cast<std::uintptr_t>(rhs) |
+                                reinterpret_cast<std::uintptr_t>(out) | 256u;
+    return static_cast<std::uint64_t>(bits & (~bits + 1));
+}
+
 inline int make_plan(Context* c, std::uint64_t m, std::uint64_t n, std::uint64_t k,
                      const void* lhs, const void* rhs, void* out, void* ws, std::size_t ws_bytes,
                      cudaStream_t s, std::unique_ptr<Plan>& result) {
@@ -134,6 +145,13 @@ inline int make_plan(Context* c, std::uint64_t m, std::uint64_t n, std::uint64_t
     if (st != CUBLAS_STATUS_SUCCESS) return fail(c, st, "cublasLtMatmulPreferenceCreate failed");
     const std::uint64_t limit = ws_bytes;
     st = a.pref_set(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &limit, sizeof(limit));
+    // only algorithms valid for these operands' alignment
+    const std::uint32_t align = static_cast<std::uint32_t>(operand_alignment(lhs, rhs, out));
+    for (const auto attr : {CUBLASLT_MATMUL_PREF_MIN_ALIGNMENT_A_BYTES,
+                            CUBLASLT_MATMUL_PREF_MIN_ALIGNMENT_B_BYTES,
+                            CUBLASLT_MATMUL_PREF_MIN_ALIGNMENT_C_BYTES,
+                            CUBLASLT_MATMUL_PREF_MIN_ALIGNMENT_D_BYTES})
+        if (st == CUBLAS_STATUS_SUCCESS) st = a.pref_set(pref, attr, &align, sizeof(align));
     if (st != CUBLAS_STATUS_SUCCESS) {
         a.pref_destroy(pref);
         return fail(c, st, "cublasLtMatmulPreferenceSetAttribute failed");
@@ -158,6 +176,7 @@ inline int make_plan(Context* c, std::uint64_t m, std::uint64_t n, std::uint64_t
     float best = std::numeric_limits<float>::infinity();
     bool found = false;
     cublasLtMatmulAlgo_t best_algo{};
+    std::size_t best_ws = 0;
     for (int i = 0; i < count; ++i) {
         if (cand[i].state != CUBLAS_STATUS_SUCCESS || cand[i].workspaceSize > ws_bytes) continue;
         plan->algo = cand[i].algo;
@@ -171,6 +190,7 @@ inline int make_plan(Context* c, std::uint64_t m, std::uint64_t n, std::uint64_t
         if (ms < best) {
             best = ms;
             best_algo = cand[i].algo;
+            best_ws = cand[i].workspaceSize;
             found = true;
         }
     }
@@ -178,6 +198,7 @@ inline int make_plan(Context* c, std::uint64_t m, std::uint64_t n, std::uint64_t
     cudaEventDestroy(stop);
     if (!found) return fail(c, kInternalError, "no cuBLASLt algorithm ran for this shape");
     plan->algo = best_algo;
+    plan->ws_need = best_ws;
     result = std::move(plan);
     return 0;
 }
@@ -241,14 +262,18 @@ extern "C" int mote_cuda_blaslt_matmul_f16_f32(void* opaque, std::uint64_t m, st
         return 0;
     }
     try {
-        const std::array<std::uint64_t, 3> key{m, n, k};
+        const std::array<std::uint64_t, 4> key{m, n, k, operand_alignment(lhs, rhs, output)};
         auto it = c->plans.find(key);
-        if (it == c->plans.end()) {
+        if (it == c->plans.end() || it->second->ws_need > workspace_bytes) {
+            // new shape, or a plan that needs more workspace than this call has
             std::unique_ptr<Plan> plan;
             const int st = make_plan(c, m, n, k, lhs, rhs, output, workspace, workspace_bytes, s,
                                      plan);
             if (st != 0) return st;
-            it = c->plans.emplace(key, std::move(plan)).first;
+            if (it == c->plans.end())
+                it = c->plans.emplace(key, std::move(plan)).first;
+            else
+                it->second = std::move(plan);
         }
         const cublasStatus_t st =
             enqueue(*c, *it->second, lhs, rhs, output, workspace, workspace_bytes, s);

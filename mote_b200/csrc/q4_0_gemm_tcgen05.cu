@@ -890,13 +890,14 @@ inline SplitPlan plan_split(std::uint64_t tiles, std::uint64_t K, std::uint64_t 
 // Resident CTAs per SM of a kernel (cached per device ordinal).
 template <typename Kernel>
 int ctas_per_sm(Kernel kernel, int smem, std::atomic<int> (&cache)[64], int dev) {
-    int v = cache[dev & 63].load(std::memory_order_relaxed);
+    const bool cached = dev >= 0 && dev < 64;  // higher ordinals are looked up every call
+    int v = cached ? cache[dev].load(std::memory_order_relaxed) : 0;
     if (v == 0) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kThreads, smem) !=
                 cudaSuccess ||
             v <= 0)
             v = 1;
-        cache[dev & 63].store(v, std::memory_order_relaxed);
+        if (cached) cache[dev].store(v, std::memory_order_relaxed);
     }
     return v;
 }
@@ -953,8 +954,9 @@ int launch_tile(const void* x, const void* w, void* y, std::uint64_t M, std::uin
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_cast<int>(e);
-    const std::uint64_t bit = 1ull << (dev & 63);
-    if (!(configured.load() & bit)) {
+    // the attribute is per device: set once per ordinal below 64, every call above
+    const std::uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0;
+    if (bit == 0 || !(configured.load() & bit)) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  L::kSmemBytes);
         if (e != cudaSuccess) return static_cast<int>(e);

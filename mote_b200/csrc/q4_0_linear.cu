@@ -48,7 +48,10 @@
 
 #include "mote_common.cuh"
 
+#include <cuda.h>
+
 #include <atomic>
+#include <mutex>
 #include <type_traits>
 
 namespace mote {
@@ -874,14 +877,15 @@ __global__ void __launch_bounds__(128) q4_0_linear_generic_kernel(const Params p
 // Host dispatch
 // ---------------------------------------------------------------------------
 // Opts a kernel into more than 48 KB of dynamic shared memory, once per
-// device (the attribute is per device; `done` is a bit mask of ordinals).
+// device (the attribute is per device; `done` is a bit mask of ordinals below
+// 64; higher ordinals set it on every call).
 template <typename Kernel>
 int ensure_smem_attribute(Kernel kernel, int bytes, std::atomic<std::uint64_t>& done) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_cast<int>(e);
-    const std::uint64_t bit = 1ull << (dev & 63);
-    if (done.load(std::memory_order_acquire) & bit) return kSuccess;
+    const std::uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return kSuccess;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     done.fetch_or(bit, std::memory_order_acq_rel);
@@ -893,11 +897,12 @@ inline int sm_count() {
     static std::atomic<int> cache[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    int v = cache[dev & 63].load(std::memory_order_relaxed);
+    const bool cached = dev >= 0 && dev < 64;
+    int v = cached ? cache[dev].load(std::memory_order_relaxed) : 0;
     if (v == 0) {
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
             v = 148;
-        cache[dev & 63].store(v, std::memory_order_relaxed);
+        if (cached) cache[dev].store(v, std::memory_order_relaxed);
     }
     return v;
 }
@@ -1495,33 +1500,78 @@ extern "C" int mote_cuda_q4_0_linear_workspace_bytes(std::uint64_t rows,
 // resolved through mote-kernel's KernelImpl::launch, which receives only the
 // opaque argument words -- the split-K scratch is a file-scope device array,
 // one per device, zero at module load (its tile counters must be zero before
-// a call, and every call leaves them zero).  Its address is looked up once
-// per device with cudaGetSymbolAddress; no memory is allocated.  Limits:
-// kNoAllocScratchBytes of scratch per device -- a request whose K split
-// needs more returns kScratchTooSmall (10200) before anything is enqueued --
-// and one scratch per device, so calls on that device must not overlap (on
-// any stream).  The first call on a device performs the lookup and must be
-// made before any stream capture that includes this entry point.  No
-// reference counterpart.
+// a call, and every call leaves them zero).  Its address is looked up with
+// cudaGetSymbolAddress the first time a device is used from a CUDA context
+// and again whenever that device's current context changes (after a
+// cudaDeviceReset the module, and with it the array, is loaded anew); no
+// memory is allocated.  Limits: kNoAllocScratchBytes of scratch per device;
+// on the decode path (at most 16 tokens per launch) a request whose K split
+// needs more returns kScratchTooSmall (10200) before anything is enqueued,
+// even where an unsplit launch would fit, while prefill shapes (more than 16
+// tokens, the tensor-core GEMM) run their last wave unsplit instead; device
+// ordinals from kNoAllocDevices up are rejected (1); and one scratch per
+// device, so calls on that device must not overlap (on any stream).  The
+// first call on a device performs the lookup and must be made before any
+// stream capture that includes this entry point.  No reference counterpart.
 // ---------------------------------------------------------------------------
 namespace mote {
 namespace q4 {
 constexpr std::uint64_t kNoAllocScratchBytes = 8ull << 20;  // 8 MiB per device
+constexpr int kNoAllocDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Address of this device's scratch (cached per device ordinal).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+template <typename Fn>
+Fn driver_fn(const char* name) {
+    void* sym = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &sym, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+        return reinterpret_cast<Fn>(sym);
+    return nullptr;
+}
+
+// Unique id of the calling thread's current context (0 if there is none).
+inline unsigned long long current_context_id() {
+    static const CtxGetCurrentFn get = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+    static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+    CUcontext cur = nullptr;
+    unsigned long long id = 0;
+    if (get == nullptr || get_id == nullptr || get(&cur) != CUDA_SUCCESS || cur == nullptr ||
+        get_id(cur, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// Address of this device's scratch, cached per device ordinal together with
+// the id of the context it was looked up in (context ids are never reused,
+// unlike context handles).
 inline int noalloc_scratch(void** out) {
-    static std::atomic<void*> cache[64];
+    struct Slot {
+        std::mutex lock;
+        unsigned long long ctx = 0;
+        void* addr = nullptr;
+    };
+    static Slot slots[kNoAllocDevices];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_cast<int>(e);
-    void* p = cache[dev & 63].load(std::memory_order_acquire);
-    if (p == nullptr) {
+    if (dev < 0 || dev >= kNoAllocDevices) return kInvalidValue;
+    Slot& s = slots[dev];
+    std::lock_guard<std::mutex> guard(s.lock);
+    unsigned long long id = current_context_id();
+    if (s.addr == nullptr || id == 0 || s.ctx != id) {
+        // the lookup also makes the device's primary context current
+        void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return static_cast<int>(e);
-        cache[dev & 63].store(p, std::memory_order_release);
+        if (id == 0) id = current_context_id();
+        s.addr = p;
+        s.ctx = id;
     }
-    *out = p;
+    *out = s.addr;
     return kSuccess;
 }
 }  // namespace q4

@@ -12,11 +12,22 @@ The specification's bound is "max relative error <= 1e-3 against an f64
 accumulation".  A dot product can cancel to (nearly) zero, so an
 element-wise relative error needs a floor; the two metrics used are
 
+* ``rel_err_elementwise_tau``: ``max_i |y_i - r_i| / max(|r_i|, tau)`` with
+  ``tau = 1e-3 * rms(r)`` -- the strict element-wise definition: only
+  outputs within a thousandth of the RMS of zero are judged on absolute
+  error;
 * ``rel_err_elementwise``: ``max_i |y_i - r_i| / max(|r_i|, rms(r))`` --
-  element-wise, floored at the RMS of the reference;
+  element-wise, floored at the RMS of the reference (looser: an output
+  smaller than the RMS is judged on its absolute error / RMS);
 * ``rel_err_normwise``: ``max_i |y_i - r_i| / max_i |r_i|``.
 
-Both are reported; each test states which bound it asserts.
+All are reported; each test states which bound it asserts.  Paths that
+compute with the exact decoded weights (the decode GEMVs) meet the strict
+tau-floored bound: their only rounding is the f32 accumulation and the
+final f16 output rounding, which is relative.  The tensor-core prefill path
+rounds every dequantized weight to f16 (as a dense f16 weight matrix is),
+an absolute error per output of ~3e-4 * rms, so it is held to the
+normwise and rms-floored bounds.
 """
 from __future__ import annotations
 
@@ -33,6 +44,18 @@ def f16_round(values) -> np.ndarray:
 def rms(values) -> float:
     v = np.asarray(values, np.float64)
     return float(np.sqrt(np.mean(v * v))) if v.size else 0.0
+
+
+TAU_FRACTION = 1e-3
+
+
+def rel_err_elementwise_tau(actual, ref, tau_fraction: float = TAU_FRACTION) -> float:
+    a = np.asarray(actual, np.float64).reshape(-1)
+    r = np.asarray(ref, np.float64).reshape(-1)
+    if r.size == 0:
+        return 0.0
+    floor = max(tau_fraction * rms(r), np.finfo(np.float64).tiny)
+    return float(np.max(np.abs(a - r) / np.maximum(np.abs(r), floor)))
 
 
 def rel_err_elementwise(actual, ref) -> float:

@@ -4,10 +4,13 @@ split-K scratch in a static per-device array.
 Compared with the existing entry point mote_cuda_quantized_linear_q4_0_f16_ws
 (given a zeroed workspace) over two calls in a row: the outputs must be
 identical, complete (the outputs start as NaN) and the same on the second
-call, which works only if the first left the static counters at zero.  A
-request whose split needs more than the static scratch is rejected with
-status 10200 before anything is enqueued.  The file is collected last and
-also passes on its own.
+call, which works only if the first left the static counters at zero.  The
+shapes cover the decode GEMV with and without its K split over CTAs, and
+the tensor-core GEMM with its last-wave K split inside the static scratch
+(64 tokens, 346 tiles: 2 or 4 parts on 148 SMs) and unsplit (2048 tokens).
+A decode request whose split needs more than the static scratch is
+rejected with status 10200 before anything is enqueued.  The file is
+collected last and also passes on its own.
 """
 from __future__ import annotations
 
@@ -32,7 +35,8 @@ def ctx():
 
 
 @pytest.mark.parametrize("m,n,k", [(16, 4096, 4096), (12, 2048, 4096), (9, 300, 8192),
-                                   (1, 4096, 4096), (16, 1000, 2048)])
+                                   (1, 4096, 4096), (16, 1000, 2048), (64, 44288, 4096),
+                                   (2048, 4096, 4096)])
 def test_noalloc_matches_workspace_entry_twice(ctx, oracle_lib, m, n, k):
     w = fx.q4_0_weights(oracle_lib, n, k, seed=800 + n)
     x = fx.activations(m, k, seed=801 + m).astype(np.float16)

@@ -740,6 +740,8 @@ class Bench:
                         row[f"{name}_tflops"] = round(2.0 * m * n * k / t / 1e9, 1)
                     else:
                         row[f"{name}_gbs"] = round(linear_bytes(m, n, k) / t / 1e6, 1)
+                row["parity"] = self.sharded_parity(
+                    m, n, k, sh, seed, x, y, recv, count, ws, peer, fused, nccl, linear)
                 result[f"m{m}"] = row
                 self.barrier()
                 peer.close(barrier=self.barrier)
@@ -749,6 +751,76 @@ class Bench:
             torch.cuda.synchronize()
             nccl.close()
         return result
+
+    def sharded_parity(self, m, n, k, sh, seed, x, y, recv, count, ws, peer, fused, nccl,
+                       linear) -> dict:
+        """After the timed arms: one more step of each transport, outside any
+        graph, and checks of what the ranks hold.
+        * On every rank the gathered [M, N] of the NCCL, peer-store and fused
+          arms are equal bit for bit.
+        * On rank 0 every rank's columns equal a single-GPU run of that
+          rank's weight rows (regenerated from their seed) through the
+          plain entry, bit for bit -- the same kernels, so the gather must
+          move them unchanged.
+        * On rank 0, 256 sampled columns are within 1e-3 normwise of a
+          float64 accumulation of their decoded weights.
+        * Every rank's device status word (bounded waits) is 0."""
+        import numpy as np
+        import torch.distributed as dist
+
+        from mote_b200 import comm
+
+        torch = self.torch
+        linear(0)
+        nccl.all_gather(y.data_ptr(), recv.data_ptr(), count, self.stream())
+        via_nccl = comm.gathered_to_rows(recv.view(-1), m, sh).clone()
+        ptr = peer.all_gather(y.data_ptr(), 0, self.stream())
+        via_p2p = comm.gathered_to_rows(
+            self.torch_view(ptr, self.world * count * 2).view(torch.float16), m, sh).clone()
+        out = fused(x.data_ptr(), ws[0].data_ptr(), 0, self.stream())
+        via_fused = self.torch_view(out, m * n * 2).view(torch.float16).view(m, n).clone()
+        self.barrier()
+        bits = lambda t: t.view(torch.int16)  # noqa: E731
+        same = bool(torch.equal(bits(via_nccl), bits(via_p2p)) and
+                    torch.equal(bits(via_nccl), bits(via_fused)))
+        single_gpu = True
+        f64_err = None
+        if self.rank == 0:
+            fn = self.lib.mote_cuda_quantized_linear_q4_0_f16
+            cols = np.random.default_rng(seed).choice(n, min(256, n), replace=False)
+            pitch = k // 32 * 18
+            xs = x.float().cpu().numpy().astype(np.float64)
+            want = np.empty((m, cols.size), np.float64)
+            for r in range(self.world):
+                part = comm.shard_rows(n, self.world, r)
+                if part.real_rows == 0:
+                    continue
+                wr = self.encode_q4_0(part.rows, k, seed=seed + r)
+                yr = torch.empty((m, part.rows), dtype=torch.float16, device=self.dev)
+                self.check(fn(x.data_ptr(), wr.data_ptr(), yr.data_ptr(), m, part.rows, k,
+                              self.stream()), "single-GPU shard")
+                got = via_fused[:, part.start:part.stop]
+                single_gpu &= bool(torch.equal(bits(yr[:, :part.real_rows]), bits(got)))
+                mine = np.nonzero((cols >= part.start) & (cols < part.stop))[0]
+                if mine.size:
+                    raw = wr.cpu().numpy().reshape(part.rows, pitch)[cols[mine] - part.start]
+                    want[:, mine] = xs @ dequant_q4_0_f64(raw, k).T
+                del wr, yr
+            got = via_fused[:, torch.as_tensor(cols, device=self.dev)].float().cpu().numpy()
+            f64_err = float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-30))
+        status = ctypes.c_uint(0)
+        self.check(self.lib.mote_cuda_device_status(ctypes.byref(status), 1), "device status")
+        flags = torch.tensor([int(same), int(single_gpu), int(status.value)],
+                             device=self.dev, dtype=torch.int64)
+        every = [torch.zeros_like(flags) for _ in range(self.world)]
+        dist.all_gather(every, flags)
+        every = [t.tolist() for t in every]
+        ok = (all(e[0] == 1 and e[1] == 1 and e[2] == 0 for e in every) and
+              (f64_err is None or f64_err <= 1e-3))
+        return {"ok": ok, "transports_equal": [bool(e[0]) for e in every],
+                "single_gpu_equal": bool(single_gpu) if self.rank == 0 else None,
+                "normwise_vs_f64": None if f64_err is None else round(f64_err, 7),
+                "device_status": [e[2] for e in every]}
 
     def norm_rope_row_split(self) -> dict:
         """Config 2 at N > 1: the T = 512 tokens split by rows, T/G per rank,
@@ -890,6 +962,22 @@ class Bench:
                 "cases": cases,
                 "extra": extra,
             }
+            if self.world > 1:
+                rows = [(leg, key, r["parity"]) for leg in ("lm_head_sharded", "ffn_up_sharded",
+                                                          "prefill_sharded")
+                        for key, r in extra[leg].items() if isinstance(r, dict) and "parity" in r]
+                result["sharded_parity"] = {
+                    "ok": all(p_["ok"] for _, _, p_ in rows),
+                    "device_status": sorted({st for _, _, p_ in rows
+                                             for st in p_["device_status"]}),
+                    "cases": {f"{leg}.{key}": p_["ok"] for leg, key, p_ in rows}}
+                lm1 = extra["lm_head_sharded"]["m1"]
+                result["lm_head_sharded_m1"] = {
+                    "n_gpus": self.world, "fused_us": lm1["fused_us"], "p2p_us": lm1["p2p_us"],
+                    "nccl_us": lm1["nccl_us"], "shard_gemv_us": lm1["gemv_us"],
+                    "single_gpu_us": extra["config5"]["lm_head_m1"]["us"],
+                    "note": "column-sharded lm_head K=4096 N=128256 M=1 (strong scaling): "
+                            "max-over-ranks us per step"}
         if self.world > 1:
             self.barrier()
             self.torch.distributed.destroy_process_group()
@@ -911,6 +999,18 @@ def traffic_ratio():
 
 # --------------------------------------------------------------------------
 CPU_SAMPLE_ROWS = 512
+
+
+def dequant_q4_0_f64(rows, k: int):
+    """Decoded Q4_0 rows [r, K/32*18] bytes -> float64 [r, K] (the block
+    layout of crates/mote-reference/src/quantized.rs:177-201)."""
+    import numpy as np
+
+    b = np.asarray(rows, np.uint8).reshape(-1, k // 32, 18)
+    d = b[:, :, 0:2].copy().view(np.float16).astype(np.float64)
+    qs = b[:, :, 2:]
+    q = np.concatenate([(qs & 15).astype(np.int16) - 8, (qs >> 4).astype(np.int16) - 8], axis=2)
+    return (q * d).reshape(-1, k)
 
 
 def sweep_config(world: int) -> dict:

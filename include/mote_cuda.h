@@ -354,9 +354,19 @@ int mote_cuda_rope_cos_sin_f32(const void* positions, void* cos_out, void* sin_o
  * absent, 10100 + ncclResult_t on an NCCL failure).  id is 128 bytes. */
 int mote_cuda_comm_unique_id(void* id_out);
 int mote_cuda_comm_init(void** comm, int nranks, const void* id, int rank);
+/* Nonblocking init with a deadline: if not every rank has joined within
+ * timeout_ms, the communicator is aborted and 10001 returned (*comm null),
+ * so a rank that never arrives cannot block the host for good.  The
+ * communicator stays nonblocking: its all-gathers are polled against the same
+ * limit (10001 and an aborted communicator past it), and destroy releases it
+ * with the NCCL abort. */
+int mote_cuda_comm_init_timeout(void** comm, int nranks, const void* id, int rank,
+                                uint64_t timeout_ms);
 int mote_cuda_comm_all_gather_f16(void* comm, const void* send, void* recv, uint64_t count,
                                   void* stream);
 int mote_cuda_comm_destroy(void* comm);
+/* Aborts a communicator (no barrier with the other ranks) and frees it. */
+int mote_cuda_comm_abort(void* comm);
 
 /* Peer-store transport over NVLink.  Buffers are shared with CUDA IPC
  * handles (64 bytes): every rank exports its receive buffer and its flag
@@ -375,6 +385,18 @@ int mote_cuda_ipc_close_handle(void* dev_ptr);
 int mote_cuda_all_gather_p2p_f16(const void* send, void* const* recv_ptrs,
                                  unsigned* const* flag_ptrs, unsigned* own_flags,
                                  uint64_t count, uint32_t rank, uint32_t nranks, void* stream);
+/* The same all-gather with its flag wait limited to wait_ns nanoseconds
+ * (the entry above waits up to 1 s); wait_ns == 0 -> 1.  On expiry bit 1 of
+ * the device status is set and the kernel returns. */
+int mote_cuda_all_gather_p2p_f16_timeout(const void* send, void* const* recv_ptrs,
+                                         unsigned* const* flag_ptrs, unsigned* own_flags,
+                                         uint64_t count, uint32_t rank, uint32_t nranks,
+                                         uint64_t wait_ns, void* stream);
+/* Resynchronisation after an expired wait: zeroes this rank's flag array
+ * (nranks + 2 words) on `stream`.  Every rank calls it, with no exchange in
+ * flight on any rank, between two host barriers; the epochs then restart
+ * together. */
+int mote_cuda_peer_flags_reset(unsigned* own_flags, uint32_t nranks, void* stream);
 
 /* Column-sharded Q4_0 linear with the all-gather fused into the epilogue:
  * `weights` holds this rank's rows [rank*shard, rank*shard + shard) of the

@@ -83,12 +83,16 @@ SIGNATURES: dict[str, tuple] = {
     # multi-GPU exchange
     "mote_cuda_comm_unique_id": (I, [P]),
     "mote_cuda_comm_init": (I, [ctypes.POINTER(P), I, P, I]),
+    "mote_cuda_comm_init_timeout": (I, [ctypes.POINTER(P), I, P, I, U64]),
+    "mote_cuda_comm_abort": (I, [P]),
     "mote_cuda_comm_all_gather_f16": (I, [P, P, P, U64, P]),
     "mote_cuda_comm_destroy": (I, [P]),
     "mote_cuda_ipc_get_handle": (I, [P, P]),
     "mote_cuda_ipc_open_handle": (I, [P, ctypes.POINTER(P)]),
     "mote_cuda_ipc_close_handle": (I, [P]),
     "mote_cuda_all_gather_p2p_f16": (I, [P, P, P, P, U64, U32, U32, P]),
+    "mote_cuda_all_gather_p2p_f16_timeout": (I, [P, P, P, P, U64, U32, U32, U64, P]),
+    "mote_cuda_peer_flags_reset": (I, [P, U32, P]),
     "mote_cuda_quantized_linear_q4_0_f16_allgather": (I, [P, P, P, P, P, U64, U64, U64, U64, U32,
                                                           U32, P]),
 }

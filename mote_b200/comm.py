@@ -76,17 +76,32 @@ def gathered_to_rows(gathered, m: int, shard: Shard):
 Exchange = Callable[[object], Sequence[object]]
 
 
-class NcclAllGather:
-    """``ncclAllGather`` of f16 through ``mote_cuda_comm_*``."""
+COMM_TIMEOUT = 10001  # status: NCCL deadline passed, communicator aborted
 
-    def __init__(self, world: int, rank: int, exchange: Exchange):
+
+class NcclAllGather:
+    """``ncclAllGather`` of f16 through ``mote_cuda_comm_*``.
+
+    With ``timeout_s`` the communicator is created nonblocking with that
+    deadline (``mote_cuda_comm_init_timeout``): if not every rank joins in
+    time the init is aborted and :class:`errors.Runtime` raised with status
+    ``COMM_TIMEOUT`` instead of blocking the host."""
+
+    def __init__(self, world: int, rank: int, exchange: Exchange,
+                 timeout_s: float | None = None):
         uid = ctypes.create_string_buffer(128)
         if rank == 0:
             errors.check(lib().mote_cuda_comm_unique_id(uid), "NCCL unique id")
         ids = exchange(bytes(uid.raw) if rank == 0 else None)
         uid = ctypes.create_string_buffer(bytes(ids[0]), 128)
+        self.comm = None
         comm = ctypes.c_void_p()
-        errors.check(lib().mote_cuda_comm_init(ctypes.byref(comm), world, uid, rank), "NCCL init")
+        if timeout_s is None:
+            st = lib().mote_cuda_comm_init(ctypes.byref(comm), world, uid, rank)
+        else:
+            st = lib().mote_cuda_comm_init_timeout(ctypes.byref(comm), world, uid, rank,
+                                                   max(1, int(timeout_s * 1000)))
+        errors.check(st, "NCCL init")
         self.comm = comm.value
         self.world, self.rank = world, rank
 
@@ -96,8 +111,14 @@ class NcclAllGather:
 
     def close(self) -> None:
         if self.comm:
-            errors.check(lib().mote_cuda_comm_destroy(self.comm), "NCCL destroy")
-            self.comm = None
+            comm, self.comm = self.comm, None
+            errors.check(lib().mote_cuda_comm_destroy(comm), "NCCL destroy")
+
+    def abort(self) -> None:
+        """Ends the communicator without a barrier with the other ranks."""
+        if self.comm:
+            comm, self.comm = self.comm, None
+            errors.check(lib().mote_cuda_comm_abort(comm), "NCCL abort")
 
 
 class PeerBuffers:
@@ -155,6 +176,17 @@ class PeerBuffers:
         self.tables = [table([ptrs[r][b] for r in range(world)]) for b in range(buffers)]
         self.flag_table = table([ptrs[r][buffers] for r in range(world)])
 
+    def reset_flags(self, stream: int, barrier: Callable[[], None]) -> None:
+        """Resynchronises the epochs after a flag wait expired (device status
+        bit 1): with no exchange in flight on any rank, every rank zeroes its
+        own flag array between two barriers, and the epochs restart
+        together."""
+        barrier()
+        errors.check(lib().mote_cuda_peer_flags_reset(self.flags, self.world, stream),
+                     "reset peer flags")
+        errors.check(lib().mote_cuda_stream_synchronize(stream), "synchronize")
+        barrier()
+
     def close(self, barrier: Callable[[], None] | None = None) -> None:
         """Unmaps the peers' buffers, waits at ``barrier`` (every rank must
         have unmapped this rank's buffers before they are freed), frees."""
@@ -182,11 +214,20 @@ class PeerAllGather(PeerBuffers):
         super().__init__(world, rank, world * count * 2, exchange, buffers)
         self.recv = self.local
 
-    def all_gather(self, send_ptr: int, buffer: int, stream: int) -> int:
-        """Gathers into receive buffer ``buffer``; returns its pointer."""
-        errors.check(lib().mote_cuda_all_gather_p2p_f16(
-            send_ptr, self.tables[buffer], self.flag_table, self.flags, self.count,
-            self.rank, self.world, stream), "peer all-gather")
+    def all_gather(self, send_ptr: int, buffer: int, stream: int,
+                   wait_ns: int | None = None) -> int:
+        """Gathers into receive buffer ``buffer``; returns its pointer.  The
+        wait for the other ranks is bounded by ``wait_ns`` (default 1 s); on
+        expiry the device status records it."""
+        if wait_ns is None:
+            st = lib().mote_cuda_all_gather_p2p_f16(
+                send_ptr, self.tables[buffer], self.flag_table, self.flags, self.count,
+                self.rank, self.world, stream)
+        else:
+            st = lib().mote_cuda_all_gather_p2p_f16_timeout(
+                send_ptr, self.tables[buffer], self.flag_table, self.flags, self.count,
+                self.rank, self.world, int(wait_ns), stream)
+        errors.check(st, "peer all-gather")
         return self.local[buffer]
 
 

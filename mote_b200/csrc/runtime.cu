@@ -126,6 +126,9 @@ extern "C" int mote_cuda_device_status(unsigned* status, int clear) {
 extern "C" const char* mote_cuda_status_string(int status) {
     if (status == mote::kInternalError) return "mote: invalid argument (internal error -1)";
     if (status == 10000) return "mote: NCCL library (libnccl.so.2) could not be loaded";
+    if (status == 10001)
+        return "mote: NCCL deadline passed (not every rank joined or completed in time); the "
+               "communicator was aborted";
     if (status == 10200)
         return "mote: the request's K split needs more than the 8 MiB static scratch of "
                "mote_cuda_quantized_linear_q4_0_f16_noalloc (use the _ws entry point)";

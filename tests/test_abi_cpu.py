@@ -223,3 +223,31 @@ def test_blaslt_argument_rules(lib):
                                                STREAM) == -1
     assert lib.mote_cuda_blaslt_last_error(None) is None
     lib.mote_cuda_blaslt_destroy(None)
+
+
+CRATE = Path(__file__).resolve().parents[1] / "mote-backend-cuda"
+
+
+def test_rust_crate_binds_every_declared_symbol():
+    """The committed Cargo crate (not compiled here: no cargo) declares every
+    entry point of the header in src/ffi.rs, with the same number of
+    parameters, and registers the same kernel table as mote_b200.kernel."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    c_arity = {}
+    for name, args in re.findall(r"\b(mote_cuda_\w+)\s*\(([^)]*)\)\s*;", text):
+        args = args.strip()
+        c_arity[name] = 0 if args in ("", "void") else args.count(",") + 1
+    ffi = (CRATE / "src" / "ffi.rs").read_text()
+    rs_arity = {name: (0 if not args.strip() else args.count(",") + 1)
+                for name, args in re.findall(r"pub fn (mote_cuda_\w+)\(([^)]*)\)", ffi)}
+    assert rs_arity == c_arity
+    kernel_rs = (CRATE / "src" / "kernel.rs").read_text()
+    rows = re.findall(r'\("(\w+)", DType::(\w+), "(mote_cuda_\w+)", (\d+), call_\w+\)', kernel_rs)
+    from mote_b200 import kernel
+
+    table = {(op, dt.lower()): sym for op, dt, sym, _ in rows}
+    assert table == {(op, dt.name.lower()): sym for (op, dt), sym in kernel.CUDA_KERNELS.items()}
+    for _, _, sym, words in rows:
+        assert int(words) == c_arity[sym], sym
+    build = (CRATE / "build.rs").read_text()
+    assert "compute_{arch},code=sm_{arch}" in build and '"100a"' in build

@@ -1144,9 +1144,20 @@ def run_single_case(args) -> None:
         x = b.randn((m, k), 2, torch.float16)
         y = torch.empty((m, n), dtype=torch.float16, device=b.dev)
 
-        def launch():
-            b.check(b.lib.mote_cuda_quantized_linear_q4_0_f16(
-                x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "gemv")
+        if args.ws:
+            # the workspace entry mote_b200.ops uses (K split over CTAs for
+            # 9-16 tokens, split last wave on the tensor-core path)
+            wsp = torch.zeros(max(b.workspace_bytes(m, n, k), 256), dtype=torch.uint8,
+                              device=b.dev)
+
+            def launch():
+                b.check(b.lib.mote_cuda_quantized_linear_q4_0_f16_ws(
+                    x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, wsp.data_ptr(),
+                    wsp.numel(), b.stream()), "gemv")
+        else:
+            def launch():
+                b.check(b.lib.mote_cuda_quantized_linear_q4_0_f16(
+                    x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), "gemv")
         nbytes = linear_bytes(m, n, k)
     elif args.only == "q8_0":
         m, n, k = args.m, args.n, args.k
@@ -1216,6 +1227,8 @@ def main() -> int:
     p.add_argument("--n", type=int, default=128256)
     p.add_argument("--k", type=int, default=4096)
     p.add_argument("--launches", type=int, default=3)
+    p.add_argument("--ws", action="store_true",
+                   help="--only gemv: the workspace entry (as mote_b200.ops calls it)")
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)

@@ -343,6 +343,40 @@ int mote_cuda_rope_cos_sin_f32(const void* positions, void* cos_out, void* sin_o
                                uint64_t tokens, uint64_t rotary_dim, double theta,
                                void* stream);
 
+/* ---- grouped-query attention over a KV cache ----------------------------
+ * No reference counterpart: the reference lists attention (GQA) with KV-cache
+ * append and KV-cache operations as planned primitives (docs/roadmap.md:58-60,
+ * docs/architecture.md:185-191) and ships none.  f16 tensors, head_dim
+ * innermost: caches [cache_rows, kv_heads, head_dim]; a batch of sequences
+ * keeps sequence b at rows b * seq_capacity + position.
+ *
+ * KV-cache append: k_new / v_new [tokens, kv_heads, head_dim] into cache row
+ * slots[t] (int32); a slot outside [0, cache_rows) is skipped and sets
+ * *error_flag (uint32, optional) to 1.  kv_heads * head_dim % 8 == 0, 16-byte
+ * aligned tensors; tokens == 0 returns 0; null pointers -> 1. */
+int mote_cuda_kv_cache_append_f16(const void* k_new, const void* v_new, void* k_cache,
+                                  void* v_cache, const void* slots, uint64_t tokens,
+                                  uint64_t kv_heads, uint64_t head_dim, uint64_t cache_rows,
+                                  void* error_flag, void* stream);
+/* Decode attention, one query token per sequence:
+ *   out[b, h] = softmax(scale * q[b, h] . K_b[:len_b, h / (q_heads / kv_heads)]) . V_b
+ * q / out [batch, q_heads, head_dim]; seq_lens int32 [batch] on the device,
+ * len_b = min(seq_lens[b], max_len), max_len <= seq_capacity; a sequence of
+ * length 0 gets zeros.  q_heads % kv_heads == 0, head_dim 64 or 128,
+ * (q_heads / kv_heads) * head_dim <= 512, 16-byte aligned tensors.  Splits the
+ * positions over CTAs and merges the parts in a second kernel: workspace of
+ * mote_cuda_gqa_attention_decode_workspace_bytes bytes (16-byte aligned; 0
+ * means none is needed; contents need no initialisation).  Other shapes or a
+ * missing workspace -> 1. */
+int mote_cuda_gqa_attention_decode_workspace_bytes(uint64_t batch, uint64_t q_heads,
+                                                   uint64_t kv_heads, uint64_t head_dim,
+                                                   uint64_t max_len, uint64_t* bytes);
+int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_cache, const void* v_cache,
+                                       const void* seq_lens, void* out, uint64_t batch,
+                                       uint64_t q_heads, uint64_t kv_heads, uint64_t head_dim,
+                                       uint64_t seq_capacity, uint64_t max_len, float scale,
+                                       void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* ---- multi-GPU exchange for column-sharded linears ----------------------
  * The reference is single-device (crates/mote-backend-hip/src/context.rs:13-80
  * holds one device and one stream); these entry points are new.  Each rank

@@ -81,6 +81,11 @@ SIGNATURES: dict[str, tuple] = {
     "mote_cuda_embedding_gather_f16": (I, [P, P, P, U64, U64, U64, P, P]),
     "mote_cuda_rope_cos_sin_f32": (I, [P, P, P, U64, U64, D, P]),
     # multi-GPU exchange
+    "mote_cuda_kv_cache_append_f16": (I, [P, P, P, P, P, U64, U64, U64, U64, P, P]),
+    "mote_cuda_gqa_attention_decode_workspace_bytes": (I, [U64, U64, U64, U64, U64,
+                                                           ctypes.POINTER(U64)]),
+    "mote_cuda_gqa_attention_decode_f16": (I, [P, P, P, P, P, U64, U64, U64, U64, U64, U64,
+                                               ctypes.c_float, P, U64, P]),
     "mote_cuda_comm_unique_id": (I, [P]),
     "mote_cuda_comm_init": (I, [ctypes.POINTER(P), I, P, I]),
     "mote_cuda_comm_init_timeout": (I, [ctypes.POINTER(P), I, P, I, U64]),

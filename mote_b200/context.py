@@ -253,6 +253,18 @@ class CudaContext:
             self._workspace = ws
         return ws.pointer, ws.size_bytes
 
+    def attention_workspace(self, nbytes: int) -> tuple[int, int]:
+        """A device workspace of at least ``nbytes`` for the attention
+        kernels' split partials (contents need no initialisation; separate
+        from the linear's zeroed workspace), grown on demand with a stream
+        synchronisation."""
+        ws = getattr(self, "_attn_workspace", None)
+        if ws is None or ws.size_bytes < nbytes:
+            self.sync()
+            ws = CudaStorage(self.inner, max(int(nbytes), 1 << 20))
+            self._attn_workspace = ws
+        return ws.pointer, ws.size_bytes
+
     def read_bytes(self, tensor: Tensor) -> bytes:
         storage = self.storage(tensor)
         return storage.read_bytes()[: tensor.desc.required_span_bytes]

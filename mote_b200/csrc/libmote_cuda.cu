@@ -10,3 +10,4 @@
 #include "q4_0_codec.cu"
 #include "comm.cu"
 #include "dense_matmul.cu"
+#include "attention.cu"

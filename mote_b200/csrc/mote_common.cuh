@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 namespace mote {
@@ -276,6 +277,38 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStrea
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+// launch_pdl with dynamic shared memory.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, int smem_bytes,
+                           cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = static_cast<std::size_t>(smem_bytes);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+// Opts a kernel into `bytes` of dynamic shared memory on the current device,
+// once per ordinal below 64 (`done` is the bit mask), every call above.
+template <typename Kernel>
+inline int ensure_dynamic_smem(Kernel kernel, int bytes, std::atomic<std::uint64_t>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const std::uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return kSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return kSuccess;
 }
 
 }  // namespace mote

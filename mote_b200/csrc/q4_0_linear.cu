@@ -503,6 +503,32 @@ __global__ void __launch_bounds__(kThreads, 2) q4_0_gemv_kernel(const Params p) 
         const std::uint32_t groups = pun * 64;
         const std::uint32_t total_groups = p.M * groups;
 
+        if (!XF32 && p.M >= 3) {
+            // Three or more rows: 16-byte chunks, row by row (no division),
+            // every thread's chunks of up to four rows loaded before use.
+            const std::uint32_t cpr = pun * 32;  // 16-byte chunks per row
+            for (std::uint32_t m0 = 0; m0 < p.M; m0 += 4) {
+                const std::uint32_t rows = min(4u, p.M - m0);
+                for (std::uint32_t c = threadIdx.x; c < cpr; c += kThreads) {
+                    uint4 v[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (j < rows)
+                            v[j] = __ldg(reinterpret_cast<const uint4*>(
+                                static_cast<const __half*>(p.x) + (m0 + j) * p.K + kx0 + 8 * c));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (j < rows) {
+                            uint4 o;
+                            o.x = prmt(v[j].x, v[j].y, 0x5410u);
+                            o.y = prmt(v[j].x, v[j].y, 0x7632u);
+                            o.z = prmt(v[j].z, v[j].w, 0x5410u);
+                            o.w = prmt(v[j].z, v[j].w, 0x7632u);
+                            *reinterpret_cast<uint4*>(xs + (m0 + j) * p.x_stride + 16 * c) = o;
+                        }
+                }
+            }
+        } else
         for (std::uint32_t i = threadIdx.x; i < total_groups; i += kThreads) {
             const std::uint32_t m = i / groups;
             const std::uint32_t gi = i - m * groups;

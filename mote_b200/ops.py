@@ -652,3 +652,85 @@ def embedding_gather_f16(context: CudaContext, table: Tensor, ids: Tensor, outpu
         value = int(np.frombuffer(context.read_bytes(flag.tensor), np.uint32)[0])
         if value:
             raise errors.IndexOutOfRange(vocab=vocab)
+
+
+# --------------------------------------------------------------- attention --
+def kv_cache_append_f16(context: CudaContext, k_new: Tensor, v_new: Tensor, k_cache: Tensor,
+                        v_cache: Tensor, slots: Tensor, check: bool = True) -> None:
+    """Writes ``k_new[t]``/``v_new[t]`` ([tokens, kv_heads, head_dim] f16)
+    into cache row ``slots[t]`` of ``k_cache``/``v_cache`` ([rows, kv_heads,
+    head_dim] f16).  Slots outside the cache are skipped; with ``check`` the
+    call synchronizes and raises :class:`errors.IndexOutOfRange` for them.
+    No reference counterpart (the reference lists KV-cache operations as
+    planned, docs/roadmap.md:60)."""
+    for t, name in ((k_new, "k_new"), (v_new, "v_new"), (k_cache, "k_cache"),
+                    (v_cache, "v_cache")):
+        _plain(t, name, DType.F16)
+        _rank(t, name, 3)
+    _plain(slots, "slots", DType.I32)
+    _rank(slots, "slots", 1)
+    tokens, kvh, hd = k_new.shape
+    _shape(v_new, "v_new", k_new.shape)
+    rows = k_cache.shape[0]
+    _shape(k_cache, "k_cache", (rows, kvh, hd))
+    _shape(v_cache, "v_cache", (rows, kvh, hd))
+    _shape(slots, "slots", (tokens,))
+    _not_aliased(k_cache, "k_cache", v_cache, "v_cache")
+    if tokens == 0:
+        return
+    flag = getattr(context, "_append_flag", None)
+    if flag is None:
+        flag = context._append_flag = _Flag(context)
+    fptr = flag.tensor.pointer
+    ptrs = [context.storage(t).pointer for t in (k_new, v_new, k_cache, v_cache, slots)]
+    context.inner.select()
+    errors.check(lib().mote_cuda_memset_async(fptr, 0, 4, context.stream), "clear append flag")
+    errors.check(lib().mote_cuda_kv_cache_append_f16(*ptrs, tokens, kvh, hd, rows, fptr,
+                                                     context.stream),
+                 "launch KV-cache append kernel")
+    if check:
+        import numpy as np
+
+        if int(np.frombuffer(context.read_bytes(flag.tensor), np.uint32)[0]):
+            raise errors.IndexOutOfRange(vocab=rows)
+
+
+def gqa_attention_decode_f16(context: CudaContext, q: Tensor, k_cache: Tensor, v_cache: Tensor,
+                             seq_lens: Tensor, output: Tensor, seq_capacity: int, max_len: int,
+                             scale: float | None = None) -> None:
+    """One query token per sequence over its cached K/V (grouped-query):
+    ``output[b, h] = softmax(scale * q[b, h] . K_b[:len_b, h // g]) . V_b``
+    with ``g = q_heads // kv_heads``, sequence ``b`` at cache rows
+    ``b * seq_capacity + position`` and ``len_b = min(seq_lens[b], max_len)``.
+    ``scale`` defaults to ``1 / sqrt(head_dim)``."""
+    import math
+
+    _plain(q, "q", DType.F16)
+    _rank(q, "q", 3)
+    _plain(output, "output", DType.F16)
+    _shape(output, "output", q.shape)
+    batch, qh, hd = q.shape
+    for t, name in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        _plain(t, name, DType.F16)
+        _rank(t, name, 3)
+    rows, kvh, hd2 = k_cache.shape
+    _shape(k_cache, "k_cache", (rows, kvh, hd))
+    _shape(v_cache, "v_cache", k_cache.shape)
+    _plain(seq_lens, "seq_lens", DType.I32)
+    _shape(seq_lens, "seq_lens", (batch,))
+    if batch * seq_capacity > rows or max_len > seq_capacity:
+        raise errors.ShapeMismatch(tensor="k_cache", expected=(batch * seq_capacity, kvh, hd),
+                                   actual=k_cache.shape)
+    _not_aliased(output, "output", q, "q")
+    if batch == 0 or qh == 0:
+        return
+    scale = 1.0 / math.sqrt(hd) if scale is None else float(scale)
+    need = ctypes.c_uint64(0)
+    errors.check(lib().mote_cuda_gqa_attention_decode_workspace_bytes(
+        batch, qh, kvh, hd, max_len, ctypes.byref(need)), "query attention workspace")
+    ws_ptr, ws_bytes = context.attention_workspace(need.value) if need.value else (None, 0)
+    ptrs = [context.storage(t).pointer for t in (q, k_cache, v_cache, seq_lens, output)]
+    context.inner.select()
+    errors.check(lib().mote_cuda_gqa_attention_decode_f16(
+        *ptrs, batch, qh, kvh, hd, seq_capacity, max_len, ctypes.c_float(scale), ws_ptr,
+        ws_bytes, context.stream), "launch GQA decode attention kernel")

@@ -144,3 +144,34 @@ def ulp_distance_f32(a, b) -> np.ndarray:
     ai = np.where(ai < 0, -(ai & 0x7FFFFFFF), ai)
     bi = np.where(bi < 0, -(bi & 0x7FFFFFFF), bi)
     return np.abs(ai - bi)
+
+
+def gqa_attention_f64(q, k, v, query_positions, scale: float) -> np.ndarray:
+    """Grouped-query attention in float64 (no reference operator: the
+    reference names attention with a KV cache as planned,
+    docs/roadmap.md:58-60; this is the standard definition).
+
+    ``q`` [T, Hq, D]; ``k``, ``v`` [S, Hkv, D] for key positions 0..S-1;
+    query ``t`` sits at position ``query_positions[t]`` and attends keys
+    ``0..query_positions[t]`` (inclusive); query head ``h`` reads KV head
+    ``h // (Hq // Hkv)``.  Returns [T, Hq, D]."""
+    q64 = np.asarray(q, np.float64)
+    k64 = np.asarray(k, np.float64)
+    v64 = np.asarray(v, np.float64)
+    t, hq, d = q64.shape
+    s_len, hkv, _ = k64.shape
+    g = hq // hkv
+    pos = np.asarray(query_positions, np.int64).reshape(t, 1)
+    mask = np.arange(s_len)[None, :] > pos  # [T, S]
+    out = np.zeros((t, hq, d), np.float64)
+    for h in range(hq):
+        kh = k64[:, h // g, :]
+        sc = (q64[:, h, :] @ kh.T) * scale  # [T, S]
+        sc[mask] = -np.inf
+        mx = np.max(sc, axis=1, keepdims=True)
+        mx[~np.isfinite(mx)] = 0.0
+        p = np.exp(sc - mx)
+        denom = p.sum(axis=1, keepdims=True)
+        denom[denom == 0] = 1.0
+        out[:, h, :] = (p / denom) @ v64[:, h // g, :]
+    return out

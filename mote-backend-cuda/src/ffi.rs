@@ -8,8 +8,8 @@
 //! them.
 //!
 //! NOT COMPILED IN THIS REPOSITORY'S BUILD ENVIRONMENT: it has no `cargo`.
-//! The declarations are generated from the header's prototypes and follow
-//! its argument order and types one for one.
+//! The declarations follow the header's prototypes one for one (argument
+//! order and types).
 #![allow(dead_code)]
 
 use std::ffi::{c_char, c_void};
@@ -70,6 +70,9 @@ unsafe extern "C" {
     pub fn mote_cuda_swiglu_f16(gate: *const c_void, up: *const c_void, output: *mut c_void, n: u64, stream: *mut c_void) -> i32;
     pub fn mote_cuda_embedding_gather_f16(table: *const c_void, ids: *const c_void, output: *mut c_void, tokens: u64, vocab: u64, hidden: u64, error_flag: *mut c_void, stream: *mut c_void) -> i32;
     pub fn mote_cuda_rope_cos_sin_f32(positions: *const c_void, cos_out: *mut c_void, sin_out: *mut c_void, tokens: u64, rotary_dim: u64, theta: f64, stream: *mut c_void) -> i32;
+    pub fn mote_cuda_kv_cache_append_f16(k_new: *const c_void, v_new: *const c_void, k_cache: *mut c_void, v_cache: *mut c_void, slots: *const c_void, tokens: u64, kv_heads: u64, head_dim: u64, cache_rows: u64, error_flag: *mut c_void, stream: *mut c_void) -> i32;
+    pub fn mote_cuda_gqa_attention_decode_workspace_bytes(batch: u64, q_heads: u64, kv_heads: u64, head_dim: u64, max_len: u64, bytes: *mut u64) -> i32;
+    pub fn mote_cuda_gqa_attention_decode_f16(q: *const c_void, k_cache: *const c_void, v_cache: *const c_void, seq_lens: *const c_void, out: *mut c_void, batch: u64, q_heads: u64, kv_heads: u64, head_dim: u64, seq_capacity: u64, max_len: u64, scale: f32, workspace: *mut c_void, workspace_bytes: u64, stream: *mut c_void) -> i32;
     pub fn mote_cuda_comm_unique_id(id_out: *mut c_void) -> i32;
     pub fn mote_cuda_comm_init(comm: *mut *mut c_void, nranks: i32, id: *const c_void, rank: i32) -> i32;
     pub fn mote_cuda_comm_init_timeout(comm: *mut *mut c_void, nranks: i32, id: *const c_void, rank: i32, timeout_ms: u64) -> i32;

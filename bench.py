@@ -664,6 +664,60 @@ class Bench:
             self.lib.mote_cuda_blaslt_destroy(h)
         return out
 
+    def attention(self) -> dict:
+        """GQA attention over a KV cache at Llama-3.2-1B geometry (32 query
+        heads, 8 KV heads, head_dim 64).  Decode: one query token per
+        sequence, GB/s = the K and V bytes of the attended positions (read
+        once) / time, caches rotated over copies holding >= 2.5x L2.
+        Prefill: causal chunks from position 0 on the tensor cores, TFLOP/s
+        = 4 * head_dim * q_heads * sum over queries of attended positions."""
+        torch = self.torch
+        qh, kvh, hd = 32, 8, 64
+        scale = ctypes.c_float(1.0 / math.sqrt(hd))
+        out = {}
+        for batch, length in ((1, 4096), (1, 32768), (16, 4096)):
+            kv_bytes = 2 * batch * length * kvh * hd * 2
+            r = copies_for(kv_bytes)
+            caches = [(self.randn((batch * length, kvh, hd), 40 + i, torch.float16),
+                       self.randn((batch * length, kvh, hd), 80 + i, torch.float16))
+                      for i in range(r)]
+            q = self.randn((batch, qh, hd), 5, torch.float16)
+            o = torch.empty_like(q)
+            lens = torch.full((batch,), length, dtype=torch.int32, device=self.dev)
+            need = ctypes.c_uint64(0)
+            self.check(self.lib.mote_cuda_gqa_attention_decode_workspace_bytes(
+                batch, qh, kvh, hd, length, ctypes.byref(need)), "attention workspace")
+            ws = torch.empty(max(need.value, 16), dtype=torch.uint8, device=self.dev)
+
+            def run(caches=caches, q=q, o=o, lens=lens, ws=ws, batch=batch, length=length):
+                for kc, vc in caches:
+                    self.check(self.lib.mote_cuda_gqa_attention_decode_f16(
+                        q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr(),
+                        o.data_ptr(), batch, qh, kvh, hd, length, length, scale, ws.data_ptr(),
+                        ws.numel(), self.stream()), "decode attention")
+            g = self.graph(run)
+            t = self.time_graph(g, 20, r) / r
+            del g, caches
+            out[f"decode_b{batch}_len{length}"] = {
+                "us": round(t * 1e3, 2), "gbs": round(kv_bytes / t / 1e6, 1), "copies": r}
+        for tokens in (512, 2048):
+            kc = self.randn((tokens, kvh, hd), 7, torch.float16)
+            vc = self.randn((tokens, kvh, hd), 8, torch.float16)
+            q = self.randn((tokens, qh, hd), 9, torch.float16)
+            o = torch.empty_like(q)
+
+            def runp(kc=kc, vc=vc, q=q, o=o, tokens=tokens):
+                self.check(self.lib.mote_cuda_gqa_attention_prefill_f16(
+                    q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), tokens, 0, qh,
+                    kvh, hd, 0, tokens, scale, self.stream()), "prefill attention")
+            g = self.graph(runp)
+            t = self.time_graph(g, 20, 1)
+            del g
+            flops = 4.0 * hd * qh * tokens * (tokens + 1) / 2
+            out[f"prefill_t{tokens}"] = {"us": round(t * 1e3, 2),
+                                         "tflops": round(flops / t / 1e9, 1)}
+        return out
+
     def sharded_linear(self, n: int, ms_list, seed: int, k: int = 4096) -> dict:
         """A linear column-sharded over the ranks (strong scaling): per step
         each rank runs the Q4_0 linear on its rows [rank * shard, ...) and the
@@ -919,6 +973,7 @@ class Bench:
             extra["q8_0_linear"] = self.q8_0()
             extra["kquant_linear"] = self.kquant()
             extra["dense_matmul_f16_f32"] = self.dense_matmul()
+            extra["gqa_attention"] = self.attention()
         e2e = self.e2e(max(3, min(args.steps, 20)))
         if self.world > 1:
             # the splits the data plane supports: lm_head and FFN up/gate by
@@ -1184,6 +1239,39 @@ def run_single_case(args) -> None:
         def launch():
             b.check(fn(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, b.stream()), args.only)
         nbytes = nb + m * k * 2 + m * n * 2
+    elif args.only in ("attn_decode", "attn_prefill"):
+        qh, kvh, hd = 32, 8, 64
+        length = args.n if args.n != 128256 else 4096
+        scale = ctypes.c_float(1.0 / math.sqrt(hd))
+        if args.only == "attn_decode":
+            batch = args.m
+            kc = b.randn((batch * length, kvh, hd), 1, torch.float16)
+            vc = b.randn((batch * length, kvh, hd), 2, torch.float16)
+            q = b.randn((batch, qh, hd), 3, torch.float16)
+            o = torch.empty_like(q)
+            lens = torch.full((batch,), length, dtype=torch.int32, device=b.dev)
+            need = ctypes.c_uint64(0)
+            b.check(b.lib.mote_cuda_gqa_attention_decode_workspace_bytes(
+                batch, qh, kvh, hd, length, ctypes.byref(need)), "workspace")
+            ws = torch.empty(max(need.value, 16), dtype=torch.uint8, device=b.dev)
+
+            def launch():
+                b.check(b.lib.mote_cuda_gqa_attention_decode_f16(
+                    q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr(), o.data_ptr(),
+                    batch, qh, kvh, hd, length, length, scale, ws.data_ptr(), ws.numel(),
+                    b.stream()), "decode attention")
+            nbytes = 2 * batch * length * kvh * hd * 2
+        else:
+            kc = b.randn((length, kvh, hd), 1, torch.float16)
+            vc = b.randn((length, kvh, hd), 2, torch.float16)
+            q = b.randn((length, qh, hd), 3, torch.float16)
+            o = torch.empty_like(q)
+
+            def launch():
+                b.check(b.lib.mote_cuda_gqa_attention_prefill_f16(
+                    q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), length, 0, qh, kvh,
+                    hd, 0, length, scale, b.stream()), "prefill attention")
+            nbytes = (3 * length * kvh * hd + 2 * length * qh * hd) * 2
     elif args.only == "norm_rope":
         t, hidden, qh, kh, hd = 512, 2048, 32, 8, 64
         pos = torch.arange(t, dtype=torch.int32, device=b.dev)
@@ -1222,7 +1310,9 @@ def run_single_case(args) -> None:
 
 def main() -> int:
     p = argparse.ArgumentParser()
-    p.add_argument("--only", default=None, help="profile one kernel: gemv | q8_0 | q4_k | q6_k | norm_rope")
+    p.add_argument("--only", default=None,
+                   help="profile one kernel: gemv | q8_0 | q4_k | q6_k | norm_rope | "
+                        "attn_decode (--m batch, --n length) | attn_prefill (--n tokens)")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=128256)
     p.add_argument("--k", type=int, default=4096)

@@ -376,6 +376,18 @@ int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_cache, const
                                        uint64_t q_heads, uint64_t kv_heads, uint64_t head_dim,
                                        uint64_t seq_capacity, uint64_t max_len, float scale,
                                        void* workspace, uint64_t workspace_bytes, void* stream);
+/* Causal prefill attention on the tensor cores (tcgen05): `tokens` queries at
+ * positions start .. start + tokens - 1 of one sequence,
+ *   out[t, h] = softmax_{p <= start + t}(scale * q[t, h] . K[p, h / g]) . V[p, h / g],
+ * q / out [tokens, q_heads, head_dim] f16, K/V from cache rows row0 + p for
+ * p < start + tokens (this chunk's K/V already appended; row0 + start +
+ * tokens <= cache_rows).  head_dim 64, q_heads % kv_heads == 0, 16-byte
+ * aligned tensors; tokens == 0 returns 0; other shapes -> 1. */
+int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_cache, const void* v_cache,
+                                        void* out, uint64_t tokens, uint64_t start,
+                                        uint64_t q_heads, uint64_t kv_heads, uint64_t head_dim,
+                                        uint64_t row0, uint64_t cache_rows, float scale,
+                                        void* stream);
 
 /* ---- multi-GPU exchange for column-sharded linears ----------------------
  * The reference is single-device (crates/mote-backend-hip/src/context.rs:13-80

@@ -73,6 +73,7 @@ unsafe extern "C" {
     pub fn mote_cuda_kv_cache_append_f16(k_new: *const c_void, v_new: *const c_void, k_cache: *mut c_void, v_cache: *mut c_void, slots: *const c_void, tokens: u64, kv_heads: u64, head_dim: u64, cache_rows: u64, error_flag: *mut c_void, stream: *mut c_void) -> i32;
     pub fn mote_cuda_gqa_attention_decode_workspace_bytes(batch: u64, q_heads: u64, kv_heads: u64, head_dim: u64, max_len: u64, bytes: *mut u64) -> i32;
     pub fn mote_cuda_gqa_attention_decode_f16(q: *const c_void, k_cache: *const c_void, v_cache: *const c_void, seq_lens: *const c_void, out: *mut c_void, batch: u64, q_heads: u64, kv_heads: u64, head_dim: u64, seq_capacity: u64, max_len: u64, scale: f32, workspace: *mut c_void, workspace_bytes: u64, stream: *mut c_void) -> i32;
+    pub fn mote_cuda_gqa_attention_prefill_f16(q: *const c_void, k_cache: *const c_void, v_cache: *const c_void, out: *mut c_void, tokens: u64, start: u64, q_heads: u64, kv_heads: u64, head_dim: u64, row0: u64, cache_rows: u64, scale: f32, stream: *mut c_void) -> i32;
     pub fn mote_cuda_comm_unique_id(id_out: *mut c_void) -> i32;
     pub fn mote_cuda_comm_init(comm: *mut *mut c_void, nranks: i32, id: *const c_void, rank: i32) -> i32;
     pub fn mote_cuda_comm_init_timeout(comm: *mut *mut c_void, nranks: i32, id: *const c_void, rank: i32, timeout_ms: u64) -> i32;

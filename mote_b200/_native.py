@@ -86,6 +86,8 @@ SIGNATURES: dict[str, tuple] = {
                                                            ctypes.POINTER(U64)]),
     "mote_cuda_gqa_attention_decode_f16": (I, [P, P, P, P, P, U64, U64, U64, U64, U64, U64,
                                                ctypes.c_float, P, U64, P]),
+    "mote_cuda_gqa_attention_prefill_f16": (I, [P, P, P, P, U64, U64, U64, U64, U64, U64, U64,
+                                                ctypes.c_float, P]),
     "mote_cuda_comm_unique_id": (I, [P]),
     "mote_cuda_comm_init": (I, [ctypes.POINTER(P), I, P, I]),
     "mote_cuda_comm_init_timeout": (I, [ctypes.POINTER(P), I, P, I, U64]),

@@ -1,0 +1,436 @@
+// Causal grouped-query attention for prefill chunks on the tcgen05 tensor
+// cores (no reference counterpart; see attention.cu).
+//
+//   out[t, h] = softmax_{p <= start + t}(scale * q[t, h] . K[p, h / g]) . V[p, h / g]
+//
+// q/out [tokens, q_heads, 64] f16 (queries at positions start .. start +
+// tokens - 1); K/V from the cache rows row0 .. row0 + start + tokens - 1
+// ([cache rows, kv_heads, 64] f16, this chunk's K/V already appended).
+//
+// One CTA computes 128 query rows of one query head (flash attention):
+// * warp 4 loads the Q tile once and the K and V tiles of 128 positions
+//   (TMA, 128-byte swizzle, two stages; tensor maps end at the last
+//   attended row, so rows past it arrive as zeros);
+// * warp 5 allocates tensor memory and one thread issues the MMAs:
+//   S = Q K^T (tcgen05.mma kind::f16, M = 128 queries, N = 128 positions,
+//   A and B K-major in shared memory) into one of two S buffers in TMEM, so
+//   S for the next tile is computed while the softmax works on this one;
+//   then O += P V (M = 128, N = 64, A = P read from tensor memory, B = V
+//   MN-major in shared memory) into the O accumulator in TMEM;
+// * warps 0-3 run the softmax, one thread per query row (= TMEM lane):
+//   each reads its S row (tcgen05.ld), masks positions past its own,
+//   keeps the running max and sum (exp2 with the scale folded in), writes
+//   P as f16 over the first half of its S buffer (tcgen05.st) and rescales
+//   its O row when the max grew, then releases the P.V MMA.  At the end it
+//   reads O, divides by the sum and stores the row.
+// Every wait is bounded; an expired wait aborts the CTA, which waits for its
+// issued MMAs (bounded) and frees its tensor memory.  No load uses cluster
+// multicast.
+#include "mote_common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace mote {
+namespace attnp {
+
+constexpr int kBM = 128;      // query rows per CTA (TMEM lanes)
+constexpr int kBN = 128;      // positions per K/V tile
+constexpr int kD = 64;        // head_dim (one 128-byte swizzle row)
+constexpr int kStages = 2;    // K/V tile stages
+constexpr int kSoftmaxWarps = 4;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 6 * 32;
+constexpr int kTileBytes = kBN * kD * 2;  // 16 KB (also the Q tile)
+
+// TMEM columns: S0 [0, 128), S1 [128, 256), O [256, 320); P_j (f16, two per
+// column) over the first 64 columns of S_{j % 2}.
+constexpr std::uint32_t kColO = 256;
+constexpr std::uint32_t kTmemCols = 512;
+
+struct Smem {
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kTileBytes;                // [kStages] tiles
+    static constexpr int kV = kK + kStages * kTileBytes;      // [kStages] tiles
+    static constexpr int kBar = kV + kStages * kTileBytes;
+    // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_ready[2], o_done, drained
+    static constexpr int kNumBars = 1 + 5 * kStages + 2;
+    static constexpr int kTmemSlot = kBar + kNumBars * 8;
+    static constexpr int kAbort = kTmemSlot + 4;
+    static constexpr int kUsed = kAbort + 4 + 1024;  // + 1024-byte alignment slack
+    // at least 120 KB: one CTA per SM, so a CTA's 512 TMEM columns never
+    // wait for another CTA of this kernel on the same SM
+    static constexpr int kBytes = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
+};
+
+// Instruction descriptors, kind::f16, f32 accumulate, f16 operands:
+// S: M = 128, N = 128, A and B K-major; PV: M = 128, N = 64, B MN-major.
+constexpr std::uint32_t kIdescS = (1u << 4) | ((kBN >> 3) << 17) | ((kBM >> 4) << 24);
+constexpr std::uint32_t kIdescPV = (1u << 4) | (1u << 16) | ((kD >> 3) << 17) | ((kBM >> 4) << 24);
+
+struct Params {
+    __half* out;
+    std::uint32_t tokens, start;
+    std::uint32_t q_heads, kv_heads;
+    std::uint64_t out_row_stride;  // elements between tokens (q_heads * 64)
+    float scale_log2;
+    std::uint32_t q_tiles;
+};
+
+__device__ __forceinline__ void tma_load_3d(std::uint32_t dst, const CUtensorMap* map, int x,
+                                            int y, int z, std::uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16, cta_group::1.
+__device__ __forceinline__ void umma_f16_ss(std::uint32_t tmem_d, std::uint64_t adesc,
+                                            std::uint64_t bdesc, std::uint32_t idesc,
+                                            std::uint32_t accumulate) {
+    const std::uint32_t mask = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+            tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask), "r"(mask), "r"(mask),
+        "r"(mask)
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive columns, no wait (the caller waits once).
+__device__ __forceinline__ void tmem_ld32_nowait(std::uint32_t taddr, std::uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(std::uint32_t taddr, const std::uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gqa_prefill_kernel(const __grid_constant__ CUtensorMap map_q,
+                       const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const Params p) {
+    using gemm::smem_desc_sw128;
+    using gemm::wait_or_abort;
+    extern __shared__ std::uint8_t smem_raw[];
+    const std::uint32_t raw_base = smem_u32(smem_raw);
+    const std::uint32_t base = (raw_base + 1023u) & ~1023u;
+    std::uint8_t* smem = smem_raw + (base - raw_base);
+    std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + Smem::kBar);
+    std::uint64_t* q_full = bars;
+    std::uint64_t* k_full = bars + 1;
+    std::uint64_t* v_full = k_full + kStages;
+    std::uint64_t* kv_empty = v_full + kStages;
+    std::uint64_t* s_full = kv_empty + kStages;
+    std::uint64_t* p_ready = s_full + kStages;
+    std::uint64_t* o_done = p_ready + kStages;
+    std::uint64_t* drained = o_done + 1;
+    volatile std::uint32_t* tmem_slot = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kTmemSlot);
+    volatile std::uint32_t* abort_flag = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kAbort);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    // the longest query tiles first (causal: later tiles attend more)
+    const std::uint32_t qt = p.q_tiles - 1 - blockIdx.x;
+    const std::uint32_t h = blockIdx.y;
+    const std::uint32_t kvh = h / (p.q_heads / p.kv_heads);
+    const std::uint32_t q0 = qt * kBM;
+    const std::uint32_t q_end = min(q0 + kBM, p.tokens);           // exclusive
+    const std::uint32_t keys = p.start + q_end;                     // attended positions
+    const std::uint32_t nkt = (keys + kBN - 1) / kBN;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+            mbar_init(&p_ready[s], kSoftmaxWarps);
+        }
+        mbar_init(o_done, 1);
+        mbar_init(drained, 1);
+        *abort_flag = 0u;
+        fence_mbarrier_init();
+    }
+    if (warp == kMmaWarp) gemm::tmem_alloc(base + Smem::kTmemSlot, kTmemCols);
+    gemm::tc_fence_before();
+    __syncthreads();
+    gemm::tc_fence_after();
+    const std::uint32_t tmem = *tmem_slot;
+    pdl_wait();
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, kTileBytes);
+            tma_load_3d(base + Smem::kQ, &map_q, 0, static_cast<int>(h), static_cast<int>(q0),
+                        smem_u32(q_full));
+            for (std::uint32_t j = 0; j < nkt; ++j) {
+                const int s = j % kStages;
+                if (j >= kStages &&
+                    !wait_or_abort(&kv_empty[s], ((j / kStages) - 1) & 1u, abort_flag))
+                    break;
+                mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+                tma_load_3d(base + Smem::kK + s * kTileBytes, &map_k, 0, static_cast<int>(kvh),
+                            static_cast<int>(j * kBN), smem_u32(&k_full[s]));
+                mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+                tma_load_3d(base + Smem::kV + s * kTileBytes, &map_v, 0, static_cast<int>(kvh),
+                            static_cast<int>(j * kBN), smem_u32(&v_full[s]));
+            }
+        }
+        __syncwarp();
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            auto issue_s = [&](std::uint32_t j) -> bool {
+                const int s = j % kStages;
+                if (!wait_or_abort(&k_full[s], (j / kStages) & 1u, abort_flag)) return false;
+                gemm::tc_fence_after();
+                const std::uint32_t kaddr = base + Smem::kK + s * kTileBytes;
+#pragma unroll
+                for (int k = 0; k < kD / 16; ++k)
+                    umma_f16_ss(tmem + s * kBN, smem_desc_sw128(base + Smem::kQ + k * 32),
+                                smem_desc_sw128(kaddr + k * 32), kIdescS, k != 0 ? 1u : 0u);
+                gemm::umma_commit(smem_u32(&s_full[s]));
+                return true;
+            };
+            bool ok = wait_or_abort(q_full, 0, abort_flag) && issue_s(0);
+            for (std::uint32_t j = 0; ok && j < nkt; ++j) {
+                const int s = j % kStages;
+                if (j + 1 < nkt && !issue_s(j + 1)) break;
+                if (!wait_or_abort(&p_ready[s], (j / kStages) & 1u, abort_flag)) break;
+                if (!wait_or_abort(&v_full[s], (j / kStages) & 1u, abort_flag)) break;
+                gemm::tc_fence_after();
+                const std::uint32_t vaddr = base + Smem::kV + s * kTileBytes;
+#pragma unroll
+                for (int k = 0; k < kBN / 16; ++k)
+                    // A = P (16 positions = 8 columns per step), B = V rows
+                    // of 16 positions (2048 bytes per step, MN-major)
+                    gemm::umma_f16_ta(tmem + kColO, tmem + s * kBN + k * 8,
+                                      smem_desc_sw128(vaddr + k * 2048), kIdescPV,
+                                      (j | k) != 0 ? 1u : 0u);
+                gemm::umma_commit(smem_u32(o_done));
+                gemm::umma_commit(smem_u32(&kv_empty[s]));
+            }
+            // every issued MMA completes before the tensor memory is freed
+            gemm::umma_commit(smem_u32(drained));
+            mbar_wait_bounded(drained, 0, &g_device_status);
+        }
+        __syncwarp();
+    } else {
+        // softmax: thread = query row r = TMEM lane
+        const int r = 32 * warp + lane;
+        const std::uint32_t lane_off = static_cast<std::uint32_t>(32 * warp) << 16;
+        const std::int64_t qpos = static_cast<std::int64_t>(p.start) + q0 + r;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (std::uint32_t j = 0; j < nkt && ok; ++j) {
+            const int s = j % kStages;
+            ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[s], (j / kStages) & 1u, abort_flag));
+            if (!ok) break;
+            gemm::tc_fence_after();
+            std::uint32_t v[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32_nowait(tmem + lane_off + s * kBN + 32 * c, v[c]);
+            tmem_wait_ld();
+            // scale (log2 units) and causal mask: position j*128 + col
+            const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN;
+            const bool masked_tile = kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + q0;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float x = __uint_as_float(v[c][i]) * p.scale_log2;
+                    if (masked_tile && kbase + 32 * c + i > qpos) x = -INFINITY;
+                    v[c][i] = __float_as_uint(x);
+                    mx = fmaxf(mx, x);
+                }
+            const float mnew = fmaxf(m, mx);  // finite: position 0 <= qpos is in tile 0
+            const float alpha = ex2f(m - mnew);  // 0 on the first tile (m = -inf)
+            float sum = 0.f;
+            std::uint32_t pk[2][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float a = ex2f(__uint_as_float(v[c][i]) - mnew);
+                    const float b = ex2f(__uint_as_float(v[c][i + 1]) - mnew);
+                    sum += a + b;
+                    std::uint32_t h2;
+                    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
+                    pk[c / 2][(c % 2) * 16 + i / 2] = h2;
+                }
+            l = fmaf(l, alpha, sum);
+            m = mnew;
+            // P over the first 64 columns of this S buffer
+            tmem_st32(tmem + lane_off + s * kBN, pk[0]);
+            tmem_st32(tmem + lane_off + s * kBN + 32, pk[1]);
+            tmem_wait_st();
+            // rescale O once the previous tile's P.V is complete
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (j - 1) & 1u, abort_flag));
+                if (!ok) break;
+                gemm::tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    std::uint32_t o[2][32];
+                    tmem_ld32_nowait(tmem + lane_off + kColO, o[0]);
+                    tmem_ld32_nowait(tmem + lane_off + kColO + 32, o[1]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 0; c < 2; ++c)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
+                    tmem_st32(tmem + lane_off + kColO, o[0]);
+                    tmem_st32(tmem + lane_off + kColO + 32, o[1]);
+                    tmem_wait_st();
+                }
+            }
+            gemm::tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_ready[s]))
+                             : "memory");
+        }
+        // output: O / l for the rows of this tile
+        if (ok && __all_sync(0xffffffffu, wait_or_abort(o_done, (nkt - 1) & 1u, abort_flag))) {
+            gemm::tc_fence_after();
+            std::uint32_t o[2][32];
+            tmem_ld32_nowait(tmem + lane_off + kColO, o[0]);
+            tmem_ld32_nowait(tmem + lane_off + kColO + 32, o[1]);
+            tmem_wait_ld();
+            if (q0 + r < p.tokens) {
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<std::uint64_t>(q0) + r) *
+                                                                   p.out_row_stride +
+                                                      static_cast<std::uint64_t>(h) * kD);
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        std::uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float a = __uint_as_float(o[c][i + 2 * e]) * inv;
+                            const float b = __uint_as_float(o[c][i + 2 * e + 1]) * inv;
+                            asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w[e]) : "f"(b), "f"(a));
+                        }
+                        dst[(32 * c + i) / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+            }
+        }
+    }
+    gemm::tc_fence_before();
+    __syncthreads();
+    gemm::tc_fence_after();
+    if (warp == kMmaWarp) gemm::tmem_dealloc(tmem, kTmemCols);
+    pdl_launch_dependents();
+}
+
+// 3-D tensor map over [rows, heads, 64] f16 (64 elements innermost), boxes
+// of 128 rows x 1 head x 64, 128-byte swizzle; rows past `rows` read zero.
+inline int make_map(CUtensorMap* map, const void* ptr, std::uint64_t rows, std::uint64_t heads) {
+    auto encode = gemm::encode_fn();
+    if (encode == nullptr) return static_cast<int>(cudaErrorNotSupported);
+    const cuuint64_t dims[3] = {kD, heads, rows};
+    const cuuint64_t strides[2] = {kD * 2, heads * kD * 2};
+    const cuuint32_t box[3] = {kD, 1, kBN};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return static_cast<int>(cudaErrorInvalidValue);
+    return kSuccess;
+}
+
+}  // namespace attnp
+}  // namespace mote
+
+// Causal prefill attention of `tokens` queries at positions start .. start +
+// tokens - 1 over cache rows row0 .. row0 + start + tokens - 1 (see the
+// header for the layout).  head_dim 64; q_heads % kv_heads == 0; 16-byte
+// aligned tensors; tokens == 0 returns 0.
+extern "C" int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_cache,
+                                                   const void* v_cache, void* out,
+                                                   uint64_t tokens, uint64_t start,
+                                                   uint64_t q_heads, uint64_t kv_heads,
+                                                   uint64_t head_dim, uint64_t row0,
+                                                   uint64_t cache_rows, float scale,
+                                                   void* stream) {
+    using namespace mote;
+    using namespace mote::attnp;
+    if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr ||
+        stream == nullptr)
+        return kInvalidValue;
+    if (tokens == 0 || q_heads == 0) return kSuccess;
+    if (head_dim != kD || kv_heads == 0 || q_heads % kv_heads != 0 || q_heads > 65535 ||
+        !std::isfinite(scale))
+        return kInvalidValue;
+    if (tokens > 0x7fffffffull || start > 0x7fffffffull || row0 + start + tokens > cache_rows ||
+        start + tokens > 0x7fffffffull)
+        return kInvalidValue;
+    for (const void* ptr : {q, k_cache, v_cache, static_cast<const void*>(out)})
+        if (reinterpret_cast<std::uintptr_t>(ptr) % 16 != 0) return kInvalidValue;
+    CUtensorMap map_q{}, map_k{}, map_v{};
+    int st = make_map(&map_q, q, tokens, q_heads);
+    // K/V maps start at the sequence's first row and end at its last
+    // attended row: positions past it read zeros
+    const std::uint64_t off = row0 * kv_heads * kD;
+    if (st == kSuccess)
+        st = make_map(&map_k, static_cast<const __half*>(k_cache) + off, start + tokens, kv_heads);
+    if (st == kSuccess)
+        st = make_map(&map_v, static_cast<const __half*>(v_cache) + off, start + tokens, kv_heads);
+    if (st != kSuccess) return st;
+    Params p{};
+    p.out = static_cast<__half*>(out);
+    p.tokens = static_cast<std::uint32_t>(tokens);
+    p.start = static_cast<std::uint32_t>(start);
+    p.q_heads = static_cast<std::uint32_t>(q_heads);
+    p.kv_heads = static_cast<std::uint32_t>(kv_heads);
+    p.out_row_stride = q_heads * kD;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.q_tiles = static_cast<std::uint32_t>((tokens + kBM - 1) / kBM);
+    static std::atomic<std::uint64_t> done{0};
+    st = ensure_dynamic_smem(gqa_prefill_kernel, Smem::kBytes, done);
+    if (st != kSuccess) return st;
+    return launch_pdl_smem(gqa_prefill_kernel, dim3(p.q_tiles, static_cast<unsigned>(q_heads)),
+                           dim3(kThreads), Smem::kBytes, static_cast<cudaStream_t>(stream), map_q,
+                           map_k, map_v, p);
+}

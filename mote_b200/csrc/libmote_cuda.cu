@@ -11,3 +11,4 @@
 #include "comm.cu"
 #include "dense_matmul.cu"
 #include "attention.cu"
+#include "attention_prefill.cu"

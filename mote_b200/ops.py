@@ -734,3 +734,37 @@ def gqa_attention_decode_f16(context: CudaContext, q: Tensor, k_cache: Tensor, v
     errors.check(lib().mote_cuda_gqa_attention_decode_f16(
         *ptrs, batch, qh, kvh, hd, seq_capacity, max_len, ctypes.c_float(scale), ws_ptr,
         ws_bytes, context.stream), "launch GQA decode attention kernel")
+
+
+def gqa_attention_prefill_f16(context: CudaContext, q: Tensor, k_cache: Tensor, v_cache: Tensor,
+                              output: Tensor, start: int, row0: int = 0,
+                              scale: float | None = None) -> None:
+    """Causal attention of a prefill chunk on the tensor cores: ``q``
+    [tokens, q_heads, 64] f16 holds the queries at positions ``start ..
+    start + tokens - 1`` of one sequence whose position ``p`` is cache row
+    ``row0 + p`` (the chunk's own K/V already appended);
+    ``output[t, h] = softmax_{p <= start + t}(scale q[t, h] . K[p, h // g]) . V[p, h // g]``.
+    ``scale`` defaults to ``1 / sqrt(head_dim)``."""
+    _plain(q, "q", DType.F16)
+    _rank(q, "q", 3)
+    _plain(output, "output", DType.F16)
+    _shape(output, "output", q.shape)
+    tokens, qh, hd = q.shape
+    for t, name in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        _plain(t, name, DType.F16)
+        _rank(t, name, 3)
+    rows, kvh, _ = k_cache.shape
+    _shape(k_cache, "k_cache", (rows, kvh, hd))
+    _shape(v_cache, "v_cache", k_cache.shape)
+    if row0 + start + tokens > rows:
+        raise errors.ShapeMismatch(tensor="k_cache", expected=(row0 + start + tokens, kvh, hd),
+                                   actual=k_cache.shape)
+    _not_aliased(output, "output", q, "q")
+    if tokens == 0 or qh == 0:
+        return
+    scale = 1.0 / math.sqrt(hd) if scale is None else float(scale)
+    ptrs = [context.storage(t).pointer for t in (q, k_cache, v_cache, output)]
+    context.inner.select()
+    errors.check(lib().mote_cuda_gqa_attention_prefill_f16(
+        *ptrs, tokens, start, qh, kvh, hd, row0, rows, ctypes.c_float(scale), context.stream),
+        "launch GQA prefill attention kernel")

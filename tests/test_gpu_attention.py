@@ -8,7 +8,12 @@ docs/roadmap.md:58-60), so the oracle is the standard definition in float64
 * attention outputs (f16): normwise max error <= 1e-3 and element-wise
   error with an rms floor <= 2e-3 against float64 -- the f16 output rounding
   is up to 4.9e-4, the softmax uses the hardware exp2 approximation
-  (relative error ~2^-22) and f32 accumulation.
+  (relative error ~2^-22) and f32 accumulation;
+* prefill (tensor cores): the probabilities P are rounded to f16 before the
+  P.V contraction (as in FlashAttention; the same class of error as the
+  Q4_0 prefill GEMM's f16 weights), so over long rows the rms-floored
+  element-wise error reaches ~3e-3 (2048 positions); its bound is 4e-3,
+  the normwise bound stays 1e-3.
 
 Shapes: Llama-3.2-1B's attention (32 query heads, 8 KV heads, head_dim 64)
 and Llama-3-8B's (32 / 8, head_dim 128) at decode with context lengths from
@@ -33,6 +38,7 @@ from mote_b200.types import DType, plain  # noqa: E402
 
 NORMWISE = 1e-3
 ELEMENTWISE = 2e-3
+PREFILL_ELEMENTWISE = 4e-3
 
 
 @pytest.fixture(scope="module")
@@ -144,3 +150,79 @@ def test_decode_argument_checks(ctx):
     with pytest.raises(errors.Runtime):
         ops.gqa_attention_decode_f16(ctx, bad, kc96, kc96, lens, ctx.empty(
             plain((1, 32, 96), DType.F16)), 128, 100)
+
+
+def _prefill_case(ctx, tokens, start, qh, kvh, seed, row0=0, extra_rows=0):
+    hd = 64
+    rng = np.random.default_rng(seed)
+    rows = row0 + start + tokens + extra_rows
+    kc = f16(rng.normal(0, 1, (rows, kvh, hd)))
+    vc = f16(rng.normal(0, 1, (rows, kvh, hd)))
+    q = f16(rng.normal(0, 1, (tokens, qh, hd)))
+    tq = ctx.from_bytes(plain(q.shape, DType.F16), q)
+    tk = ctx.from_bytes(plain(kc.shape, DType.F16), kc)
+    tv = ctx.from_bytes(plain(vc.shape, DType.F16), vc)
+    to = ctx.from_bytes(plain(q.shape, DType.F16), np.full(q.shape, np.nan, np.float16))
+    ops.gqa_attention_prefill_f16(ctx, tq, tk, tv, to, start, row0)
+    got = np.frombuffer(ctx.read_bytes(to), np.float16).astype(np.float32).reshape(q.shape)
+    assert ctx.device_status() == 0
+    n = start + tokens
+    ref = checker.gqa_attention_f64(q, kc[row0:row0 + n], vc[row0:row0 + n],
+                                    np.arange(start, start + tokens), 1.0 / math.sqrt(hd))
+    assert not np.isnan(got).any()
+    assert checker.rel_err_normwise(got, ref) <= NORMWISE
+    assert checker.rel_err_elementwise(got, ref) <= PREFILL_ELEMENTWISE
+    return got
+
+
+@pytest.mark.parametrize("tokens", [1, 5, 128, 129, 300, 512])
+def test_prefill_causal_from_position_zero(ctx, tokens):
+    """Llama-3.2-1B heads (32 query, 8 KV, head_dim 64): one query tile,
+    ragged tiles and several key tiles per query tile."""
+    _prefill_case(ctx, tokens, 0, 32, 8, seed=tokens)
+
+
+@pytest.mark.parametrize("tokens,start", [(64, 200), (128, 128), (200, 1000), (1, 777)])
+def test_prefill_chunk_after_cached_prefix(ctx, tokens, start):
+    """A chunk whose queries start after `start` cached positions (chunked
+    prefill): the first key tiles are fully visible, the last are masked."""
+    _prefill_case(ctx, tokens, start, 32, 8, seed=tokens + start)
+
+
+def test_prefill_sequence_at_a_cache_offset(ctx):
+    """The sequence sits at cache rows row0..; rows after its last position
+    hold other data (here random) that must not leak in."""
+    _prefill_case(ctx, 150, 40, 32, 8, seed=9, row0=300, extra_rows=500)
+
+
+@pytest.mark.parametrize("qh,kvh", [(8, 8), (64, 8), (12, 2)])
+def test_prefill_group_sizes(ctx, qh, kvh):
+    _prefill_case(ctx, 260, 30, qh, kvh, seed=qh + kvh)
+
+
+def test_prefill_long_chunk(ctx):
+    """2048 tokens: 16 query tiles x up to 16 key tiles each."""
+    _prefill_case(ctx, 2048, 0, 32, 8, seed=2048)
+
+
+def test_prefill_matches_decode_for_last_token(ctx):
+    """The last query of a prefill chunk attends exactly what a decode step
+    at that position attends."""
+    rng = np.random.default_rng(21)
+    tokens, start, qh, kvh, hd = 90, 300, 32, 8, 64
+    n = start + tokens
+    kc = f16(rng.normal(0, 1, (n, kvh, hd)))
+    vc = f16(rng.normal(0, 1, (n, kvh, hd)))
+    q = f16(rng.normal(0, 1, (tokens, qh, hd)))
+    tk = ctx.from_bytes(plain(kc.shape, DType.F16), kc)
+    tv = ctx.from_bytes(plain(vc.shape, DType.F16), vc)
+    tq = ctx.from_bytes(plain(q.shape, DType.F16), q)
+    to = ctx.empty(plain(q.shape, DType.F16))
+    ops.gqa_attention_prefill_f16(ctx, tq, tk, tv, to, start)
+    pre = np.frombuffer(ctx.read_bytes(to), np.float16).astype(np.float32).reshape(q.shape)
+    tq1 = ctx.from_bytes(plain((1, qh, hd), DType.F16), q[-1:])
+    lens = ctx.from_bytes(plain((1,), DType.I32), np.array([n], np.int32))
+    to1 = ctx.empty(plain((1, qh, hd), DType.F16))
+    ops.gqa_attention_decode_f16(ctx, tq1, tk, tv, lens, to1, n, n)
+    dec = np.frombuffer(ctx.read_bytes(to1), np.float16).astype(np.float32).reshape(1, qh, hd)
+    assert checker.rel_err_normwise(pre[-1:], dec) <= 2e-3

@@ -343,6 +343,48 @@ int mote_cuda_rope_cos_sin_f32(const void* positions, void* cos_out, void* sin_o
                                uint64_t tokens, uint64_t rotary_dim, double theta,
                                void* stream);
 
+/* ---- persistent decoder stack ---------------------------------------------
+ * The non-attention ops of num_layers Llama-style decoder layers at one token
+ * in ONE cooperative kernel launch (grid barriers in place of kernel
+ * boundaries; each warp's weight stream runs ahead across them).  No reference
+ * counterpart (the reference composes the operators launch by launch,
+ * docs/architecture.md:180-192).  Per layer l, with h = h_in for l == 0 and
+ * the previous layer's `out` after:
+ *   qkv = rope(rms_norm(h, gamma1) @ w_qkv^T)     (HalfSplit, rotary = head_dim)
+ *   h1  = h + attn @ w_o^T
+ *   a   = silu(rms_norm(h1, gamma2) @ w_gate^T) * (rms_norm(h1, gamma2) @ w_up^T)
+ *   out = h1 + a @ w_down^T
+ * Weights Q4_0 [rows, in/32*18]; f16 vectors; cos/sin f32 [head_dim/2] of the
+ * token's position.  `layers` is a DEVICE array of num_layers descriptors;
+ * `workspace` (256-byte aligned) holds the grid-barrier words and the down
+ * projection's partial sums: mote_cuda_q4_0_decoder_stack_workspace_bytes
+ * bytes (its first 256 are zeroed by the call).  hidden and ffn
+ * multiples of 256, head_dim a multiple of 16, q_heads a multiple of
+ * kv_heads, 16-byte aligned tensors (cos/sin 4-byte); eps finite and >= 0;
+ * otherwise 1.  A bounded grid-barrier wait that expires sets bit 1 of the
+ * device status. */
+typedef struct mote_cuda_stack_layer {
+    const void* w_qkv;
+    const void* w_o;
+    const void* w_gate;
+    const void* w_up;
+    const void* w_down;
+    const void* gamma1;
+    const void* gamma2;
+    const void* attn;
+    const void* cos;
+    const void* sin;
+    void* qkv;
+    void* h1;
+    void* a;
+    void* out;
+} mote_cuda_stack_layer;
+int mote_cuda_q4_0_decoder_stack_workspace_bytes(uint64_t hidden, uint64_t* bytes);
+int mote_cuda_q4_0_decoder_stack_f16(const void* layers, uint32_t num_layers, const void* h_in,
+                                     uint64_t hidden, uint64_t ffn, uint64_t q_heads,
+                                     uint64_t kv_heads, uint64_t head_dim, float epsilon,
+                                     void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* ---- grouped-query attention over a KV cache ----------------------------
  * No reference counterpart: the reference lists attention (GQA) with KV-cache
  * append and KV-cache operations as planned primitives (docs/roadmap.md:58-60,

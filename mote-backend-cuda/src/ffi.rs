@@ -17,6 +17,26 @@ use std::ffi::{c_char, c_void};
 pub type Status = i32;
 pub const SUCCESS: Status = 0;
 
+/// One layer of `mote_cuda_q4_0_decoder_stack_f16` (`mote_cuda_stack_layer`).
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct StackLayer {
+    pub w_qkv: *const c_void,
+    pub w_o: *const c_void,
+    pub w_gate: *const c_void,
+    pub w_up: *const c_void,
+    pub w_down: *const c_void,
+    pub gamma1: *const c_void,
+    pub gamma2: *const c_void,
+    pub attn: *const c_void,
+    pub cos: *const c_void,
+    pub sin: *const c_void,
+    pub qkv: *mut c_void,
+    pub h1: *mut c_void,
+    pub a: *mut c_void,
+    pub out: *mut c_void,
+}
+
 unsafe extern "C" {
     pub fn mote_cuda_get_device_count(count: *mut i32) -> i32;
     pub fn mote_cuda_set_device(ordinal: i32) -> i32;
@@ -70,6 +90,8 @@ unsafe extern "C" {
     pub fn mote_cuda_swiglu_f16(gate: *const c_void, up: *const c_void, output: *mut c_void, n: u64, stream: *mut c_void) -> i32;
     pub fn mote_cuda_embedding_gather_f16(table: *const c_void, ids: *const c_void, output: *mut c_void, tokens: u64, vocab: u64, hidden: u64, error_flag: *mut c_void, stream: *mut c_void) -> i32;
     pub fn mote_cuda_rope_cos_sin_f32(positions: *const c_void, cos_out: *mut c_void, sin_out: *mut c_void, tokens: u64, rotary_dim: u64, theta: f64, stream: *mut c_void) -> i32;
+    pub fn mote_cuda_q4_0_decoder_stack_workspace_bytes(hidden: u64, bytes: *mut u64) -> i32;
+    pub fn mote_cuda_q4_0_decoder_stack_f16(layers: *const c_void, num_layers: u32, h_in: *const c_void, hidden: u64, ffn: u64, q_heads: u64, kv_heads: u64, head_dim: u64, epsilon: f32, workspace: *mut c_void, workspace_bytes: u64, stream: *mut c_void) -> i32;
     pub fn mote_cuda_kv_cache_append_f16(k_new: *const c_void, v_new: *const c_void, k_cache: *mut c_void, v_cache: *mut c_void, slots: *const c_void, tokens: u64, kv_heads: u64, head_dim: u64, cache_rows: u64, error_flag: *mut c_void, stream: *mut c_void) -> i32;
     pub fn mote_cuda_gqa_attention_decode_workspace_bytes(batch: u64, q_heads: u64, kv_heads: u64, head_dim: u64, max_len: u64, bytes: *mut u64) -> i32;
     pub fn mote_cuda_gqa_attention_decode_f16(q: *const c_void, k_cache: *const c_void, v_cache: *const c_void, seq_lens: *const c_void, out: *mut c_void, batch: u64, q_heads: u64, kv_heads: u64, head_dim: u64, seq_capacity: u64, max_len: u64, scale: f32, workspace: *mut c_void, workspace_bytes: u64, stream: *mut c_void) -> i32;

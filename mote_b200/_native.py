@@ -88,6 +88,9 @@ SIGNATURES: dict[str, tuple] = {
                                                ctypes.c_float, P, U64, P]),
     "mote_cuda_gqa_attention_prefill_f16": (I, [P, P, P, P, U64, U64, U64, U64, U64, U64, U64,
                                                 ctypes.c_float, P]),
+    "mote_cuda_q4_0_decoder_stack_workspace_bytes": (I, [U64, ctypes.POINTER(U64)]),
+    "mote_cuda_q4_0_decoder_stack_f16": (I, [P, U32, P, U64, U64, U64, U64, U64, ctypes.c_float,
+                                             P, U64, P]),
     "mote_cuda_comm_unique_id": (I, [P]),
     "mote_cuda_comm_init": (I, [ctypes.POINTER(P), I, P, I]),
     "mote_cuda_comm_init_timeout": (I, [ctypes.POINTER(P), I, P, I, U64]),

@@ -4,6 +4,7 @@
 #include "runtime.cu"
 #include "q4_0_gemm_tcgen05.cu"
 #include "q4_0_linear.cu"
+#include "decoder_stack.cu"
 #include "q8_0_linear.cu"
 #include "kquant_linear.cu"
 #include "layer_ops.cu"

@@ -67,6 +67,7 @@ class DecoderLayerQ4_0:
         self.n2 = ctx.empty(plain((1, h), DType.F16))
         self.a = ctx.empty(plain((1, s.ffn), DType.F16))
         self.out = ctx.empty(plain((1, h), DType.F16))      # h2
+        self.h1 = ctx.empty(plain((1, h), DType.F16))       # h1 of the persistent stack
         self.cos = ctx.empty(plain((1, s.head_dim // 2), DType.F32))
         self.sin = ctx.empty(plain((1, s.head_dim // 2), DType.F32))
         self.pos = ctx.empty(plain((1,), DType.I32))
@@ -169,3 +170,48 @@ def random_layer(ctx: CudaContext, shape: LayerShape, seed: int = 0, vocab: int 
                              w_gate=q4(shape.ffn, h), w_up=q4(shape.ffn, h),
                              w_down=q4(h, shape.ffn), gamma1=g1, gamma2=g2)
     return layer
+
+
+class DecoderStackQ4_0:
+    """A stack of layers run by the persistent kernel
+    (``mote_cuda_q4_0_decoder_stack_f16``): one cooperative launch for all
+    layers, grid barriers in place of kernel boundaries.  Per layer it writes
+    ``qkv`` (RoPE applied), ``h1`` (= h + attn @ Wo^T, its own buffer), ``a``
+    (SwiGLU) and ``out``; layer 0 reads ``hidden``, layer l the previous
+    layer's ``out`` -- the arithmetic of ``step_fused``."""
+
+    def __init__(self, ctx: CudaContext, layers: list[DecoderLayerQ4_0]):
+        import ctypes
+
+        import numpy as np
+
+        self.ctx, self.layers = ctx, layers
+        s = layers[0].shape
+        rows = []
+        for layer in layers:
+            rows.append([t.pointer for t in (layer.w_qkv, layer.w_o, layer.w_gate, layer.w_up,
+                                             layer.w_down, layer.gamma1, layer.gamma2,
+                                             layer.attn, layer.cos, layer.sin, layer.qkv,
+                                             layer.h1, layer.a, layer.out)])
+        table = np.asarray(rows, np.uint64).reshape(-1)
+        self.table = ctx.from_bytes(plain((table.size * 8,), DType.U8), table.view(np.uint8))
+        from ._native import lib
+        from . import errors
+
+        need = ctypes.c_uint64(0)
+        errors.check(lib().mote_cuda_q4_0_decoder_stack_workspace_bytes(s.hidden,
+                                                                         ctypes.byref(need)),
+                     "stack workspace size")
+        self.workspace = ctx.empty(plain((need.value,), DType.U8))
+        self._c = ctypes
+
+    def run(self, hidden: Tensor) -> None:
+        from ._native import lib
+        from . import errors
+
+        s = self.layers[0].shape
+        self.ctx.inner.select()
+        errors.check(lib().mote_cuda_q4_0_decoder_stack_f16(
+            self.table.pointer, len(self.layers), hidden.pointer, s.hidden, s.ffn, s.q_heads,
+            s.kv_heads, s.head_dim, self._c.c_float(s.eps), self.workspace.pointer,
+            self.workspace.desc.required_span_bytes, self.ctx.stream), "launch decoder stack")

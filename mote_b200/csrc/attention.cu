@@ -17,22 +17,30 @@
 //   rows (one slot per token), 16-byte vectors; a slot outside the cache
 //   sets an error flag and is skipped (as the embedding gather does).
 // * Decode (one query token per sequence) is HBM-bound: every cached K and
-//   V byte of the sequence is read once.  Flash-decoding: a CTA takes one
-//   (sequence, KV head, chunk of positions) and all q_heads / kv_heads query
-//   heads that share the KV head, streams its chunk through shared memory in
-//   128-position tiles (cp.async, double-buffered), keeps an online softmax
-//   (running max and sum per query head, exp2 with the scale folded in) and
-//   f32 output accumulators, and writes its unnormalised partial output with
-//   its max and sum to the workspace; a second kernel merges the chunks.
-//   With a single chunk per sequence the first kernel writes the output.
+//   V byte of the sequence is read once.  Flash-decoding on the tensor
+//   cores: a CTA takes one (sequence, KV head, group of up to 16 query
+//   heads, chunk of positions); its query heads are the 16 rows of
+//   mma.sync.m16n8k16 (f16 in, f32 accumulate).  Each of its four warps
+//   streams tiles of 4096 / head_dim positions through a private
+//   three-stage cp.async ring (K and V rows swizzled for conflict-free
+//   ldmatrix) and computes S = Q K^T, an online softmax on the S
+//   accumulators (exp2 with the scale folded in), and O += P V with the S
+//   accumulators reused as the A operand.  P is split into f16 hi + lo
+//   parts (two MMAs), so the probabilities keep ~22 bits.  The warps'
+//   states meet in shared memory; the CTA writes its output, or with
+//   several chunks per sequence its unnormalised partial output with its
+//   max and sum, and a second kernel merges the chunks.
 #include "mote_common.cuh"
 
 namespace mote {
 namespace attn {
 
-constexpr int kThreads = 128;
-constexpr int kTile = 128;        // cached positions per shared-memory tile
-constexpr int kMaxGroupDim = 512; // (q_heads / kv_heads) * head_dim per CTA
+constexpr int kThreads = 128;        // decode split kernel: four warps
+constexpr int kWarpsPerCta = 4;
+constexpr int kStageBytes = 16384;   // K and V of one tile
+constexpr int kStagesPerWarp = 3;    // 48 KB ring per warp, 192 KB per CTA
+constexpr int kHeadsPerCta = 16;     // query heads per CTA (the MMA rows)
+constexpr int kSplitSmem = kWarpsPerCta * kStagesPerWarp * kStageBytes;
 
 // ---------------------------------------------------------------------------
 // KV-cache append
@@ -73,7 +81,8 @@ struct DecodeParams {
     float* part_ml;             // [batch, q_heads, chunks, 2] (max, sum), log2 units
     std::uint64_t seq_capacity; // cache rows per sequence
     std::uint32_t q_heads, kv_heads, group;  // group = q_heads / kv_heads
-    std::uint32_t chunks, chunk_len;         // positions per chunk (multiple of kTile)
+    std::uint32_t head_groups;               // CTAs per KV head: ceil(group / 16)
+    std::uint32_t chunks, chunk_len;         // positions per chunk (whole tiles)
     std::uint64_t max_len;      // positions beyond are not attended
     float scale_log2;           // scale * log2(e)
 };
@@ -90,241 +99,287 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// Shared memory of the split kernel (byte offsets).
+// Geometry of the decode split kernel for head_dim D.  A tile is kPos
+// cached positions of one KV head: K (8 KB) then V (8 KB) in shared memory,
+// each [kPos rows][D] f16 with the 16-byte chunk c of row r stored at chunk
+// c ^ (r & 7), so the eight rows an ldmatrix reads at one chunk column fall
+// in eight different 16-byte bank groups.
 template <int D>
-struct DecodeSmem {
-    static constexpr int GMAX = kMaxGroupDim / D;  // query heads per CTA
-    static constexpr int kRowBytes = D * 2;        // one position of one KV head
-    static constexpr int kTileBytes = kTile * kRowBytes;
-    static constexpr int kK = 0;                          // [2][kTile][D] f16
-    static constexpr int kV = kK + 2 * kTileBytes;        // [2][kTile][D] f16
-    static constexpr int kScores = kV + 2 * kTileBytes;   // [GMAX][kTile] f32
-    static constexpr int kAlpha = kScores + GMAX * kTile * 4;  // [GMAX] rescale of this tile
-    static constexpr int kMax = kAlpha + GMAX * 4;        // [GMAX] running max (log2 units)
-    static constexpr int kSum = kMax + GMAX * 4;          // [GMAX] running sum
-    static constexpr int kBytes = kSum + GMAX * 4;
-    // after the last tile the K buffers hold the 16 position lanes' partial
-    // outputs [16][GMAX][D] f32
-    static_assert(16 * kMaxGroupDim * 4 <= 2 * kTileBytes, "lane reduction fits the K buffers");
+struct DecodeTile {
+    static constexpr int kPos = 4096 / D;              // 64 (D = 64) or 32 (D = 128)
+    static constexpr int kCpr = D / 8;                 // 16-byte chunks per row
+    static constexpr int kHalfBytes = kPos * D * 2;    // 8 KB: the K (or V) rows
+    static constexpr int kChunksPerLane = kHalfBytes / 16 / 32;  // 16
+    static constexpr int kRowStep = 32 / kCpr;         // rows between a lane's chunks
+    static_assert(2 * kHalfBytes == kStageBytes, "a stage holds K and V of one tile");
+    static_assert(kPos % 16 == 0, "whole k16 steps of positions");
 };
 
-// One CTA: sequence b = blockIdx.z, KV head = blockIdx.y, chunk blockIdx.x.
-// Threads: 16 position lanes x 8 dimension slices of D/8 elements.
-template <int D>
-__global__ void __launch_bounds__(kThreads) gqa_decode_split_kernel(const DecodeParams p) {
-    using S = DecodeSmem<D>;
-    constexpr int DPT = D / 8;      // dimensions per thread
-    constexpr int GMAX = S::GMAX;
-    constexpr int kRowBytes = S::kRowBytes;
-    constexpr int kTileBytes = S::kTileBytes;
-    static_assert(DPT % 8 == 0, "16-byte slices");
-    extern __shared__ __align__(128) std::uint8_t smem[];
-    std::uint8_t* kt = smem + S::kK;
-    std::uint8_t* vt = smem + S::kV;
-    float* ps = reinterpret_cast<float*>(smem + S::kScores);
-    float* alpha_s = reinterpret_cast<float*>(smem + S::kAlpha);
-    float* mrun = reinterpret_cast<float*>(smem + S::kMax);
-    float* lrun = reinterpret_cast<float*>(smem + S::kSum);
-    float* red = reinterpret_cast<float*>(smem + S::kK);
+__device__ __forceinline__ void ldsm_x4(std::uint32_t addr, std::uint32_t& r0, std::uint32_t& r1,
+                                        std::uint32_t& r2, std::uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
 
-    const int tid = threadIdx.x;
-    const int slice = tid & 7;
-    const int lane16 = tid >> 3;
-    const std::uint32_t b = blockIdx.z, kvh = blockIdx.y, chunk = blockIdx.x;
-    const std::uint32_t G = p.group;
-    if (tid < GMAX) {
-        mrun[tid] = -INFINITY;
-        lrun[tid] = 0.f;
-    }
+__device__ __forceinline__ void ldsm_x4_trans(std::uint32_t addr, std::uint32_t& r0,
+                                              std::uint32_t& r1, std::uint32_t& r2,
+                                              std::uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ std::uint32_t half2_bits(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    std::uint32_t u;
+    memcpy(&u, &h, sizeof(u));
+    return u;
+}
+
+// p = hi + lo with hi = f16(p) and lo = f16(p - hi): the probabilities keep
+// about 22 bits through the f16 P.V contraction.
+__device__ __forceinline__ void split_pair(float a, float b, std::uint32_t& hi,
+                                           std::uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    memcpy(&hi, &h, sizeof(hi));
+    lo = half2_bits(a - f.x, b - f.y);
+}
+
+// One CTA: sequence b = blockIdx.z, (KV head, head group) = blockIdx.y,
+// chunk = blockIdx.x.  The CTA's up to 16 query heads are the MMA rows.
+// Warp w takes the chunk's tiles w, w + 4, ... through its own ring of
+// kStagesPerWarp stages and keeps its own online softmax; the four warps'
+// states meet in shared memory at the end.
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) gqa_decode_split_kernel(const DecodeParams p) {
+    using T = DecodeTile<D>;
+    constexpr int TP = T::kPos;
+    constexpr int CPR = T::kCpr;
+    constexpr int NK = T::kChunksPerLane;
+    constexpr int RS = T::kRowStep;
+    constexpr int NT = TP / 8;   // n8 tiles of S per tile
+    constexpr int DN = D / 8;    // n8 tiles of O
+    constexpr int DK = D / 16;   // k16 steps of S
+    extern __shared__ __align__(128) std::uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const std::uint32_t b = blockIdx.z;
+    const std::uint32_t kvh = blockIdx.y / p.head_groups;
+    const std::uint32_t hgrp = blockIdx.y - kvh * p.head_groups;
+    const std::uint32_t chunk = blockIdx.x;
+    const std::uint32_t h0 = kvh * p.group + hgrp * kHeadsPerCta;  // first query head
+    const std::uint32_t nh = min(static_cast<std::uint32_t>(kHeadsPerCta),
+                                 p.group - hgrp * kHeadsPerCta);
+    std::uint8_t* wsm = smem + warp * (kStagesPerWarp * kStageBytes);
+    const std::uint32_t ring = smem_u32(wsm);
 
     pdl_wait();
     const std::int64_t len = min(static_cast<std::int64_t>(p.seq_lens[b]),
                                  static_cast<std::int64_t>(p.max_len));
     const std::int64_t t0 = static_cast<std::int64_t>(chunk) * p.chunk_len;
     const std::int64_t t1 = min(len, t0 + static_cast<std::int64_t>(p.chunk_len));
-    const std::uint64_t rowbase = static_cast<std::uint64_t>(b) * p.seq_capacity;
+    const int chunk_tiles = t1 > t0 ? static_cast<int>((t1 - t0 + TP - 1) / TP) : 0;
+    const int my_tiles = chunk_tiles > warp ? (chunk_tiles - warp + kWarpsPerCta - 1) / kWarpsPerCta : 0;
 
-    // query slices (f32) of the group's heads
-    float qv[GMAX][DPT];
+    // Q as the MMA A operand: rows g and g + 8 (query heads h0 + row; rows
+    // past the CTA's heads are zero), k-step s covers dimensions 16s .. 16s+15.
+    std::uint32_t qa[DK][4];
+    {
+        const __half* q_b = p.q + static_cast<std::uint64_t>(b) * p.q_heads * D;
+        const bool r0ok = static_cast<std::uint32_t>(g) < nh, r1ok = static_cast<std::uint32_t>(g + 8) < nh;
+        const std::uint32_t* q0 = reinterpret_cast<const std::uint32_t*>(q_b + (h0 + g) * D);
+        const std::uint32_t* q1 = reinterpret_cast<const std::uint32_t*>(q_b + (h0 + g + 8) * D);
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-#pragma unroll
-        for (int j = 0; j < DPT; ++j) qv[g][j] = 0.f;
-        if (static_cast<std::uint32_t>(g) < G) {
-            const __half* qh = p.q + (static_cast<std::uint64_t>(b) * p.q_heads + kvh * G + g) * D +
-                               slice * DPT;
-#pragma unroll
-            for (int j = 0; j < DPT; j += 8) {
-                const uint4 w = *reinterpret_cast<const uint4*>(qh + j);
-                const std::uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = half2_bits_to_float2(ws[e]);
-                    qv[g][j + 2 * e] = f.x;
-                    qv[g][j + 2 * e + 1] = f.y;
-                }
-            }
+        for (int s = 0; s < DK; ++s) {
+            qa[s][0] = r0ok ? q0[8 * s + t] : 0u;
+            qa[s][1] = r1ok ? q1[8 * s + t] : 0u;
+            qa[s][2] = r0ok ? q0[8 * s + 4 + t] : 0u;
+            qa[s][3] = r1ok ? q1[8 * s + 4 + t] : 0u;
         }
     }
-    float o[GMAX][DPT];
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g)
-#pragma unroll
-        for (int j = 0; j < DPT; ++j) o[g][j] = 0.f;
 
-    const int tiles = t1 > t0 ? static_cast<int>((t1 - t0 + kTile - 1) / kTile) : 0;
-    // tile loader: kTile rows of K and of V, 16-byte copies; rows past the
-    // end re-read the last valid row (their scores are masked)
-    auto load_tile = [&](int tile, int buf) {
-        const std::int64_t base = t0 + static_cast<std::int64_t>(tile) * kTile;
-        constexpr int kVecsPerRow = kRowBytes / 16;
-        for (int i = tid; i < kTile * kVecsPerRow; i += kThreads) {
-            const int r = i / kVecsPerRow;
-            const int c = i - r * kVecsPerRow;
-            const std::int64_t pos = min(base + r, t1 - 1);
-            const std::uint64_t off =
-                ((rowbase + static_cast<std::uint64_t>(pos)) * p.kv_heads + kvh) * kRowBytes + c * 16;
-            cp_async_16_default(smem_u32(kt + buf * kTileBytes + r * kRowBytes + c * 16),
-                                reinterpret_cast<const std::uint8_t*>(p.k_cache) + off);
-            cp_async_16_default(smem_u32(vt + buf * kTileBytes + r * kRowBytes + c * 16),
-                                reinterpret_cast<const std::uint8_t*>(p.v_cache) + off);
+    // Loader: lane l copies chunks l + 32k (row r0 + k RS, chunk column c)
+    // of K and of V; rows past the chunk's end re-read its last row (their
+    // scores are masked, and re-read rows hold finite cache data).
+    const int r0 = lane / CPR, c = lane % CPR;
+    const std::uint64_t row_bytes = static_cast<std::uint64_t>(p.kv_heads) * D * 2;
+    const std::uint8_t* kbase = reinterpret_cast<const std::uint8_t*>(p.k_cache) +
+                                (static_cast<std::uint64_t>(b) * p.seq_capacity * p.kv_heads + kvh) * D * 2 + c * 16;
+    const std::uint8_t* vbase = reinterpret_cast<const std::uint8_t*>(p.v_cache) +
+                                (static_cast<std::uint64_t>(b) * p.seq_capacity * p.kv_heads + kvh) * D * 2 + c * 16;
+    auto issue = [&](int n) {
+        if (n < my_tiles) {
+            const std::int64_t pos0 = t0 + static_cast<std::int64_t>(warp + kWarpsPerCta * n) * TP;
+            const std::uint32_t dst0 = ring + (n % kStagesPerWarp) * kStageBytes;
+#pragma unroll
+            for (int k = 0; k < NK; ++k) {
+                const int r = r0 + k * RS;
+                const std::int64_t pos = min(pos0 + r, t1 - 1);
+                const std::uint64_t off = static_cast<std::uint64_t>(pos) * row_bytes;
+                const std::uint32_t dst = dst0 + (r * CPR + (c ^ (r & 7))) * 16;
+                cp_async_16_default(dst, kbase + off);
+                cp_async_16_default(dst + T::kHalfBytes, vbase + off);
+            }
         }
         cp_async_commit();
     };
-    if (tiles > 0) load_tile(0, 0);
-    for (int tile = 0; tile < tiles; ++tile) {
-        const int buf = tile & 1;
-        if (tile + 1 < tiles) {
-            load_tile(tile + 1, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        const std::int64_t base = t0 + static_cast<std::int64_t>(tile) * kTile;
-        // scores: 16 positions at a time, 8 threads per position
-#pragma unroll 2
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-            const int r = kk * 16 + lane16;
-            const std::uint8_t* krow = kt + buf * kTileBytes + r * kRowBytes + slice * DPT * 2;
-            float kv[DPT];
 #pragma unroll
-            for (int j = 0; j < DPT; j += 8) {
-                const uint4 w = *reinterpret_cast<const uint4*>(krow + 2 * j);
-                const std::uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int s = 0; s + 1 < kStagesPerWarp; ++s) issue(s);
+
+    // ldmatrix lane addresses (bytes from a stage): matrix i = lane / 8,
+    // row r = lane % 8.  K (non-transposed): rows 8j + r, chunk 4kk + i.
+    // V (transposed): rows 16kk + 8 (i & 1) + r, chunk n + (i >> 1).
+    const int li = lane >> 3, lr = lane & 7;
+    std::uint32_t koff[DK / 2];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = half2_bits_to_float2(ws[e]);
-                    kv[j + 2 * e] = f.x;
-                    kv[j + 2 * e + 1] = f.y;
-                }
-            }
-            const bool valid = base + r < t1;
+    for (int kk = 0; kk < DK / 2; ++kk) koff[kk] = (lr * CPR + ((4 * kk + li) ^ lr)) * 16;
+    std::uint32_t voff[DN / 2];
 #pragma unroll
-            for (int g = 0; g < GMAX; ++g) {
-                float a = 0.f;
+    for (int n = 0; n < DN / 2; ++n)
+        voff[n] = T::kHalfBytes + ((8 * (li & 1) + lr) * CPR + ((2 * n + (li >> 1)) ^ lr)) * 16;
+
+    float m0 = -INFINITY, m1 = -INFINITY;  // running max of rows g, g + 8 (log2 units)
+    float l0 = 0.f, l1 = 0.f;              // this lane's share of the running sums
+    float o[DN][4];
 #pragma unroll
-                for (int j = 0; j < DPT; ++j) a = fmaf(qv[g][j], kv[j], a);
-                a += __shfl_xor_sync(0xffffffffu, a, 1);
-                a += __shfl_xor_sync(0xffffffffu, a, 2);
-                a += __shfl_xor_sync(0xffffffffu, a, 4);
-                if (slice == 0 && static_cast<std::uint32_t>(g) < G)
-                    ps[g * kTile + r] = valid ? a * p.scale_log2 : -INFINITY;
-            }
-        }
-        __syncthreads();
-        // online softmax per query head: warp w takes heads w, w + 4, ...
-        {
-            const int w = tid >> 5, ln = tid & 31;
-            for (int g = w; g < static_cast<int>(G); g += kThreads / 32) {
-                float v[kTile / 32];
-                float mx = -INFINITY;
+    for (int n = 0; n < DN; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    for (int n = 0; n < my_tiles; ++n) {
+        issue(n + kStagesPerWarp - 1);
+        cp_async_wait<kStagesPerWarp - 1>();
+        __syncwarp();
+        const std::uint32_t st = ring + (n % kStagesPerWarp) * kStageBytes;
+        // S = Q K^T for the tile's TP positions (columns)
+        float s[NT][4];
 #pragma unroll
-                for (int i = 0; i < kTile / 32; ++i) {
-                    v[i] = ps[g * kTile + ln + 32 * i];
-                    mx = fmaxf(mx, v[i]);
-                }
+        for (int j = 0; j < NT; ++j) {
+            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1)
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-                const float mold = mrun[g];
-                const float mnew = fmaxf(mold, mx);  // finite: a tile has a valid position
-                float sum = 0.f;
-#pragma unroll
-                for (int i = 0; i < kTile / 32; ++i) {
-                    v[i] = ex2(v[i] - mnew);
-                    ps[g * kTile + ln + 32 * i] = v[i];
-                    sum += v[i];
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                if (ln == 0) {
-                    const float a = mold == -INFINITY ? 0.f : ex2(mold - mnew);
-                    alpha_s[g] = a;
-                    mrun[g] = mnew;
-                    lrun[g] = fmaf(lrun[g], a, sum);
-                }
+            for (int kk = 0; kk < DK / 2; ++kk) {
+                std::uint32_t b0, b1, b2, b3;
+                ldsm_x4(st + koff[kk] + j * 8 * CPR * 16, b0, b1, b2, b3);
+                mma_16816(s[j], qa[2 * kk][0], qa[2 * kk][1], qa[2 * kk][2], qa[2 * kk][3], b0, b1, s[j]);
+                mma_16816(s[j], qa[2 * kk + 1][0], qa[2 * kk + 1][1], qa[2 * kk + 1][2], qa[2 * kk + 1][3],
+                          b2, b3, s[j]);
             }
         }
-        __syncthreads();
-        // P . V: position lane lane16 takes positions lane16 + 16 kk
+        // scale into log2 units; mask positions past the chunk's end
+        const std::int64_t valid = t1 - (t0 + static_cast<std::int64_t>(warp + kWarpsPerCta * n) * TP);
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-            if (static_cast<std::uint32_t>(g) < G) {
-                const float a = alpha_s[g];
+        for (int j = 0; j < NT; ++j)
 #pragma unroll
-                for (int j = 0; j < DPT; ++j) o[g][j] *= a;
+            for (int e = 0; e < 4; ++e) {
+                const int col = 8 * j + 2 * t + (e & 1);
+                float x = s[j][e] * p.scale_log2;
+                if (valid < TP && col >= valid) x = -INFINITY;
+                s[j][e] = x;
+                if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+            }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        // every tile holds a valid position, so the new maxima are finite
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float a0 = ex2(m0 - mn0), a1 = ex2(m1 - mn1);  // ex2(-inf) = 0
+        m0 = mn0;
+        m1 = mn1;
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            s[j][0] = ex2(s[j][0] - mn0);
+            s[j][1] = ex2(s[j][1] - mn0);
+            s[j][2] = ex2(s[j][2] - mn1);
+            s[j][3] = ex2(s[j][3] - mn1);
+            ps0 += s[j][0] + s[j][1];
+            ps1 += s[j][2] + s[j][3];
+        }
+        l0 = fmaf(l0, a0, ps0);
+        l1 = fmaf(l1, a1, ps1);
+#pragma unroll
+        for (int dn = 0; dn < DN; ++dn) {
+            o[dn][0] *= a0;
+            o[dn][1] *= a0;
+            o[dn][2] *= a1;
+            o[dn][3] *= a1;
+        }
+        // O += P V: the S accumulators of n8 tiles 2kk, 2kk+1 are the A
+        // fragment of k-step kk (positions 16kk .. 16kk+15)
+#pragma unroll
+        for (int kk = 0; kk < TP / 16; ++kk) {
+            std::uint32_t ah[4], al[4];
+            split_pair(s[2 * kk][0], s[2 * kk][1], ah[0], al[0]);
+            split_pair(s[2 * kk][2], s[2 * kk][3], ah[1], al[1]);
+            split_pair(s[2 * kk + 1][0], s[2 * kk + 1][1], ah[2], al[2]);
+            split_pair(s[2 * kk + 1][2], s[2 * kk + 1][3], ah[3], al[3]);
+#pragma unroll
+            for (int dn = 0; dn < DN / 2; ++dn) {
+                std::uint32_t b0, b1, b2, b3;
+                ldsm_x4_trans(st + voff[dn] + kk * 16 * CPR * 16, b0, b1, b2, b3);
+                mma_16816(o[2 * dn], ah[0], ah[1], ah[2], ah[3], b0, b1, o[2 * dn]);
+                mma_16816(o[2 * dn], al[0], al[1], al[2], al[3], b0, b1, o[2 * dn]);
+                mma_16816(o[2 * dn + 1], ah[0], ah[1], ah[2], ah[3], b2, b3, o[2 * dn + 1]);
+                mma_16816(o[2 * dn + 1], al[0], al[1], al[2], al[3], b2, b3, o[2 * dn + 1]);
             }
         }
-#pragma unroll 2
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-            const int r = kk * 16 + lane16;
-            const std::uint8_t* vrow = vt + buf * kTileBytes + r * kRowBytes + slice * DPT * 2;
-            float vv[DPT];
-#pragma unroll
-            for (int j = 0; j < DPT; j += 8) {
-                const uint4 w = *reinterpret_cast<const uint4*>(vrow + 2 * j);
-                const std::uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = half2_bits_to_float2(ws[e]);
-                    vv[j + 2 * e] = f.x;
-                    vv[j + 2 * e + 1] = f.y;
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < GMAX; ++g) {
-                if (static_cast<std::uint32_t>(g) < G) {
-                    const float pw = ps[g * kTile + r];
-#pragma unroll
-                    for (int j = 0; j < DPT; ++j) o[g][j] = fmaf(pw, vv[j], o[g][j]);
-                }
-            }
-        }
-        __syncthreads();  // the tile's buffers and scores are reused
+        __syncwarp();  // the slot is refilled by the next iteration's issue
     }
-    __syncthreads();  // (no tiles) the running statistics are initialised
-    // merge the 16 position lanes' partial outputs (K buffers are free now)
+    cp_async_wait<0>();
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    // The warps' states meet in shared memory, each warp writing into its
+    // own (drained) ring: O [16][D] f32, then max [16] and sum [16].
+    __syncwarp();
+    float* co = reinterpret_cast<float*>(wsm);
+    float* cm = co + kHeadsPerCta * D;
+    float* cl = cm + kHeadsPerCta;
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g)
-        if (static_cast<std::uint32_t>(g) < G)
-#pragma unroll
-            for (int j = 0; j < DPT; ++j) red[(lane16 * GMAX + g) * D + slice * DPT + j] = o[g][j];
+    for (int dn = 0; dn < DN; ++dn) {
+        *reinterpret_cast<float2*>(co + g * D + 8 * dn + 2 * t) = make_float2(o[dn][0], o[dn][1]);
+        *reinterpret_cast<float2*>(co + (g + 8) * D + 8 * dn + 2 * t) = make_float2(o[dn][2], o[dn][3]);
+    }
+    if (t == 0) {
+        cm[g] = m0;
+        cm[g + 8] = m1;
+        cl[g] = l0;
+        cl[g + 8] = l1;
+    }
     __syncthreads();
-    const std::uint64_t qh0 = static_cast<std::uint64_t>(b) * p.q_heads + kvh * G;
-    for (std::uint32_t i = tid; i < G * D; i += kThreads) {
-        const std::uint32_t g = i / D, d = i - g * D;
-        float acc = 0.f;
-#pragma unroll 4
-        for (int r = 0; r < 16; ++r) acc += red[(r * GMAX + g) * D + d];
+    const std::uint64_t qh0 = static_cast<std::uint64_t>(b) * p.q_heads + h0;
+    for (std::uint32_t i = threadIdx.x; i < nh * D; i += kThreads) {
+        const std::uint32_t row = i / D, d = i - row * D;
+        float mw[kWarpsPerCta];
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarpsPerCta; ++w) {
+            mw[w] = reinterpret_cast<const float*>(smem + w * (kStagesPerWarp * kStageBytes))[kHeadsPerCta * D + row];
+            M = fmaxf(M, mw[w]);
+        }
+        float acc = 0.f, L = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kWarpsPerCta; ++w) {
+                const float* cw = reinterpret_cast<const float*>(smem + w * (kStagesPerWarp * kStageBytes));
+                const float wt = ex2(mw[w] - M);  // a warp without tiles: ex2(-inf) = 0
+                acc = fmaf(cw[row * D + d], wt, acc);
+                L = fmaf(cw[kHeadsPerCta * D + kHeadsPerCta + row], wt, L);
+            }
+        }
         if (p.chunks == 1) {
-            const float L = lrun[g];
-            p.out[(qh0 + g) * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
+            p.out[(qh0 + row) * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
         } else {
-            p.part_o[((qh0 + g) * p.chunks + chunk) * D + d] = acc;
+            p.part_o[((qh0 + row) * p.chunks + chunk) * D + d] = acc;
             if (d == 0) {
-                p.part_ml[((qh0 + g) * p.chunks + chunk) * 2] = mrun[g];
-                p.part_ml[((qh0 + g) * p.chunks + chunk) * 2 + 1] = lrun[g];
+                p.part_ml[((qh0 + row) * p.chunks + chunk) * 2] = M;
+                p.part_ml[((qh0 + row) * p.chunks + chunk) * 2 + 1] = L;
             }
         }
     }
@@ -352,23 +407,31 @@ __global__ void __launch_bounds__(D) gqa_decode_merge_kernel(const DecodeParams 
     p.out[qh * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
 }
 
-template <int D>
-constexpr int decode_smem_bytes() {
-    return DecodeSmem<D>::kBytes;
-}
-
-// Chunks per sequence: enough CTAs for two per SM, each chunk a whole number
-// of tiles.
-inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64_t max_len,
-                        std::uint32_t& chunks, std::uint32_t& chunk_len) {
-    const std::uint64_t tiles = (max_len + kTile - 1) / kTile;
-    std::uint64_t want = (2ull * 148 + batch * kv_heads - 1) / (batch * kv_heads);
-    if (want < 1) want = 1;
-    if (want > tiles) want = tiles;
-    if (tiles == 0) want = 1;
-    const std::uint64_t tiles_per = tiles == 0 ? 1 : (tiles + want - 1) / want;
-    chunk_len = static_cast<std::uint32_t>(tiles_per * kTile);
-    chunks = static_cast<std::uint32_t>(tiles == 0 ? 1 : (tiles + tiles_per - 1) / tiles_per);
+// Chunks per sequence.  The split kernel holds one CTA per SM (192 KB of
+// rings); a chunk is a whole number of tiles, dealt to the four warps.
+// Cost model: waves of CTAs x (tiles per warp + 2 tiles of fixed latency);
+// the fewest chunks that reach the minimum.
+inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64_t head_groups,
+                        std::uint64_t head_dim, std::uint64_t max_len, std::uint32_t& chunks,
+                        std::uint32_t& chunk_len) {
+    const std::uint64_t tp = 4096 / head_dim;  // positions per tile
+    const std::uint64_t tiles = (max_len + tp - 1) / tp;
+    chunks = 1;
+    chunk_len = static_cast<std::uint32_t>(tp * (tiles > 0 ? tiles : 1));
+    if (tiles == 0) return;
+    const std::uint64_t units = batch * kv_heads * head_groups;
+    std::uint64_t best = ~0ull;
+    for (std::uint64_t c = 1; c <= tiles && c <= 4096; ++c) {
+        const std::uint64_t tpc = (tiles + c - 1) / c;
+        if ((tiles + tpc - 1) / tpc != c) continue;  // same split as a smaller c
+        const std::uint64_t waves = (units * c + 147) / 148;
+        const std::uint64_t cost = waves * ((tpc + kWarpsPerCta - 1) / kWarpsPerCta + 2);
+        if (cost < best) {
+            best = cost;
+            chunks = static_cast<std::uint32_t>(c);
+            chunk_len = static_cast<std::uint32_t>(tpc * tp);
+        }
+    }
 }
 
 }  // namespace attn
@@ -415,8 +478,12 @@ extern "C" int mote_cuda_gqa_attention_decode_workspace_bytes(uint64_t batch, ui
     if (bytes == nullptr) return kInvalidValue;
     *bytes = 0;
     if (batch == 0 || q_heads == 0 || kv_heads == 0 || head_dim == 0) return kSuccess;
+    if (kv_heads > q_heads || q_heads % kv_heads != 0 || (head_dim != 64 && head_dim != 128))
+        return kSuccess;  // the attention call rejects these shapes
+    const std::uint64_t group = q_heads / kv_heads;
     std::uint32_t chunks = 1, chunk_len = 0;
-    attn::decode_plan(batch, kv_heads, max_len, chunks, chunk_len);
+    attn::decode_plan(batch, kv_heads, (group + attn::kHeadsPerCta - 1) / attn::kHeadsPerCta,
+                      head_dim, max_len, chunks, chunk_len);
     if (chunks > 1) *bytes = batch * q_heads * chunks * (head_dim + 2) * 4;
     return kSuccess;
 }
@@ -428,8 +495,8 @@ extern "C" int mote_cuda_gqa_attention_decode_workspace_bytes(uint64_t batch, ui
 // head_dim] f16, sequence b at rows b * seq_capacity + position; seq_lens
 // int32 [batch] on the device, each <= max_len <= seq_capacity (max_len
 // sizes the split over positions; a longer seq_len is clipped to max_len).
-// q_heads a multiple of kv_heads, head_dim 64 or 128, (q_heads / kv_heads)
-// * head_dim <= 512; 16-byte aligned pointers.  A sequence of length 0
+// q_heads a multiple of kv_heads, head_dim 64 or 128; 16-byte aligned
+// pointers.  A sequence of length 0
 // gets zeros.  workspace: mote_cuda_gqa_attention_decode_workspace_bytes.
 extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_cache,
                                                   const void* v_cache, const void* seq_lens,
@@ -445,8 +512,10 @@ extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_c
     if (batch == 0 || q_heads == 0) return kSuccess;
     if (kv_heads == 0 || q_heads % kv_heads != 0 || (head_dim != 64 && head_dim != 128))
         return kInvalidValue;
-    if ((q_heads / kv_heads) * head_dim > attn::kMaxGroupDim || max_len > seq_capacity ||
-        !std::isfinite(scale) || batch > 65535 || kv_heads > 65535)
+    const std::uint64_t head_groups =
+        (q_heads / kv_heads + attn::kHeadsPerCta - 1) / attn::kHeadsPerCta;
+    if (max_len > seq_capacity || !std::isfinite(scale) || batch > 65535 ||
+        kv_heads * head_groups > 65535 || q_heads > 0xffffffffull)
         return kInvalidValue;
     for (const void* ptr : {q, k_cache, v_cache, static_cast<const void*>(out)})
         if (reinterpret_cast<std::uintptr_t>(ptr) % 16 != 0) return kInvalidValue;
@@ -460,9 +529,10 @@ extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_c
     p.q_heads = static_cast<std::uint32_t>(q_heads);
     p.kv_heads = static_cast<std::uint32_t>(kv_heads);
     p.group = static_cast<std::uint32_t>(q_heads / kv_heads);
+    p.head_groups = static_cast<std::uint32_t>(head_groups);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.max_len = max_len;
-    attn::decode_plan(batch, kv_heads, max_len, p.chunks, p.chunk_len);
+    attn::decode_plan(batch, kv_heads, head_groups, head_dim, max_len, p.chunks, p.chunk_len);
     if (p.chunks > 1) {
         const std::uint64_t need = batch * q_heads * p.chunks * (head_dim + 2) * 4;
         if (workspace == nullptr || workspace_bytes < need ||
@@ -471,11 +541,12 @@ extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_c
         p.part_o = static_cast<float*>(workspace);
         p.part_ml = p.part_o + batch * q_heads * p.chunks * head_dim;
     }
-    const dim3 grid(p.chunks, static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
+    const dim3 grid(p.chunks, static_cast<unsigned>(kv_heads * head_groups),
+                    static_cast<unsigned>(batch));
     const auto s = static_cast<cudaStream_t>(stream);
     int st;
     if (head_dim == 64) {
-        constexpr int smem = attn::decode_smem_bytes<64>();
+        constexpr int smem = attn::kSplitSmem;
         static std::atomic<std::uint64_t> done{0};
         st = ensure_dynamic_smem(attn::gqa_decode_split_kernel<64>, smem, done);
         if (st == kSuccess)
@@ -485,7 +556,7 @@ extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_c
             st = launch_pdl(attn::gqa_decode_merge_kernel<64>,
                             dim3(static_cast<unsigned>(batch * q_heads)), dim3(64), s, p);
     } else {
-        constexpr int smem = attn::decode_smem_bytes<128>();
+        constexpr int smem = attn::kSplitSmem;
         static std::atomic<std::uint64_t> done{0};
         st = ensure_dynamic_smem(attn::gqa_decode_split_kernel<128>, smem, done);
         if (st == kSuccess)

@@ -127,9 +127,15 @@ def test_decode_batch_of_ragged_sequences(ctx):
     assert got.shape == (6, 32, 64)
 
 
-@pytest.mark.parametrize("qh,kvh,hd", [(8, 8, 64), (64, 8, 64), (16, 4, 128), (12, 2, 64)])
+@pytest.mark.parametrize("qh,kvh,hd", [(8, 8, 64), (64, 8, 64), (16, 4, 128), (12, 2, 64),
+                                       (32, 2, 64), (64, 2, 128), (48, 1, 64)])
 def test_decode_group_sizes(ctx, qh, kvh, hd):
     _decode_case(ctx, 2, qh, kvh, hd, [700, 1900], 2048, seed=qh * 10 + kvh)
+
+
+def test_decode_long_context(ctx):
+    """32768 cached positions: many chunks per sequence, each warp many tiles."""
+    _decode_case(ctx, 1, 32, 8, 64, [32768], 32768, seed=21)
 
 
 def test_decode_repeat_is_deterministic(ctx):

@@ -989,8 +989,8 @@ inline bool plan_gemv(std::uint64_t M, std::uint64_t K, bool xf32, bool peers, s
     if (K > (1ull << 24)) return false;
     x_stride = static_cast<std::uint32_t>(K * 2 + 32);
     // Preference: two CTAs per SM (16 warps to hide latency) with a deep
-    // ring, then one CTA per SM.
-    constexpr int kOptions[4][2] = {{2, 4}, {2, 3}, {1, 4}, {1, 2}};
+    // ring, then one CTA per SM with the deepest ring that fits.
+    constexpr int kOptions[5][2] = {{2, 4}, {2, 3}, {1, 4}, {1, 3}, {1, 2}};
     for (; m >= 1; m = m / 2) {
         x_rows = m * rows_per_token;
         x_bytes = ((x_rows + 1) * x_stride + 127u) & ~127u;  // + the zero row
@@ -1177,10 +1177,14 @@ int run_linear(const void* x, const void* w, const void* w2, void* y, std::uint6
     // CTA per SM, split K over 2 or 4 CTAs: each stages its part's columns
     // only, two CTAs fit per SM, and the parts meet in the workspace.
     if constexpr (!kFastOnly) {
-        // Measured on the decode sweep: worth it with two n8 tiles of tokens
-        // (more than 8 staged rows) and up to a few thousand tiles; with
-        // fewer rows or lm_head-sized N the unsplit kernel is as fast.
-        if (fast && workspace != nullptr && ctas == 1 && nt == 2 && p.tiles <= 4096) {
+        // Measured on the decode sweep (16 tokens, K = 4096): the split into
+        // four parts (two CTAs per SM) beats the unsplit three-stage ring at
+        // 896 tiles (17.5 vs 17.8 us) but loses at 688 and 256 tiles (16.4 vs
+        // 14.8 us, 8.8 vs 8.4 us: fewer tile rounds per warp group, and the
+        // partial sums' fences stall); with 8 or fewer tokens, or lm_head-sized
+        // N, the unsplit kernel is faster.
+        if (fast && workspace != nullptr && ctas == 1 && nt == 2 && p.tiles >= 850 &&
+            p.tiles <= 4096) {
             for (std::uint32_t parts = 2; parts <= 4; parts *= 2) {
                 if (p.units < parts) break;
                 const std::uint64_t kp = ((p.units + parts - 1) / parts) * 256ull;

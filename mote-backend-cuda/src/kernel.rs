@@ -45,6 +45,10 @@ const KERNELS: &[(&str, DType, &str, usize, Call)] = &[
     ("q4_0_decode", DType::F32, "mote_cuda_q4_0_decode_f32", 5, call_q4_0_decode_f32),
     ("q4_0_encode", DType::F32, "mote_cuda_q4_0_encode_f32", 5, call_q4_0_encode_f32),
     ("rope_cos_sin", DType::F32, "mote_cuda_rope_cos_sin_f32", 7, call_rope_cos_sin_f32),
+    ("kv_cache_append", DType::F16, "mote_cuda_kv_cache_append_f16", 11, call_kv_cache_append_f16),
+    ("gqa_attention_decode", DType::F16, "mote_cuda_gqa_attention_decode_f16", 15, call_gqa_attention_decode_f16),
+    ("gqa_attention_prefill", DType::F16, "mote_cuda_gqa_attention_prefill_f16", 13, call_gqa_attention_prefill_f16),
+    ("decoder_stack_q4_0", DType::F16, "mote_cuda_q4_0_decoder_stack_f16", 12, call_q4_0_decoder_stack_f16),
 ];
 
 struct CudaKernel {
@@ -195,4 +199,20 @@ fn call_q4_0_encode_f32(w: &[usize]) -> i32 {
 fn call_rope_cos_sin_f32(w: &[usize]) -> i32 {
     // SAFETY: the caller's words follow the entry point's argument list.
     unsafe { ffi::mote_cuda_rope_cos_sin_f32(w[0] as *const c_void, w[1] as *mut c_void, w[2] as *mut c_void, w[3] as u64, w[4] as u64, f64::from_bits(w[5] as u64), w[6] as *mut c_void) }
+}
+fn call_kv_cache_append_f16(w: &[usize]) -> i32 {
+    // SAFETY: the caller's words follow the entry point's argument list.
+    unsafe { ffi::mote_cuda_kv_cache_append_f16(w[0] as *const c_void, w[1] as *const c_void, w[2] as *mut c_void, w[3] as *mut c_void, w[4] as *const c_void, w[5] as u64, w[6] as u64, w[7] as u64, w[8] as u64, w[9] as *mut c_void, w[10] as *mut c_void) }
+}
+fn call_gqa_attention_decode_f16(w: &[usize]) -> i32 {
+    // SAFETY: the caller's words follow the entry point's argument list.
+    unsafe { ffi::mote_cuda_gqa_attention_decode_f16(w[0] as *const c_void, w[1] as *const c_void, w[2] as *const c_void, w[3] as *const c_void, w[4] as *mut c_void, w[5] as u64, w[6] as u64, w[7] as u64, w[8] as u64, w[9] as u64, w[10] as u64, f32::from_bits(w[11] as u32), w[12] as *mut c_void, w[13] as u64, w[14] as *mut c_void) }
+}
+fn call_gqa_attention_prefill_f16(w: &[usize]) -> i32 {
+    // SAFETY: the caller's words follow the entry point's argument list.
+    unsafe { ffi::mote_cuda_gqa_attention_prefill_f16(w[0] as *const c_void, w[1] as *const c_void, w[2] as *const c_void, w[3] as *mut c_void, w[4] as u64, w[5] as u64, w[6] as u64, w[7] as u64, w[8] as u64, w[9] as u64, w[10] as u64, f32::from_bits(w[11] as u32), w[12] as *mut c_void) }
+}
+fn call_q4_0_decoder_stack_f16(w: &[usize]) -> i32 {
+    // SAFETY: the caller's words follow the entry point's argument list.
+    unsafe { ffi::mote_cuda_q4_0_decoder_stack_f16(w[0] as *const c_void, w[1] as u32, w[2] as *const c_void, w[3] as u64, w[4] as u64, w[5] as u64, w[6] as u64, w[7] as u64, f32::from_bits(w[8] as u32), w[9] as *mut c_void, w[10] as u64, w[11] as *mut c_void) }
 }

@@ -122,6 +122,10 @@ _ARG_KINDS = {
     "mote_cuda_q4_0_decode_f32": "ppuup",
     "mote_cuda_q4_0_encode_f32": "ppuup",
     "mote_cuda_rope_cos_sin_f32": "pppuudp",
+    "mote_cuda_kv_cache_append_f16": "pppppuuuupp",
+    "mote_cuda_gqa_attention_decode_f16": "pppppuuuuuufpup",
+    "mote_cuda_gqa_attention_prefill_f16": "ppppuuuuuuufp",
+    "mote_cuda_q4_0_decoder_stack_f16": "pwpuuuuufpup",
 }
 
 # (op, dtype) -> entry point
@@ -150,6 +154,10 @@ CUDA_KERNELS = {
     ("q4_0_decode", DType.F32): "mote_cuda_q4_0_decode_f32",
     ("q4_0_encode", DType.F32): "mote_cuda_q4_0_encode_f32",
     ("rope_cos_sin", DType.F32): "mote_cuda_rope_cos_sin_f32",
+    ("kv_cache_append", DType.F16): "mote_cuda_kv_cache_append_f16",
+    ("gqa_attention_decode", DType.F16): "mote_cuda_gqa_attention_decode_f16",
+    ("gqa_attention_prefill", DType.F16): "mote_cuda_gqa_attention_prefill_f16",
+    ("decoder_stack_q4_0", DType.F16): "mote_cuda_q4_0_decoder_stack_f16",
 }
 
 

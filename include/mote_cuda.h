@@ -423,8 +423,8 @@ int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_cache, const
  *   out[t, h] = softmax_{p <= start + t}(scale * q[t, h] . K[p, h / g]) . V[p, h / g],
  * q / out [tokens, q_heads, head_dim] f16, K/V from cache rows row0 + p for
  * p < start + tokens (this chunk's K/V already appended; row0 + start +
- * tokens <= cache_rows).  head_dim 64, q_heads % kv_heads == 0, 16-byte
- * aligned tensors; tokens == 0 returns 0; other shapes -> 1. */
+ * tokens <= cache_rows).  head_dim 64, q_heads % kv_heads == 0, scale > 0,
+ * 16-byte aligned tensors; tokens == 0 returns 0; other shapes -> 1. */
 int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_cache, const void* v_cache,
                                         void* out, uint64_t tokens, uint64_t start,
                                         uint64_t q_heads, uint64_t kv_heads, uint64_t head_dim,

@@ -8,21 +8,25 @@
 // ([cache rows, kv_heads, 64] f16, this chunk's K/V already appended).
 //
 // One CTA computes 128 query rows of one query head (flash attention):
-// * warp 4 loads the Q tile once and the K and V tiles of 128 positions
-//   (TMA, 128-byte swizzle, two stages; tensor maps end at the last
+// * warp 8 loads the Q tile once and the K and V tiles of 128 positions
+//   (TMA, 128-byte swizzle, four stages; tensor maps end at the last
 //   attended row, so rows past it arrive as zeros);
-// * warp 5 allocates tensor memory and one thread issues the MMAs:
+// * warp 9 allocates tensor memory and one thread issues the MMAs:
 //   S = Q K^T (tcgen05.mma kind::f16, M = 128 queries, N = 128 positions,
 //   A and B K-major in shared memory) into one of two S buffers in TMEM, so
 //   S for the next tile is computed while the softmax works on this one;
 //   then O += P V (M = 128, N = 64, A = P read from tensor memory, B = V
 //   MN-major in shared memory) into the O accumulator in TMEM;
-// * warps 0-3 run the softmax, one thread per query row (= TMEM lane):
-//   each reads its S row (tcgen05.ld), masks positions past its own,
-//   keeps the running max and sum (exp2 with the scale folded in), writes
-//   P as f16 over the first half of its S buffer (tcgen05.st) and rescales
-//   its O row when the max grew, then releases the P.V MMA.  At the end it
-//   reads O, divides by the sum and stores the row.
+// * warps 0-7 run the softmax, two threads per query row (= TMEM lane):
+//   warps w and w + 4 share the lanes of w % 4 and take 64 of a tile's 128
+//   columns each.  A thread reads its S columns (tcgen05.ld), masks
+//   positions past its row's, exchanges its maximum with its partner
+//   through shared memory (a 64-thread named barrier per pair), keeps the
+//   running max and its share of the sum (exp2 with the scale folded in),
+//   writes its P as f16 over the first half of the S buffer (tcgen05.st),
+//   rescales its half of the O row when the max grew, then releases the
+//   P.V MMA.  At the end the pair adds its sums and each thread stores its
+//   half of O / sum.
 // Every wait is bounded; an expired wait aborts the CTA, which waits for its
 // issued MMAs (bounded) and frees its tensor memory.  No load uses cluster
 // multicast.
@@ -37,11 +41,14 @@ namespace attnp {
 constexpr int kBM = 128;      // query rows per CTA (TMEM lanes)
 constexpr int kBN = 128;      // positions per K/V tile
 constexpr int kD = 64;        // head_dim (one 128-byte swizzle row)
-constexpr int kStages = 2;    // K/V tile stages
-constexpr int kSoftmaxWarps = 4;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
+constexpr int kKV = 4;        // K/V tile stages (TMA ring)
+constexpr int kSBuf = 2;      // S buffers in tensor memory
+// Softmax: warps w and w + 4 share the TMEM lanes 32 (w % 4) .. + 31 (one
+// query row per lane) and take columns [0, 64) and [64, 128) of a tile.
+constexpr int kSoftmaxWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
 constexpr int kTileBytes = kBN * kD * 2;  // 16 KB (also the Q tile)
 
 // TMEM columns: S0 [0, 128), S1 [128, 256), O [256, 320); P_j (f16, two per
@@ -51,14 +58,18 @@ constexpr std::uint32_t kTmemCols = 512;
 
 struct Smem {
     static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kTileBytes;                // [kStages] tiles
-    static constexpr int kV = kK + kStages * kTileBytes;      // [kStages] tiles
-    static constexpr int kBar = kV + kStages * kTileBytes;
-    // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_ready[2], o_done, drained
-    static constexpr int kNumBars = 1 + 5 * kStages + 2;
+    static constexpr int kK = kQ + kTileBytes;                // [kKV] tiles
+    static constexpr int kV = kK + kKV * kTileBytes;          // [kKV] tiles
+    static constexpr int kBar = kV + kKV * kTileBytes;
+    // q_full, k_full[kKV], v_full[kKV], kv_empty[kKV], s_full[kSBuf], p_ready[kSBuf], o_done, drained
+    static constexpr int kNumBars = 1 + 3 * kKV + 2 * kSBuf + 2;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kAbort = kTmemSlot + 4;
-    static constexpr int kUsed = kAbort + 4 + 1024;  // + 1024-byte alignment slack
+    // row maxima of the two column halves, double-buffered by tile:
+    // [2][2 halves][kBM] f32, then the halves' row sums [2][kBM]
+    static constexpr int kXchg = (kAbort + 4 + 15) / 16 * 16;
+    static constexpr int kSums = kXchg + 2 * 2 * kBM * 4;
+    static constexpr int kUsed = kSums + 2 * kBM * 4 + 1024;  // + 1024-byte alignment slack
     // at least 120 KB: one CTA per SM, so a CTA's 512 TMEM columns never
     // wait for another CTA of this kernel on the same SM
     static constexpr int kBytes = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
@@ -137,6 +148,10 @@ __device__ __forceinline__ void tmem_st32(std::uint32_t taddr, const std::uint32
         : "memory");
 }
 
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -156,11 +171,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + Smem::kBar);
     std::uint64_t* q_full = bars;
     std::uint64_t* k_full = bars + 1;
-    std::uint64_t* v_full = k_full + kStages;
-    std::uint64_t* kv_empty = v_full + kStages;
-    std::uint64_t* s_full = kv_empty + kStages;
-    std::uint64_t* p_ready = s_full + kStages;
-    std::uint64_t* o_done = p_ready + kStages;
+    std::uint64_t* v_full = k_full + kKV;
+    std::uint64_t* kv_empty = v_full + kKV;
+    std::uint64_t* s_full = kv_empty + kKV;
+    std::uint64_t* p_ready = s_full + kSBuf;
+    std::uint64_t* o_done = p_ready + kSBuf;
     std::uint64_t* drained = o_done + 1;
     volatile std::uint32_t* tmem_slot = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kTmemSlot);
     volatile std::uint32_t* abort_flag = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kAbort);
@@ -178,10 +193,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kKV; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
             mbar_init(&kv_empty[s], 1);
+        }
+        for (int s = 0; s < kSBuf; ++s) {
             mbar_init(&s_full[s], 1);
             mbar_init(&p_ready[s], kSoftmaxWarps);
         }
@@ -203,9 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(base + Smem::kQ, &map_q, 0, static_cast<int>(h), static_cast<int>(q0),
                         smem_u32(q_full));
             for (std::uint32_t j = 0; j < nkt; ++j) {
-                const int s = j % kStages;
-                if (j >= kStages &&
-                    !wait_or_abort(&kv_empty[s], ((j / kStages) - 1) & 1u, abort_flag))
+                const int s = j % kKV;
+                if (j >= kKV &&
+                    !wait_or_abort(&kv_empty[s], ((j / kKV) - 1) & 1u, abort_flag))
                     break;
                 mbar_arrive_expect_tx(&k_full[s], kTileBytes);
                 tma_load_3d(base + Smem::kK + s * kTileBytes, &map_k, 0, static_cast<int>(kvh),
@@ -219,34 +236,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             auto issue_s = [&](std::uint32_t j) -> bool {
-                const int s = j % kStages;
-                if (!wait_or_abort(&k_full[s], (j / kStages) & 1u, abort_flag)) return false;
+                const int kv = j % kKV, sb = j % kSBuf;
+                if (!wait_or_abort(&k_full[kv], (j / kKV) & 1u, abort_flag)) return false;
                 gemm::tc_fence_after();
-                const std::uint32_t kaddr = base + Smem::kK + s * kTileBytes;
+                const std::uint32_t kaddr = base + Smem::kK + kv * kTileBytes;
 #pragma unroll
                 for (int k = 0; k < kD / 16; ++k)
-                    umma_f16_ss(tmem + s * kBN, smem_desc_sw128(base + Smem::kQ + k * 32),
+                    umma_f16_ss(tmem + sb * kBN, smem_desc_sw128(base + Smem::kQ + k * 32),
                                 smem_desc_sw128(kaddr + k * 32), kIdescS, k != 0 ? 1u : 0u);
-                gemm::umma_commit(smem_u32(&s_full[s]));
+                gemm::umma_commit(smem_u32(&s_full[sb]));
                 return true;
             };
             bool ok = wait_or_abort(q_full, 0, abort_flag) && issue_s(0);
             for (std::uint32_t j = 0; ok && j < nkt; ++j) {
-                const int s = j % kStages;
+                const int kv = j % kKV, sb = j % kSBuf;
                 if (j + 1 < nkt && !issue_s(j + 1)) break;
-                if (!wait_or_abort(&p_ready[s], (j / kStages) & 1u, abort_flag)) break;
-                if (!wait_or_abort(&v_full[s], (j / kStages) & 1u, abort_flag)) break;
+                if (!wait_or_abort(&p_ready[sb], (j / kSBuf) & 1u, abort_flag)) break;
+                if (!wait_or_abort(&v_full[kv], (j / kKV) & 1u, abort_flag)) break;
                 gemm::tc_fence_after();
-                const std::uint32_t vaddr = base + Smem::kV + s * kTileBytes;
+                const std::uint32_t vaddr = base + Smem::kV + kv * kTileBytes;
 #pragma unroll
                 for (int k = 0; k < kBN / 16; ++k)
                     // A = P (16 positions = 8 columns per step), B = V rows
                     // of 16 positions (2048 bytes per step, MN-major)
-                    gemm::umma_f16_ta(tmem + kColO, tmem + s * kBN + k * 8,
+                    gemm::umma_f16_ta(tmem + kColO, tmem + sb * kBN + k * 8,
                                       smem_desc_sw128(vaddr + k * 2048), kIdescPV,
                                       (j | k) != 0 ? 1u : 0u);
                 gemm::umma_commit(smem_u32(o_done));
-                gemm::umma_commit(smem_u32(&kv_empty[s]));
+                gemm::umma_commit(smem_u32(&kv_empty[kv]));
             }
             // every issued MMA completes before the tensor memory is freed
             gemm::umma_commit(smem_u32(drained));
@@ -254,72 +271,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // softmax: thread = query row r = TMEM lane
-        const int r = 32 * warp + lane;
-        const std::uint32_t lane_off = static_cast<std::uint32_t>(32 * warp) << 16;
+        // softmax: query row r = TMEM lane; this thread takes the row's
+        // columns [64 half, 64 half + 64) of every S tile
+        const int quarter = warp % 4, half = warp / 4;
+        const int r = 32 * quarter + lane;
+        const std::uint32_t lane_off = static_cast<std::uint32_t>(32 * quarter) << 16;
+        const std::uint32_t col0 = 64u * static_cast<std::uint32_t>(half);
         const std::int64_t qpos = static_cast<std::int64_t>(p.start) + q0 + r;
+        float* xchg = reinterpret_cast<float*>(smem + Smem::kXchg);  // [2][2][kBM]
+        float* sums = reinterpret_cast<float*>(smem + Smem::kSums);  // [2][kBM]
+        const int pair_bar = 1 + quarter;  // named barrier of warps quarter, quarter + 4
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (std::uint32_t j = 0; j < nkt && ok; ++j) {
-            const int s = j % kStages;
-            ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[s], (j / kStages) & 1u, abort_flag));
-            if (!ok) break;
-            gemm::tc_fence_after();
-            std::uint32_t v[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32_nowait(tmem + lane_off + s * kBN + 32 * c, v[c]);
-            tmem_wait_ld();
-            // scale (log2 units) and causal mask: position j*128 + col
-            const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN;
-            const bool masked_tile = kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + q0;
+        // Both warps of a pair pass the same pair barriers on every path (a
+        // failed wait skips the work, never the barrier), so an aborted
+        // launch cannot leave one of them waiting at a barrier.
+        for (std::uint32_t j = 0; j < nkt; ++j) {
+            const int s = j % kSBuf;
+            if (ok)
+                ok = __all_sync(0xffffffffu,
+                                wait_or_abort(&s_full[s], (j / kSBuf) & 1u, abort_flag));
+            std::uint32_t v[2][32];
             float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float x = __uint_as_float(v[c][i]) * p.scale_log2;
-                    if (masked_tile && kbase + 32 * c + i > qpos) x = -INFINITY;
-                    v[c][i] = __float_as_uint(x);
-                    mx = fmaxf(mx, x);
-                }
-            const float mnew = fmaxf(m, mx);  // finite: position 0 <= qpos is in tile 0
-            const float alpha = ex2f(m - mnew);  // 0 on the first tile (m = -inf)
-            float sum = 0.f;
-            std::uint32_t pk[2][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float a = ex2f(__uint_as_float(v[c][i]) - mnew);
-                    const float b = ex2f(__uint_as_float(v[c][i + 1]) - mnew);
-                    sum += a + b;
-                    std::uint32_t h2;
-                    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
-                    pk[c / 2][(c % 2) * 16 + i / 2] = h2;
-                }
-            l = fmaf(l, alpha, sum);
-            m = mnew;
-            // P over the first 64 columns of this S buffer
-            tmem_st32(tmem + lane_off + s * kBN, pk[0]);
-            tmem_st32(tmem + lane_off + s * kBN + 32, pk[1]);
-            tmem_wait_st();
-            // rescale O once the previous tile's P.V is complete
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (j - 1) & 1u, abort_flag));
-                if (!ok) break;
+            if (ok) {
                 gemm::tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                    std::uint32_t o[2][32];
-                    tmem_ld32_nowait(tmem + lane_off + kColO, o[0]);
-                    tmem_ld32_nowait(tmem + lane_off + kColO + 32, o[1]);
-                    tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+                    tmem_ld32_nowait(tmem + lane_off + s * kBN + col0 + 32 * c, v[c]);
+                tmem_wait_ld();
+                // causal mask: position j*128 + col0 + col; masked scores
+                // become -inf (the scale is positive, so the maximum of the
+                // raw scores gives the maximum of the scaled ones)
+                const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN + col0;
+                const bool masked_tile = kbase + 63 > static_cast<std::int64_t>(p.start) + q0;
+                if (masked_tile) {
 #pragma unroll
                     for (int c = 0; c < 2; ++c)
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
-                            o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
-                    tmem_st32(tmem + lane_off + kColO, o[0]);
-                    tmem_st32(tmem + lane_off + kColO + 32, o[1]);
+                            if (kbase + 32 * c + i > qpos) v[c][i] = __float_as_uint(-INFINITY);
+                }
+                // eight independent maximum chains, then a tree
+                float e[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) e[i] = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) e[i % 8] = fmaxf(e[i % 8], __uint_as_float(v[c][i]));
+                mx = fmaxf(fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])),
+                           fmaxf(fmaxf(e[4], e[5]), fmaxf(e[6], e[7])));
+            }
+            // the row maximum over both halves: after this barrier the
+            // partner has also read its S columns, which this thread's P
+            // stores may overwrite
+            float* xb = xchg + (j & 1u) * 2 * kBM;
+            xb[half * kBM + r] = mx;
+            named_bar_sync(pair_bar, 64);
+            if (!ok) continue;
+            mx = fmaxf(mx, xb[(half ^ 1) * kBM + r]);
+            // running maximum m in raw score units; probabilities
+            // 2^(scale_log2 * (s - m)) with the scale folded into one FMA
+            const float mnew = fmaxf(m, mx);  // finite: position 0 <= qpos is in tile 0
+            const float sc = p.scale_log2;
+            const float alpha = ex2f((m - mnew) * sc);  // 0 on the first tile (m = -inf)
+            const float neg_m = -mnew * sc;
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+            std::uint32_t pk[32];
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float a = ex2f(fmaf(__uint_as_float(v[c][i]), sc, neg_m));
+                    const float b = ex2f(fmaf(__uint_as_float(v[c][i + 1]), sc, neg_m));
+                    sum4[(i / 2) % 4] += a + b;
+                    std::uint32_t h2;
+                    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
+                    pk[c * 16 + i / 2] = h2;
+                }
+            l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            m = mnew;
+            // P (positions col0 .. col0 + 63) over columns [32 half, 32 half + 32)
+            tmem_st32(tmem + lane_off + s * kBN + 32u * static_cast<std::uint32_t>(half), pk);
+            tmem_wait_st();
+            // rescale this thread's half of the O row once the previous
+            // tile's P.V is complete
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (j - 1) & 1u, abort_flag));
+                if (!ok) continue;
+                gemm::tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    std::uint32_t o[32];
+                    const std::uint32_t oa = tmem + lane_off + kColO + 32u * static_cast<std::uint32_t>(half);
+                    tmem_ld32_nowait(oa, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(oa, o);
                     tmem_wait_st();
                 }
             }
@@ -329,31 +377,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_ready[s]))
                              : "memory");
         }
-        // output: O / l for the rows of this tile
+        // output: this thread's half of O / (sum of both halves' sums)
+        sums[half * kBM + r] = l;
+        named_bar_sync(pair_bar, 64);
+        const float lrow = l + sums[(half ^ 1) * kBM + r];
         if (ok && __all_sync(0xffffffffu, wait_or_abort(o_done, (nkt - 1) & 1u, abort_flag))) {
             gemm::tc_fence_after();
-            std::uint32_t o[2][32];
-            tmem_ld32_nowait(tmem + lane_off + kColO, o[0]);
-            tmem_ld32_nowait(tmem + lane_off + kColO + 32, o[1]);
+            std::uint32_t o[32];
+            tmem_ld32_nowait(tmem + lane_off + kColO + 32u * static_cast<std::uint32_t>(half), o);
             tmem_wait_ld();
             if (q0 + r < p.tokens) {
-                const float inv = l > 0.f ? 1.f / l : 0.f;
+                const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
                 uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<std::uint64_t>(q0) + r) *
                                                                    p.out_row_stride +
-                                                      static_cast<std::uint64_t>(h) * kD);
+                                                      static_cast<std::uint64_t>(h) * kD + 32 * half);
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
+                for (int i = 0; i < 32; i += 8) {
+                    std::uint32_t w[4];
 #pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        std::uint32_t w[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float a = __uint_as_float(o[c][i + 2 * e]) * inv;
-                            const float b = __uint_as_float(o[c][i + 2 * e + 1]) * inv;
-                            asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w[e]) : "f"(b), "f"(a));
-                        }
-                        dst[(32 * c + i) / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int e = 0; e < 4; ++e) {
+                        const float a = __uint_as_float(o[i + 2 * e]) * inv;
+                        const float b = __uint_as_float(o[i + 2 * e + 1]) * inv;
+                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w[e]) : "f"(b), "f"(a));
                     }
+                    dst[i / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
             }
         }
     }
@@ -385,8 +433,8 @@ inline int make_map(CUtensorMap* map, const void* ptr, std::uint64_t rows, std::
 
 // Causal prefill attention of `tokens` queries at positions start .. start +
 // tokens - 1 over cache rows row0 .. row0 + start + tokens - 1 (see the
-// header for the layout).  head_dim 64; q_heads % kv_heads == 0; 16-byte
-// aligned tensors; tokens == 0 returns 0.
+// header for the layout).  head_dim 64; q_heads % kv_heads == 0; scale > 0;
+// 16-byte aligned tensors; tokens == 0 returns 0.
 extern "C" int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_cache,
                                                    const void* v_cache, void* out,
                                                    uint64_t tokens, uint64_t start,
@@ -401,7 +449,7 @@ extern "C" int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_
         return kInvalidValue;
     if (tokens == 0 || q_heads == 0) return kSuccess;
     if (head_dim != kD || kv_heads == 0 || q_heads % kv_heads != 0 || q_heads > 65535 ||
-        !std::isfinite(scale))
+        !std::isfinite(scale) || !(scale > 0.f))
         return kInvalidValue;
     if (tokens > 0x7fffffffull || start > 0x7fffffffull || row0 + start + tokens > cache_rows ||
         start + tokens > 0x7fffffffull)

@@ -24,7 +24,8 @@
 //   through shared memory (a 64-thread named barrier per pair), keeps the
 //   running max and its share of the sum (exp2 with the scale folded in),
 //   writes its P as f16 over the first half of the S buffer (tcgen05.st),
-//   rescales its half of the O row when the max grew, then releases the
+//   rescales its half of the O row when the max grew by more than 8 (log2
+//   units; probabilities stay below 2^8), then releases the
 //   P.V MMA.  At the end the pair adds its sums and each thread stores its
 //   half of O / sum.
 // Every wait is bounded; an expired wait aborts the CTA, which waits for its
@@ -330,12 +331,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(pair_bar, 64);
             if (!ok) continue;
             mx = fmaxf(mx, xb[(half ^ 1) * kBM + r]);
-            // running maximum m in raw score units; probabilities
-            // 2^(scale_log2 * (s - m)) with the scale folded into one FMA
+            // Reference maximum m in raw score units; probabilities
+            // 2^(scale_log2 * (s - m)) with the scale folded into one FMA.
+            // m moves (and O and the sum are rescaled) only when the row
+            // maximum exceeds it by more than 8 in log2 units, so a
+            // probability stays below 2^8 (exact in f16 as any other) and
+            // most tiles need no rescale -- and no wait for the previous
+            // tile's P.V.  Both threads of a row take the same decision.
             const float mnew = fmaxf(m, mx);  // finite: position 0 <= qpos is in tile 0
             const float sc = p.scale_log2;
-            const float alpha = ex2f((m - mnew) * sc);  // 0 on the first tile (m = -inf)
-            const float neg_m = -mnew * sc;
+            const bool grow = (mnew - m) * sc > 8.f;  // always on the first tile (m = -inf)
+            float alpha = 1.f;
+            if (grow) {
+                alpha = ex2f((m - mnew) * sc);  // 0 on the first tile
+                m = mnew;
+            }
+            const float neg_m = -m * sc;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
             std::uint32_t pk[32];
 #pragma unroll
@@ -350,17 +361,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[c * 16 + i / 2] = h2;
                 }
             l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            m = mnew;
             // P (positions col0 .. col0 + 63) over columns [32 half, 32 half + 32)
             tmem_st32(tmem + lane_off + s * kBN + 32u * static_cast<std::uint32_t>(half), pk);
             tmem_wait_st();
             // rescale this thread's half of the O row once the previous
             // tile's P.V is complete
-            if (j > 0) {
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
                 ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (j - 1) & 1u, abort_flag));
                 if (!ok) continue;
                 gemm::tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                {
                     std::uint32_t o[32];
                     const std::uint32_t oa = tmem + lane_off + kColO + 32u * static_cast<std::uint32_t>(half);
                     tmem_ld32_nowait(oa, o);

@@ -17,17 +17,17 @@
 //   S for the next tile is computed while the softmax works on this one;
 //   then O += P V (M = 128, N = 64, A = P read from tensor memory, B = V
 //   MN-major in shared memory) into the O accumulator in TMEM;
-// * warps 0-7 run the softmax, two threads per query row (= TMEM lane):
-//   warps w and w + 4 share the lanes of w % 4 and take 64 of a tile's 128
-//   columns each.  A thread reads its S columns (tcgen05.ld), masks
-//   positions past its row's, exchanges its maximum with its partner
-//   through shared memory (a 64-thread named barrier per pair), keeps the
-//   running max and its share of the sum (exp2 with the scale folded in),
-//   writes its P as f16 over the first half of the S buffer (tcgen05.st),
-//   rescales its half of the O row when the max grew by more than 8 (log2
-//   units; probabilities stay below 2^8), then releases the
-//   P.V MMA.  At the end the pair adds its sums and each thread stores its
-//   half of O / sum.
+// * warps 0-7 run the softmax in two groups of four: group g takes the
+//   tiles j with j % 2 == g (S buffer g) and keeps, per query row (= TMEM
+//   lane, one thread), its own reference maximum, sum and O accumulator
+//   O_g, so the groups never wait for each other and one group's softmax
+//   overlaps the other's hand-offs.  A thread reads its S row (tcgen05.ld),
+//   masks positions past its row's, keeps the maximum and sum (exp2 with
+//   the scale folded in), writes P as f16 over the first half of the S
+//   buffer (tcgen05.st), rescales O_g only when the maximum grew by more
+//   than 8 (log2 units; probabilities stay below 2^8), then releases the
+//   P.V MMA into O_g.  At the end the groups exchange maxima and sums and
+//   each thread writes half of its row: (O_0 w_0 + O_1 w_1) / sum.
 // Every wait is bounded; an expired wait aborts the CTA, which waits for its
 // issued MMAs (bounded) and frees its tensor memory.  No load uses cluster
 // multicast.
@@ -44,17 +44,16 @@ constexpr int kBN = 128;      // positions per K/V tile
 constexpr int kD = 64;        // head_dim (one 128-byte swizzle row)
 constexpr int kKV = 4;        // K/V tile stages (TMA ring)
 constexpr int kSBuf = 2;      // S buffers in tensor memory
-// Softmax: warps w and w + 4 share the TMEM lanes 32 (w % 4) .. + 31 (one
-// query row per lane) and take columns [0, 64) and [64, 128) of a tile.
+// Softmax: two groups of four warps (tiles of even and odd index).
 constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 10 * 32;
 constexpr int kTileBytes = kBN * kD * 2;  // 16 KB (also the Q tile)
 
-// TMEM columns: S0 [0, 128), S1 [128, 256), O [256, 320); P_j (f16, two per
-// column) over the first 64 columns of S_{j % 2}.
-constexpr std::uint32_t kColO = 256;
+// TMEM columns: S0 [0, 128), S1 [128, 256), O_0 [256, 320), O_1 [320, 384);
+// P_j (f16, two per column) over the first 64 columns of S_{j % 2}.
+constexpr std::uint32_t kColO = 256;  // O_g at kColO + 64 g (g = tile parity)
 constexpr std::uint32_t kTmemCols = 512;
 
 struct Smem {
@@ -62,12 +61,11 @@ struct Smem {
     static constexpr int kK = kQ + kTileBytes;                // [kKV] tiles
     static constexpr int kV = kK + kKV * kTileBytes;          // [kKV] tiles
     static constexpr int kBar = kV + kKV * kTileBytes;
-    // q_full, k_full[kKV], v_full[kKV], kv_empty[kKV], s_full[kSBuf], p_ready[kSBuf], o_done, drained
-    static constexpr int kNumBars = 1 + 3 * kKV + 2 * kSBuf + 2;
+    // q_full, k_full[kKV], v_full[kKV], kv_empty[kKV], s_full[2], p_ready[2], o_done[2], drained
+    static constexpr int kNumBars = 1 + 3 * kKV + 3 * kSBuf + 1;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kAbort = kTmemSlot + 4;
-    // row maxima of the two column halves, double-buffered by tile:
-    // [2][2 halves][kBM] f32, then the halves' row sums [2][kBM]
+    // the softmax groups' row maxima [2][kBM] and row sums [2][kBM] (f32)
     static constexpr int kXchg = (kAbort + 4 + 15) / 16 * 16;
     static constexpr int kSums = kXchg + 2 * 2 * kBM * 4;
     static constexpr int kUsed = kSums + 2 * kBM * 4 + 1024;  // + 1024-byte alignment slack
@@ -177,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     std::uint64_t* s_full = kv_empty + kKV;
     std::uint64_t* p_ready = s_full + kSBuf;
     std::uint64_t* o_done = p_ready + kSBuf;
-    std::uint64_t* drained = o_done + 1;
+    std::uint64_t* drained = o_done + kSBuf;
     volatile std::uint32_t* tmem_slot = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kTmemSlot);
     volatile std::uint32_t* abort_flag = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kAbort);
 
@@ -201,9 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int s = 0; s < kSBuf; ++s) {
             mbar_init(&s_full[s], 1);
-            mbar_init(&p_ready[s], kSoftmaxWarps);
+            mbar_init(&p_ready[s], kSoftmaxWarps / 2);  // the tile parity's group
+            mbar_init(&o_done[s], 1);
         }
-        mbar_init(o_done, 1);
         mbar_init(drained, 1);
         *abort_flag = 0u;
         fence_mbarrier_init();
@@ -213,6 +211,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     gemm::tc_fence_after();
     const std::uint32_t tmem = *tmem_slot;
+    // the tensor-map descriptors are kernel parameters (not written by the
+    // previous kernel): fetch them while it may still be running
+    if (warp == kProducerWarp && lane == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<std::uint64_t>(&map_q))
+                     : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<std::uint64_t>(&map_k))
+                     : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<std::uint64_t>(&map_v))
+                     : "memory");
+    }
     pdl_wait();
 
     if (warp == kProducerWarp) {
@@ -260,10 +268,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < kBN / 16; ++k)
                     // A = P (16 positions = 8 columns per step), B = V rows
                     // of 16 positions (2048 bytes per step, MN-major)
-                    gemm::umma_f16_ta(tmem + kColO, tmem + sb * kBN + k * 8,
+                    gemm::umma_f16_ta(tmem + kColO + 64u * static_cast<std::uint32_t>(sb),
+                                      tmem + sb * kBN + k * 8,
                                       smem_desc_sw128(vaddr + k * 2048), kIdescPV,
-                                      (j | k) != 0 ? 1u : 0u);
-                gemm::umma_commit(smem_u32(o_done));
+                                      (j >= static_cast<std::uint32_t>(kSBuf) || k != 0) ? 1u : 0u);
+                gemm::umma_commit(smem_u32(&o_done[sb]));
                 gemm::umma_commit(smem_u32(&kv_empty[kv]));
             }
             // every issued MMA completes before the tensor memory is freed
@@ -272,85 +281,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // softmax: query row r = TMEM lane; this thread takes the row's
-        // columns [64 half, 64 half + 64) of every S tile
-        const int quarter = warp % 4, half = warp / 4;
+        // softmax: group g = warp / 4 takes the tiles j with j % 2 == g, one
+        // thread per query row r = TMEM lane, with its own reference maximum,
+        // sum and O accumulator O_g; the groups meet once at the end
+        const int quarter = warp % 4, grp = warp / 4;
         const int r = 32 * quarter + lane;
         const std::uint32_t lane_off = static_cast<std::uint32_t>(32 * quarter) << 16;
-        const std::uint32_t col0 = 64u * static_cast<std::uint32_t>(half);
+        const std::uint32_t o_col = kColO + 64u * static_cast<std::uint32_t>(grp);
         const std::int64_t qpos = static_cast<std::int64_t>(p.start) + q0 + r;
-        float* xchg = reinterpret_cast<float*>(smem + Smem::kXchg);  // [2][2][kBM]
-        float* sums = reinterpret_cast<float*>(smem + Smem::kSums);  // [2][kBM]
-        const int pair_bar = 1 + quarter;  // named barrier of warps quarter, quarter + 4
+        const float sc = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        // Both warps of a pair pass the same pair barriers on every path (a
-        // failed wait skips the work, never the barrier), so an aborted
-        // launch cannot leave one of them waiting at a barrier.
-        for (std::uint32_t j = 0; j < nkt; ++j) {
-            const int s = j % kSBuf;
-            if (ok)
-                ok = __all_sync(0xffffffffu,
-                                wait_or_abort(&s_full[s], (j / kSBuf) & 1u, abort_flag));
-            std::uint32_t v[2][32];
-            float mx = -INFINITY;
-            if (ok) {
-                gemm::tc_fence_after();
+        std::uint32_t jj = 0;  // tiles of this group processed
+        for (std::uint32_t j = static_cast<std::uint32_t>(grp); j < nkt && ok; j += kSBuf, ++jj) {
+            ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[grp], jj & 1u, abort_flag));
+            if (!ok) break;
+            gemm::tc_fence_after();
+            std::uint32_t v[4][32];
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    tmem_ld32_nowait(tmem + lane_off + s * kBN + col0 + 32 * c, v[c]);
-                tmem_wait_ld();
-                // causal mask: position j*128 + col0 + col; masked scores
-                // become -inf (the scale is positive, so the maximum of the
-                // raw scores gives the maximum of the scaled ones)
-                const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN + col0;
-                const bool masked_tile = kbase + 63 > static_cast<std::int64_t>(p.start) + q0;
-                if (masked_tile) {
+            for (int c = 0; c < 4; ++c) tmem_ld32_nowait(tmem + lane_off + grp * kBN + 32 * c, v[c]);
+            tmem_wait_ld();
+            // causal mask (position j*128 + col past the row's) as -inf; the
+            // scale is positive, so the maximum of the raw scores gives the
+            // maximum of the scaled ones
+            const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN;
+            if (kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + q0) {
 #pragma unroll
-                    for (int c = 0; c < 2; ++c)
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (kbase + 32 * c + i > qpos) v[c][i] = __float_as_uint(-INFINITY);
-                }
-                // eight independent maximum chains, then a tree
-                float e[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) e[i] = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) e[i % 8] = fmaxf(e[i % 8], __uint_as_float(v[c][i]));
-                mx = fmaxf(fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])),
-                           fmaxf(fmaxf(e[4], e[5]), fmaxf(e[6], e[7])));
+                    for (int i = 0; i < 32; ++i)
+                        if (kbase + 32 * c + i > qpos) v[c][i] = __float_as_uint(-INFINITY);
             }
-            // the row maximum over both halves: after this barrier the
-            // partner has also read its S columns, which this thread's P
-            // stores may overwrite
-            float* xb = xchg + (j & 1u) * 2 * kBM;
-            xb[half * kBM + r] = mx;
-            named_bar_sync(pair_bar, 64);
-            if (!ok) continue;
-            mx = fmaxf(mx, xb[(half ^ 1) * kBM + r]);
-            // Reference maximum m in raw score units; probabilities
-            // 2^(scale_log2 * (s - m)) with the scale folded into one FMA.
-            // m moves (and O and the sum are rescaled) only when the row
-            // maximum exceeds it by more than 8 in log2 units, so a
-            // probability stays below 2^8 (exact in f16 as any other) and
-            // most tiles need no rescale -- and no wait for the previous
-            // tile's P.V.  Both threads of a row take the same decision.
-            const float mnew = fmaxf(m, mx);  // finite: position 0 <= qpos is in tile 0
-            const float sc = p.scale_log2;
-            const bool grow = (mnew - m) * sc > 8.f;  // always on the first tile (m = -inf)
+            float e[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) e[i] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) e[i % 8] = fmaxf(e[i % 8], __uint_as_float(v[c][i]));
+            const float mx = fmaxf(fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])),
+                                   fmaxf(fmaxf(e[4], e[5]), fmaxf(e[6], e[7])));
+            // The reference maximum m (raw units) moves, and O_g and the sum
+            // are rescaled, only when the row maximum exceeds it by more than
+            // 8 in log2 units: a probability stays below 2^8 (exact in f16 as
+            // any other) and most tiles skip the rescale and its wait for
+            // the previous P.V.
+            // A row can have no attended position in a tile of group 1 (its
+            // first tile starts at position 128): while m is -inf its
+            // probabilities are exact zeros and nothing moves.
+            const float mnew = fmaxf(m, mx);
+            const bool grow = (mnew - m) * sc > 8.f;  // false while both are -inf (NaN)
             float alpha = 1.f;
             if (grow) {
-                alpha = ex2f((m - mnew) * sc);  // 0 on the first tile
+                alpha = ex2f((m - mnew) * sc);  // 0 when m was -inf
                 m = mnew;
             }
-            const float neg_m = -m * sc;
+            const float neg_m = m == -INFINITY ? 0.f : -m * sc;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            std::uint32_t pk[32];
+            std::uint32_t pk[2][32];
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+            for (int c = 0; c < 4; ++c)
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     const float a = ex2f(fmaf(__uint_as_float(v[c][i]), sc, neg_m));
@@ -358,59 +348,78 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sum4[(i / 2) % 4] += a + b;
                     std::uint32_t h2;
                     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
-                    pk[c * 16 + i / 2] = h2;
+                    pk[c / 2][(c % 2) * 16 + i / 2] = h2;
                 }
             l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            // P (positions col0 .. col0 + 63) over columns [32 half, 32 half + 32)
-            tmem_st32(tmem + lane_off + s * kBN + 32u * static_cast<std::uint32_t>(half), pk);
+            // P over the first 64 columns of this group's S buffer
+            tmem_st32(tmem + lane_off + grp * kBN, pk[0]);
+            tmem_st32(tmem + lane_off + grp * kBN + 32, pk[1]);
             tmem_wait_st();
-            // rescale this thread's half of the O row once the previous
-            // tile's P.V is complete
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                ok = __all_sync(0xffffffffu, wait_or_abort(o_done, (j - 1) & 1u, abort_flag));
-                if (!ok) continue;
+            if (jj > 0 && __any_sync(0xffffffffu, grow)) {
+                // the group's previous P.V must be complete before O_g moves
+                ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[grp], (jj - 1) & 1u, abort_flag));
+                if (!ok) break;
                 gemm::tc_fence_after();
-                {
-                    std::uint32_t o[32];
-                    const std::uint32_t oa = tmem + lane_off + kColO + 32u * static_cast<std::uint32_t>(half);
-                    tmem_ld32_nowait(oa, o);
-                    tmem_wait_ld();
+                std::uint32_t o[2][32];
+                tmem_ld32_nowait(tmem + lane_off + o_col, o[0]);
+                tmem_ld32_nowait(tmem + lane_off + o_col + 32, o[1]);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(oa, o);
-                    tmem_wait_st();
-                }
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
+                tmem_st32(tmem + lane_off + o_col, o[0]);
+                tmem_st32(tmem + lane_off + o_col + 32, o[1]);
+                tmem_wait_st();
             }
             gemm::tc_fence_before();
             __syncwarp();
             if (lane == 0)
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_ready[s]))
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_ready[grp]))
                              : "memory");
         }
-        // output: this thread's half of O / (sum of both halves' sums)
-        sums[half * kBM + r] = l;
-        named_bar_sync(pair_bar, 64);
-        const float lrow = l + sums[(half ^ 1) * kBM + r];
-        if (ok && __all_sync(0xffffffffu, wait_or_abort(o_done, (nkt - 1) & 1u, abort_flag))) {
+        // The two groups' states meet: every softmax thread reaches this
+        // barrier (an aborted loop only ends early), then the thread of group
+        // g writes dimensions [32 g, 32 g + 32) of its row from O_0 and O_1.
+        float* xm = reinterpret_cast<float*>(smem + Smem::kXchg);  // [2][kBM] maxima
+        float* xl = reinterpret_cast<float*>(smem + Smem::kSums);  // [2][kBM] sums
+        xm[grp * kBM + r] = m;
+        xl[grp * kBM + r] = l;
+        named_bar_sync(1, kSoftmaxWarps * 32);
+        const std::uint32_t n0 = (nkt + 1) / 2, n1 = nkt / 2;  // P.V count into O_0, O_1
+        const float m0 = xm[r], m1 = xm[kBM + r];
+        const float mt = fmaxf(m0, m1);
+        const float w0 = n0 > 0 ? ex2f((m0 - mt) * sc) : 0.f;
+        const float w1 = n1 > 0 ? ex2f((m1 - mt) * sc) : 0.f;
+        const float lrow = xl[r] * w0 + xl[kBM + r] * w1;
+        ok = ok && (n0 == 0 || __all_sync(0xffffffffu, wait_or_abort(&o_done[0], (n0 - 1) & 1u, abort_flag)));
+        ok = ok && (n1 == 0 || __all_sync(0xffffffffu, wait_or_abort(&o_done[1], (n1 - 1) & 1u, abort_flag)));
+        if (ok) {
             gemm::tc_fence_after();
-            std::uint32_t o[32];
-            tmem_ld32_nowait(tmem + lane_off + kColO + 32u * static_cast<std::uint32_t>(half), o);
+            const std::uint32_t dcol = 32u * static_cast<std::uint32_t>(grp);
+            std::uint32_t a[32], b[32];
+            tmem_ld32_nowait(tmem + lane_off + kColO + dcol, a);
+            if (n1 > 0) tmem_ld32_nowait(tmem + lane_off + kColO + 64 + dcol, b);
             tmem_wait_ld();
             if (q0 + r < p.tokens) {
                 const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
                 uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<std::uint64_t>(q0) + r) *
                                                                    p.out_row_stride +
-                                                      static_cast<std::uint64_t>(h) * kD + 32 * half);
+                                                      static_cast<std::uint64_t>(h) * kD + dcol);
 #pragma unroll
                 for (int i = 0; i < 32; i += 8) {
-                    std::uint32_t w[4];
+                    std::uint32_t wv[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float a = __uint_as_float(o[i + 2 * e]) * inv;
-                        const float b = __uint_as_float(o[i + 2 * e + 1]) * inv;
-                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(w[e]) : "f"(b), "f"(a));
+                    for (int e2 = 0; e2 < 4; ++e2) {
+                        const int k0 = i + 2 * e2;
+                        float x0 = __uint_as_float(a[k0]) * w0, x1 = __uint_as_float(a[k0 + 1]) * w0;
+                        if (n1 > 0) {
+                            x0 = fmaf(__uint_as_float(b[k0]), w1, x0);
+                            x1 = fmaf(__uint_as_float(b[k0 + 1]), w1, x1);
+                        }
+                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(wv[e2]) : "f"(x1 * inv), "f"(x0 * inv));
                     }
-                    dst[i / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+                    dst[i / 8] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
             }
         }

@@ -7,10 +7,14 @@
 // tokens - 1); K/V from the cache rows row0 .. row0 + start + tokens - 1
 // ([cache rows, kv_heads, 64] f16, this chunk's K/V already appended).
 //
-// One CTA computes 128 query rows of one query head (flash attention):
-// * warp 8 loads the Q tile once and the K and V tiles of 128 positions
-//   (TMA, 128-byte swizzle, four stages; tensor maps end at the last
-//   attended row, so rows past it arrive as zeros);
+// Persistent: one CTA per SM walks work items (128 query rows of one query
+// head; longest first) with tensor memory allocated once, so the next
+// item's Q and first K/V tiles load while the current item finishes
+// (flash attention per item):
+// * warp 8 loads each item's Q tile (two buffers) and the K and V tiles
+//   of 128 positions (TMA, 128-byte swizzle, four stages shared by all
+//   items; tensor maps end at the last attended row, so rows past it
+//   arrive as zeros);
 // * warp 9 allocates tensor memory and one thread issues the MMAs:
 //   S = Q K^T (tcgen05.mma kind::f16, M = 128 queries, N = 128 positions,
 //   A and B K-major in shared memory) into one of two S buffers in TMEM, so
@@ -57,18 +61,19 @@ constexpr std::uint32_t kColO = 256;  // O_g at kColO + 64 g (g = tile parity)
 constexpr std::uint32_t kTmemCols = 512;
 
 struct Smem {
-    static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kTileBytes;                // [kKV] tiles
+    static constexpr int kQ = 0;                              // [2] Q tiles (items alternate)
+    static constexpr int kK = kQ + 2 * kTileBytes;            // [kKV] tiles
     static constexpr int kV = kK + kKV * kTileBytes;          // [kKV] tiles
     static constexpr int kBar = kV + kKV * kTileBytes;
-    // q_full, k_full[kKV], v_full[kKV], kv_empty[kKV], s_full[2], p_ready[2], o_done[2], drained
-    static constexpr int kNumBars = 1 + 3 * kKV + 3 * kSBuf + 1;
+    // q_full[2], q_empty[2], k_full[kKV], v_full[kKV], kv_empty[kKV], s_full[2],
+    // p_ready[2], o_done[2], epi_done, drained
+    static constexpr int kNumBars = 4 + 3 * kKV + 3 * kSBuf + 2;
     static constexpr int kTmemSlot = kBar + kNumBars * 8;
     static constexpr int kAbort = kTmemSlot + 4;
-    // the softmax groups' row maxima [2][kBM] and row sums [2][kBM] (f32)
+    // the softmax groups' row maxima and sums, by item parity: [2][2][kBM] f32 each
     static constexpr int kXchg = (kAbort + 4 + 15) / 16 * 16;
     static constexpr int kSums = kXchg + 2 * 2 * kBM * 4;
-    static constexpr int kUsed = kSums + 2 * kBM * 4 + 1024;  // + 1024-byte alignment slack
+    static constexpr int kUsed = kSums + 2 * 2 * kBM * 4 + 1024;  // + 1024-byte alignment slack
     // at least 120 KB: one CTA per SM, so a CTA's 512 TMEM columns never
     // wait for another CTA of this kernel on the same SM
     static constexpr int kBytes = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
@@ -151,6 +156,12 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+__device__ __forceinline__ float2 half2_bits_to_float2_f(std::uint32_t v) {
+    __half2 h;
+    memcpy(&h, &v, sizeof(h));
+    return __half22float2(h);
+}
+
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -169,29 +180,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     std::uint8_t* smem = smem_raw + (base - raw_base);
     std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + Smem::kBar);
     std::uint64_t* q_full = bars;
-    std::uint64_t* k_full = bars + 1;
+    std::uint64_t* q_empty = bars + 2;
+    std::uint64_t* k_full = bars + 4;
     std::uint64_t* v_full = k_full + kKV;
     std::uint64_t* kv_empty = v_full + kKV;
     std::uint64_t* s_full = kv_empty + kKV;
     std::uint64_t* p_ready = s_full + kSBuf;
     std::uint64_t* o_done = p_ready + kSBuf;
-    std::uint64_t* drained = o_done + kSBuf;
+    std::uint64_t* epi_done = o_done + kSBuf;
+    std::uint64_t* drained = epi_done + 1;
     volatile std::uint32_t* tmem_slot = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kTmemSlot);
     volatile std::uint32_t* abort_flag = reinterpret_cast<volatile std::uint32_t*>(smem + Smem::kAbort);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // the longest query tiles first (causal: later tiles attend more)
-    const std::uint32_t qt = p.q_tiles - 1 - blockIdx.x;
-    const std::uint32_t h = blockIdx.y;
-    const std::uint32_t kvh = h / (p.q_heads / p.kv_heads);
-    const std::uint32_t q0 = qt * kBM;
-    const std::uint32_t q_end = min(q0 + kBM, p.tokens);           // exclusive
-    const std::uint32_t keys = p.start + q_end;                     // attended positions
-    const std::uint32_t nkt = (keys + kBN - 1) / kBN;
+    // Work items (query tile, query head), longest first (causal: later
+    // query tiles attend more positions): item i is query tile
+    // q_tiles - 1 - i / q_heads of head i % q_heads; CTA b takes items
+    // b, b + gridDim.x, ...
+    const std::uint32_t items = p.q_tiles * p.q_heads;
+    struct Item {
+        std::uint32_t h, kvh, q0, nkt;
+    };
+    auto item_at = [&](std::uint32_t i) {
+        Item it;
+        const std::uint32_t qt = p.q_tiles - 1 - i / p.q_heads;
+        it.h = i % p.q_heads;
+        it.kvh = it.h / (p.q_heads / p.kv_heads);
+        it.q0 = qt * kBM;
+        const std::uint32_t q_end = min(it.q0 + kBM, p.tokens);  // exclusive
+        it.nkt = (p.start + q_end + kBN - 1) / kBN;              // tiles of attended positions
+        return it;
+    };
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&q_full[s], 1);
+            mbar_init(&q_empty[s], 1);
+        }
         for (int s = 0; s < kKV; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
@@ -202,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&p_ready[s], kSoftmaxWarps / 2);  // the tile parity's group
             mbar_init(&o_done[s], 1);
         }
+        mbar_init(epi_done, kSoftmaxWarps);
         mbar_init(drained, 1);
         *abort_flag = 0u;
         fence_mbarrier_init();
@@ -225,55 +252,92 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, kTileBytes);
-            tma_load_3d(base + Smem::kQ, &map_q, 0, static_cast<int>(h), static_cast<int>(q0),
-                        smem_u32(q_full));
-            for (std::uint32_t j = 0; j < nkt; ++j) {
-                const int s = j % kKV;
-                if (j >= kKV &&
-                    !wait_or_abort(&kv_empty[s], ((j / kKV) - 1) & 1u, abort_flag))
-                    break;
-                mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-                tma_load_3d(base + Smem::kK + s * kTileBytes, &map_k, 0, static_cast<int>(kvh),
-                            static_cast<int>(j * kBN), smem_u32(&k_full[s]));
-                mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-                tma_load_3d(base + Smem::kV + s * kTileBytes, &map_v, 0, static_cast<int>(kvh),
-                            static_cast<int>(j * kBN), smem_u32(&v_full[s]));
+            // runs ahead across items: the next item's Q and first K/V tiles
+            // load while the current item is still in its last tiles
+            std::uint32_t kt = 0;  // K/V tiles loaded by this CTA
+            bool ok = true;
+            std::uint32_t n = 0;
+            for (std::uint32_t i = blockIdx.x; ok && i < items; i += gridDim.x, ++n) {
+                const Item it = item_at(i);
+                const int qb = n & 1;
+                if (n >= 2 && !wait_or_abort(&q_empty[qb], ((n / 2) - 1) & 1u, abort_flag)) break;
+                mbar_arrive_expect_tx(&q_full[qb], kTileBytes);
+                tma_load_3d(base + Smem::kQ + qb * kTileBytes, &map_q, 0, static_cast<int>(it.h),
+                            static_cast<int>(it.q0), smem_u32(&q_full[qb]));
+                for (std::uint32_t j = 0; j < it.nkt; ++j, ++kt) {
+                    const int s = kt % kKV;
+                    if (kt >= kKV &&
+                        !wait_or_abort(&kv_empty[s], ((kt / kKV) - 1) & 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+                    tma_load_3d(base + Smem::kK + s * kTileBytes, &map_k, 0, static_cast<int>(it.kvh),
+                                static_cast<int>(j * kBN), smem_u32(&k_full[s]));
+                    mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+                    tma_load_3d(base + Smem::kV + s * kTileBytes, &map_v, 0, static_cast<int>(it.kvh),
+                                static_cast<int>(j * kBN), smem_u32(&v_full[s]));
+                }
             }
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
-            auto issue_s = [&](std::uint32_t j) -> bool {
-                const int kv = j % kKV, sb = j % kSBuf;
-                if (!wait_or_abort(&k_full[kv], (j / kKV) & 1u, abort_flag)) return false;
-                gemm::tc_fence_after();
-                const std::uint32_t kaddr = base + Smem::kK + kv * kTileBytes;
+            std::uint32_t kt = 0;                // K/V tiles consumed
+            std::uint32_t cnt0 = 0, cnt1 = 0;   // P.V into O_0 / O_1 so far (all items)
+            bool ok = true;
+            std::uint32_t n = 0;
+            for (std::uint32_t i = blockIdx.x; ok && i < items; i += gridDim.x, ++n) {
+                const Item it = item_at(i);
+                const int qb = n & 1;
+                const std::uint32_t qaddr = base + Smem::kQ + qb * kTileBytes;
+                const std::uint32_t kt0 = kt;
+                auto issue_s = [&](std::uint32_t j) -> bool {
+                    const std::uint32_t t = kt0 + j;
+                    const int kv = t % kKV, sb = j % kSBuf;
+                    if (!wait_or_abort(&k_full[kv], (t / kKV) & 1u, abort_flag)) return false;
+                    gemm::tc_fence_after();
+                    const std::uint32_t kaddr = base + Smem::kK + kv * kTileBytes;
 #pragma unroll
-                for (int k = 0; k < kD / 16; ++k)
-                    umma_f16_ss(tmem + sb * kBN, smem_desc_sw128(base + Smem::kQ + k * 32),
-                                smem_desc_sw128(kaddr + k * 32), kIdescS, k != 0 ? 1u : 0u);
-                gemm::umma_commit(smem_u32(&s_full[sb]));
-                return true;
-            };
-            bool ok = wait_or_abort(q_full, 0, abort_flag) && issue_s(0);
-            for (std::uint32_t j = 0; ok && j < nkt; ++j) {
-                const int kv = j % kKV, sb = j % kSBuf;
-                if (j + 1 < nkt && !issue_s(j + 1)) break;
-                if (!wait_or_abort(&p_ready[sb], (j / kSBuf) & 1u, abort_flag)) break;
-                if (!wait_or_abort(&v_full[kv], (j / kKV) & 1u, abort_flag)) break;
-                gemm::tc_fence_after();
-                const std::uint32_t vaddr = base + Smem::kV + kv * kTileBytes;
+                    for (int k = 0; k < kD / 16; ++k)
+                        umma_f16_ss(tmem + sb * kBN, smem_desc_sw128(qaddr + k * 32),
+                                    smem_desc_sw128(kaddr + k * 32), kIdescS, k != 0 ? 1u : 0u);
+                    gemm::umma_commit(smem_u32(&s_full[sb]));
+                    // the item's last S: its Q buffer is free once it completes
+                    if (j + 1 == it.nkt) gemm::umma_commit(smem_u32(&q_empty[qb]));
+                    return true;
+                };
+                ok = wait_or_abort(&q_full[qb], (n / 2) & 1u, abort_flag) && issue_s(0);
+                // the previous item's epilogue has read O_0 and O_1 before the
+                // first P.V of this item overwrites them
+                if (ok && n > 0) ok = wait_or_abort(epi_done, (n - 1) & 1u, abort_flag);
+                for (std::uint32_t j = 0; ok && j < it.nkt; ++j) {
+                    const std::uint32_t t = kt0 + j;
+                    const int kv = t % kKV, sb = j % kSBuf;
+                    if (j + 1 < it.nkt && !issue_s(j + 1)) {
+                        ok = false;
+                        break;
+                    }
+                    if (!wait_or_abort(&p_ready[sb], (sb ? cnt1 : cnt0) & 1u, abort_flag) ||
+                        !wait_or_abort(&v_full[kv], (t / kKV) & 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    gemm::tc_fence_after();
+                    const std::uint32_t vaddr = base + Smem::kV + kv * kTileBytes;
 #pragma unroll
-                for (int k = 0; k < kBN / 16; ++k)
-                    // A = P (16 positions = 8 columns per step), B = V rows
-                    // of 16 positions (2048 bytes per step, MN-major)
-                    gemm::umma_f16_ta(tmem + kColO + 64u * static_cast<std::uint32_t>(sb),
-                                      tmem + sb * kBN + k * 8,
-                                      smem_desc_sw128(vaddr + k * 2048), kIdescPV,
-                                      (j >= static_cast<std::uint32_t>(kSBuf) || k != 0) ? 1u : 0u);
-                gemm::umma_commit(smem_u32(&o_done[sb]));
-                gemm::umma_commit(smem_u32(&kv_empty[kv]));
+                    for (int k = 0; k < kBN / 16; ++k)
+                        // A = P (16 positions = 8 columns per step), B = V rows
+                        // of 16 positions (2048 bytes per step, MN-major)
+                        gemm::umma_f16_ta(tmem + kColO + 64u * static_cast<std::uint32_t>(sb),
+                                          tmem + sb * kBN + k * 8,
+                                          smem_desc_sw128(vaddr + k * 2048), kIdescPV,
+                                          (j >= static_cast<std::uint32_t>(kSBuf) || k != 0) ? 1u : 0u);
+                    gemm::umma_commit(smem_u32(&o_done[sb]));
+                    gemm::umma_commit(smem_u32(&kv_empty[kv]));
+                    if (sb) ++cnt1; else ++cnt0;
+                }
+                kt = kt0 + it.nkt;
             }
             // every issued MMA completes before the tensor memory is freed
             gemm::umma_commit(smem_u32(drained));
@@ -283,143 +347,181 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // softmax: group g = warp / 4 takes the tiles j with j % 2 == g, one
         // thread per query row r = TMEM lane, with its own reference maximum,
-        // sum and O accumulator O_g; the groups meet once at the end
+        // sum and O accumulator O_g; the groups meet once per item.  Every
+        // softmax thread walks every item of the CTA (a failed wait only
+        // skips work), so all reach each item's named barrier.
         const int quarter = warp % 4, grp = warp / 4;
         const int r = 32 * quarter + lane;
         const std::uint32_t lane_off = static_cast<std::uint32_t>(32 * quarter) << 16;
         const std::uint32_t o_col = kColO + 64u * static_cast<std::uint32_t>(grp);
-        const std::int64_t qpos = static_cast<std::int64_t>(p.start) + q0 + r;
         const float sc = p.scale_log2;
-        float m = -INFINITY, l = 0.f;
+        std::uint32_t cnt0 = 0, cnt1 = 0;  // tiles of each parity group (all items)
         bool ok = true;
-        std::uint32_t jj = 0;  // tiles of this group processed
-        for (std::uint32_t j = static_cast<std::uint32_t>(grp); j < nkt && ok; j += kSBuf, ++jj) {
-            ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[grp], jj & 1u, abort_flag));
-            if (!ok) break;
-            gemm::tc_fence_after();
-            std::uint32_t v[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32_nowait(tmem + lane_off + grp * kBN + 32 * c, v[c]);
-            tmem_wait_ld();
-            // causal mask (position j*128 + col past the row's) as -inf; the
-            // scale is positive, so the maximum of the raw scores gives the
-            // maximum of the scaled ones
-            const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN;
-            if (kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + q0) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (kbase + 32 * c + i > qpos) v[c][i] = __float_as_uint(-INFINITY);
-            }
-            float e[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) e[i] = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 32; ++i) e[i % 8] = fmaxf(e[i % 8], __uint_as_float(v[c][i]));
-            const float mx = fmaxf(fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])),
-                                   fmaxf(fmaxf(e[4], e[5]), fmaxf(e[6], e[7])));
-            // The reference maximum m (raw units) moves, and O_g and the sum
-            // are rescaled, only when the row maximum exceeds it by more than
-            // 8 in log2 units: a probability stays below 2^8 (exact in f16 as
-            // any other) and most tiles skip the rescale and its wait for
-            // the previous P.V.
-            // A row can have no attended position in a tile of group 1 (its
-            // first tile starts at position 128): while m is -inf its
-            // probabilities are exact zeros and nothing moves.
-            const float mnew = fmaxf(m, mx);
-            const bool grow = (mnew - m) * sc > 8.f;  // false while both are -inf (NaN)
-            float alpha = 1.f;
-            if (grow) {
-                alpha = ex2f((m - mnew) * sc);  // 0 when m was -inf
-                m = mnew;
-            }
-            const float neg_m = m == -INFINITY ? 0.f : -m * sc;
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            std::uint32_t pk[2][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float a = ex2f(fmaf(__uint_as_float(v[c][i]), sc, neg_m));
-                    const float b = ex2f(fmaf(__uint_as_float(v[c][i + 1]), sc, neg_m));
-                    sum4[(i / 2) % 4] += a + b;
-                    std::uint32_t h2;
-                    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
-                    pk[c / 2][(c % 2) * 16 + i / 2] = h2;
-                }
-            l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            // P over the first 64 columns of this group's S buffer
-            tmem_st32(tmem + lane_off + grp * kBN, pk[0]);
-            tmem_st32(tmem + lane_off + grp * kBN + 32, pk[1]);
-            tmem_wait_st();
-            if (jj > 0 && __any_sync(0xffffffffu, grow)) {
-                // the group's previous P.V must be complete before O_g moves
-                ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[grp], (jj - 1) & 1u, abort_flag));
+        std::uint32_t n = 0;
+        for (std::uint32_t i = blockIdx.x; i < items; i += gridDim.x, ++n) {
+            const Item it = item_at(i);
+            const std::int64_t qpos = static_cast<std::int64_t>(p.start) + it.q0 + r;
+            const std::uint32_t n0 = (it.nkt + 1) / 2, n1 = it.nkt / 2;  // tiles per group
+            float m = -INFINITY, l = 0.f;
+            std::uint32_t jj = 0;  // this group's tiles of the item
+            for (std::uint32_t j = static_cast<std::uint32_t>(grp); j < it.nkt && ok; j += kSBuf, ++jj) {
+                const std::uint32_t c = (grp ? cnt1 : cnt0) + jj;  // this group's tile, all items
+                ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[grp], c & 1u, abort_flag));
                 if (!ok) break;
                 gemm::tc_fence_after();
-                std::uint32_t o[2][32];
-                tmem_ld32_nowait(tmem + lane_off + o_col, o[0]);
-                tmem_ld32_nowait(tmem + lane_off + o_col + 32, o[1]);
-                tmem_wait_ld();
+                // the row in two halves of 64 positions; the reference maximum
+                // m (raw units) moves, and O_g and the sum are rescaled, only
+                // when the row maximum exceeds it by more than 8 in log2 units:
+                // a probability stays below 2^8 (exact in f16 as any other) and
+                // most tiles skip the rescale and its wait for the previous
+                // P.V.  A row can have no attended position in a half (group
+                // 1's first tile starts at position 128): while m is -inf its
+                // probabilities are exact zeros and nothing moves.
+                const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN;
+                const bool masked_tile = kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + it.q0;
+                float alpha = 1.f, tile_sum = 0.f;
+                bool grow = false;
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
+                for (int hh = 0; hh < 2; ++hh) {
+                    std::uint32_t v[2][32];
+                    tmem_ld32_nowait(tmem + lane_off + grp * kBN + 64 * hh, v[0]);
+                    tmem_ld32_nowait(tmem + lane_off + grp * kBN + 64 * hh + 32, v[1]);
+                    tmem_wait_ld();
+                    // causal mask (positions past the row's) as -inf; the scale
+                    // is positive, so the maximum of the raw scores gives the
+                    // maximum of the scaled ones
+                    if (masked_tile) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
-                tmem_st32(tmem + lane_off + o_col, o[0]);
-                tmem_st32(tmem + lane_off + o_col + 32, o[1]);
-                tmem_wait_st();
-            }
-            gemm::tc_fence_before();
-            __syncwarp();
-            if (lane == 0)
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_ready[grp]))
-                             : "memory");
-        }
-        // The two groups' states meet: every softmax thread reaches this
-        // barrier (an aborted loop only ends early), then the thread of group
-        // g writes dimensions [32 g, 32 g + 32) of its row from O_0 and O_1.
-        float* xm = reinterpret_cast<float*>(smem + Smem::kXchg);  // [2][kBM] maxima
-        float* xl = reinterpret_cast<float*>(smem + Smem::kSums);  // [2][kBM] sums
-        xm[grp * kBM + r] = m;
-        xl[grp * kBM + r] = l;
-        named_bar_sync(1, kSoftmaxWarps * 32);
-        const std::uint32_t n0 = (nkt + 1) / 2, n1 = nkt / 2;  // P.V count into O_0, O_1
-        const float m0 = xm[r], m1 = xm[kBM + r];
-        const float mt = fmaxf(m0, m1);
-        const float w0 = n0 > 0 ? ex2f((m0 - mt) * sc) : 0.f;
-        const float w1 = n1 > 0 ? ex2f((m1 - mt) * sc) : 0.f;
-        const float lrow = xl[r] * w0 + xl[kBM + r] * w1;
-        ok = ok && (n0 == 0 || __all_sync(0xffffffffu, wait_or_abort(&o_done[0], (n0 - 1) & 1u, abort_flag)));
-        ok = ok && (n1 == 0 || __all_sync(0xffffffffu, wait_or_abort(&o_done[1], (n1 - 1) & 1u, abort_flag)));
-        if (ok) {
-            gemm::tc_fence_after();
-            const std::uint32_t dcol = 32u * static_cast<std::uint32_t>(grp);
-            std::uint32_t a[32], b[32];
-            tmem_ld32_nowait(tmem + lane_off + kColO + dcol, a);
-            if (n1 > 0) tmem_ld32_nowait(tmem + lane_off + kColO + 64 + dcol, b);
-            tmem_wait_ld();
-            if (q0 + r < p.tokens) {
-                const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
-                uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<std::uint64_t>(q0) + r) *
-                                                                   p.out_row_stride +
-                                                      static_cast<std::uint64_t>(h) * kD + dcol);
+                        for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
-                for (int i = 0; i < 32; i += 8) {
-                    std::uint32_t wv[4];
-#pragma unroll
-                    for (int e2 = 0; e2 < 4; ++e2) {
-                        const int k0 = i + 2 * e2;
-                        float x0 = __uint_as_float(a[k0]) * w0, x1 = __uint_as_float(a[k0 + 1]) * w0;
-                        if (n1 > 0) {
-                            x0 = fmaf(__uint_as_float(b[k0]), w1, x0);
-                            x1 = fmaf(__uint_as_float(b[k0 + 1]), w1, x1);
-                        }
-                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(wv[e2]) : "f"(x1 * inv), "f"(x0 * inv));
+                            for (int e = 0; e < 32; ++e)
+                                if (kbase + 64 * hh + 32 * cc + e > qpos) v[cc][e] = __float_as_uint(-INFINITY);
                     }
-                    dst[i / 8] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                    float mx8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) mx8[e % 8] = fmaxf(mx8[e % 8], __uint_as_float(v[cc][e]));
+                    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    const float mnew = fmaxf(m, mx);
+                    if ((mnew - m) * sc > 8.f) {  // false while both are -inf (NaN)
+                        const float f = ex2f((m - mnew) * sc);  // 0 when m was -inf
+                        alpha *= f;
+                        tile_sum *= f;
+                        m = mnew;
+                        grow = true;
+                        if (hh == 1) {
+                            // rare: half 0's P (columns [0, 32)) was stored with
+                            // the old maximum
+                            std::uint32_t q[32];
+                            tmem_wait_st();
+                            tmem_ld32_nowait(tmem + lane_off + grp * kBN, q);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                const float2 pf = half2_bits_to_float2_f(q[e]);
+                                asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(q[e]) : "f"(pf.y * f), "f"(pf.x * f));
+                            }
+                            tmem_st32(tmem + lane_off + grp * kBN, q);
+                        }
+                    }
+                    const float neg_m = m == -INFINITY ? 0.f : -m * sc;
+                    float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+                    std::uint32_t pk[32];
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const float a = ex2f(fmaf(__uint_as_float(v[cc][e]), sc, neg_m));
+                            const float b = ex2f(fmaf(__uint_as_float(v[cc][e + 1]), sc, neg_m));
+                            sum4[(e / 2) % 4] += a + b;
+                            std::uint32_t h2;
+                            asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
+                            pk[cc * 16 + e / 2] = h2;
+                        }
+                    tile_sum += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+                    // P of this half over columns [32 hh, 32 hh + 32) of the S buffer
+                    tmem_st32(tmem + lane_off + grp * kBN + 32 * hh, pk);
+                }
+                l = fmaf(l, alpha, tile_sum);
+                tmem_wait_st();
+                if (jj > 0 && __any_sync(0xffffffffu, grow)) {
+                    // the group's previous P.V must be complete before O_g moves
+                    ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[grp], (c - 1) & 1u, abort_flag));
+                    if (!ok) break;
+                    gemm::tc_fence_after();
+                    std::uint32_t o[2][32];
+                    tmem_ld32_nowait(tmem + lane_off + o_col, o[0]);
+                    tmem_ld32_nowait(tmem + lane_off + o_col + 32, o[1]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[cc][e] = __float_as_uint(__uint_as_float(o[cc][e]) * alpha);
+                    tmem_st32(tmem + lane_off + o_col, o[0]);
+                    tmem_st32(tmem + lane_off + o_col + 32, o[1]);
+                    tmem_wait_st();
+                }
+                gemm::tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&p_ready[grp]))
+                                 : "memory");
+            }
+            cnt0 += n0;
+            cnt1 += n1;
+            // The groups' states meet (by item parity in shared memory), then
+            // the thread of group g writes dimensions [32 g, 32 g + 32) of its
+            // row from O_0 and O_1 and releases them for the next item.
+            float* xm = reinterpret_cast<float*>(smem + Smem::kXchg) + (n & 1u) * 2 * kBM;
+            float* xl = reinterpret_cast<float*>(smem + Smem::kSums) + (n & 1u) * 2 * kBM;
+            xm[grp * kBM + r] = m;
+            xl[grp * kBM + r] = l;
+            named_bar_sync(1, kSoftmaxWarps * 32);
+            const float m0 = xm[r], m1 = xm[kBM + r];
+            const float mt = fmaxf(m0, m1);
+            const float w0 = m0 == -INFINITY ? 0.f : ex2f((m0 - mt) * sc);
+            const float w1 = (n1 == 0 || m1 == -INFINITY) ? 0.f : ex2f((m1 - mt) * sc);
+            const float lrow = xl[r] * w0 + (n1 > 0 ? xl[kBM + r] * w1 : 0.f);
+            if (ok)
+                ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[0], (cnt0 - 1) & 1u, abort_flag));
+            if (ok && n1 > 0)
+                ok = __all_sync(0xffffffffu, wait_or_abort(&o_done[1], (cnt1 - 1) & 1u, abort_flag));
+            if (ok) {
+                gemm::tc_fence_after();
+                const std::uint32_t dcol = 32u * static_cast<std::uint32_t>(grp);
+                std::uint32_t a[32], b[32];
+                tmem_ld32_nowait(tmem + lane_off + kColO + dcol, a);
+                if (n1 > 0) tmem_ld32_nowait(tmem + lane_off + kColO + 64 + dcol, b);
+                tmem_wait_ld();
+                gemm::tc_fence_before();
+                __syncwarp();
+                if (lane == 0)  // O_0 and O_1 are read: the next item may overwrite them
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(epi_done))
+                                 : "memory");
+                if (it.q0 + r < p.tokens) {
+                    const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
+                    uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<std::uint64_t>(it.q0) + r) *
+                                                                       p.out_row_stride +
+                                                          static_cast<std::uint64_t>(it.h) * kD + dcol);
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8) {
+                        std::uint32_t wv[4];
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; ++e2) {
+                            const int k0 = e + 2 * e2;
+                            float x0 = __uint_as_float(a[k0]) * w0, x1 = __uint_as_float(a[k0 + 1]) * w0;
+                            if (n1 > 0) {
+                                x0 = fmaf(__uint_as_float(b[k0]), w1, x0);
+                                x1 = fmaf(__uint_as_float(b[k0 + 1]), w1, x1);
+                            }
+                            asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(wv[e2]) : "f"(x1 * inv), "f"(x0 * inv));
+                        }
+                        dst[e / 8] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                    }
                 }
             }
         }
@@ -497,7 +599,13 @@ extern "C" int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_
     static std::atomic<std::uint64_t> done{0};
     st = ensure_dynamic_smem(gqa_prefill_kernel, Smem::kBytes, done);
     if (st != kSuccess) return st;
-    return launch_pdl_smem(gqa_prefill_kernel, dim3(p.q_tiles, static_cast<unsigned>(q_heads)),
-                           dim3(kThreads), Smem::kBytes, static_cast<cudaStream_t>(stream), map_q,
-                           map_k, map_v, p);
+    // persistent: one CTA per SM (at most one per item)
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const std::uint64_t items = static_cast<std::uint64_t>(p.q_tiles) * q_heads;
+    const unsigned grid = static_cast<unsigned>(items < static_cast<std::uint64_t>(sms) ? items : sms);
+    return launch_pdl_smem(gqa_prefill_kernel, dim3(grid), dim3(kThreads), Smem::kBytes,
+                           static_cast<cudaStream_t>(stream), map_q, map_k, map_v, p);
 }

@@ -52,7 +52,17 @@ constexpr int kSBuf = 2;      // S buffers in tensor memory
 constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kThreads = 10 * 32;
+// Warps 10 and 11 only complete the third warpgroup (register split below).
+constexpr int kThreads = 12 * 32;
+// Register split (setmaxnreg, per warpgroup): launched at 168 per thread
+// (12 warps: 3 per SM sub-partition); the producer/MMA warpgroup gives up to
+// 40 and the two softmax warpgroups take 232:  384 x 168 = 64512 =
+// 256 x 232 + 128 x 40, and per sub-partition 32 x (232 + 232 + 40) <= 16384.
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 232;
+constexpr int kOtherRegs = 40;
+static_assert(kThreads * kLaunchRegs == 256 * kSoftmaxRegs + 128 * kOtherRegs, "register split");
+static_assert(32 * (2 * kSoftmaxRegs + kOtherRegs) <= 16384, "registers of a sub-partition");
 constexpr int kTileBytes = kBN * kD * 2;  // 16 KB (also the Q tile)
 
 // TMEM columns: S0 [0, 128), S1 [128, 256), O_0 [256, 320), O_1 [320, 384);
@@ -250,7 +260,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     pdl_wait();
 
-    if (warp == kProducerWarp) {
+    if (warp >= kSoftmaxWarps) {
+      // the third warpgroup (producer, MMA issuer, two idle warps) gives up
+      // registers for the softmax warpgroups
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
+      if (warp == kProducerWarp) {
         if (lane == 0) {
             // runs ahead across items: the next item's Q and first K/V tiles
             // load while the current item is still in its last tiles
@@ -344,7 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_bounded(drained, 0, &g_device_status);
         }
         __syncwarp();
+      }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
         // softmax: group g = warp / 4 takes the tiles j with j % 2 == g, one
         // thread per query row r = TMEM lane, with its own reference maximum,
         // sum and O accumulator O_g; the groups meet once per item.  Every
@@ -369,84 +385,63 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[grp], c & 1u, abort_flag));
                 if (!ok) break;
                 gemm::tc_fence_after();
-                // the row in two halves of 64 positions; the reference maximum
-                // m (raw units) moves, and O_g and the sum are rescaled, only
-                // when the row maximum exceeds it by more than 8 in log2 units:
-                // a probability stays below 2^8 (exact in f16 as any other) and
-                // most tiles skip the rescale and its wait for the previous
-                // P.V.  A row can have no attended position in a half (group
-                // 1's first tile starts at position 128): while m is -inf its
-                // probabilities are exact zeros and nothing moves.
+                std::uint32_t v[4][32];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) tmem_ld32_nowait(tmem + lane_off + grp * kBN + 32 * cc, v[cc]);
+                tmem_wait_ld();
+                // causal mask (position j*128 + col past the row's) as -inf;
+                // the scale is positive, so the maximum of the raw scores
+                // gives the maximum of the scaled ones
                 const std::int64_t kbase = static_cast<std::int64_t>(j) * kBN;
-                const bool masked_tile = kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + it.q0;
-                float alpha = 1.f, tile_sum = 0.f;
-                bool grow = false;
+                if (kbase + kBN - 1 > static_cast<std::int64_t>(p.start) + it.q0) {
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    std::uint32_t v[2][32];
-                    tmem_ld32_nowait(tmem + lane_off + grp * kBN + 64 * hh, v[0]);
-                    tmem_ld32_nowait(tmem + lane_off + grp * kBN + 64 * hh + 32, v[1]);
-                    tmem_wait_ld();
-                    // causal mask (positions past the row's) as -inf; the scale
-                    // is positive, so the maximum of the raw scores gives the
-                    // maximum of the scaled ones
-                    if (masked_tile) {
+                    for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-                        for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-                            for (int e = 0; e < 32; ++e)
-                                if (kbase + 64 * hh + 32 * cc + e > qpos) v[cc][e] = __float_as_uint(-INFINITY);
-                    }
-                    float mx8[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
-#pragma unroll
-                    for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) mx8[e % 8] = fmaxf(mx8[e % 8], __uint_as_float(v[cc][e]));
-                    const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                           fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-                    const float mnew = fmaxf(m, mx);
-                    if ((mnew - m) * sc > 8.f) {  // false while both are -inf (NaN)
-                        const float f = ex2f((m - mnew) * sc);  // 0 when m was -inf
-                        alpha *= f;
-                        tile_sum *= f;
-                        m = mnew;
-                        grow = true;
-                        if (hh == 1) {
-                            // rare: half 0's P (columns [0, 32)) was stored with
-                            // the old maximum
-                            std::uint32_t q[32];
-                            tmem_wait_st();
-                            tmem_ld32_nowait(tmem + lane_off + grp * kBN, q);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) {
-                                const float2 pf = half2_bits_to_float2_f(q[e]);
-                                asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(q[e]) : "f"(pf.y * f), "f"(pf.x * f));
-                            }
-                            tmem_st32(tmem + lane_off + grp * kBN, q);
-                        }
-                    }
-                    const float neg_m = m == -INFINITY ? 0.f : -m * sc;
-                    float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-                    std::uint32_t pk[32];
-#pragma unroll
-                    for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2) {
-                            const float a = ex2f(fmaf(__uint_as_float(v[cc][e]), sc, neg_m));
-                            const float b = ex2f(fmaf(__uint_as_float(v[cc][e + 1]), sc, neg_m));
-                            sum4[(e / 2) % 4] += a + b;
-                            std::uint32_t h2;
-                            asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
-                            pk[cc * 16 + e / 2] = h2;
-                        }
-                    tile_sum += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-                    // P of this half over columns [32 hh, 32 hh + 32) of the S buffer
-                    tmem_st32(tmem + lane_off + grp * kBN + 32 * hh, pk);
+                        for (int e = 0; e < 32; ++e)
+                            if (kbase + 32 * cc + e > qpos) v[cc][e] = __float_as_uint(-INFINITY);
                 }
-                l = fmaf(l, alpha, tile_sum);
+                float mx8[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mx8[e % 8] = fmaxf(mx8[e % 8], __uint_as_float(v[cc][e]));
+                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                // The reference maximum m (raw units) moves, and O_g and the
+                // sum are rescaled, only when the row maximum exceeds it by
+                // more than 8 in log2 units: a probability stays below 2^8
+                // (exact in f16 as any other) and most tiles skip the rescale
+                // and its wait for the previous P.V.  A row can have no
+                // attended position in a tile of group 1 (its first tile
+                // starts at position 128): while m is -inf its probabilities
+                // are exact zeros and nothing moves.
+                const float mnew = fmaxf(m, mx);
+                const bool grow = (mnew - m) * sc > 8.f;  // false while both are -inf (NaN)
+                float alpha = 1.f;
+                if (grow) {
+                    alpha = ex2f((m - mnew) * sc);  // 0 when m was -inf
+                    m = mnew;
+                }
+                const float neg_m = m == -INFINITY ? 0.f : -m * sc;
+                float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+                std::uint32_t pk[2][32];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float a = ex2f(fmaf(__uint_as_float(v[cc][e]), sc, neg_m));
+                        const float b = ex2f(fmaf(__uint_as_float(v[cc][e + 1]), sc, neg_m));
+                        sum4[(e / 2) % 4] += a + b;
+                        std::uint32_t h2;
+                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
+                        pk[cc / 2][(cc % 2) * 16 + e / 2] = h2;
+                    }
+                l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+                // P over the first 64 columns of this group's S buffer
+                tmem_st32(tmem + lane_off + grp * kBN, pk[0]);
+                tmem_st32(tmem + lane_off + grp * kBN + 32, pk[1]);
                 tmem_wait_st();
                 if (jj > 0 && __any_sync(0xffffffffu, grow)) {
                     // the group's previous P.V must be complete before O_g moves
@@ -599,6 +594,17 @@ extern "C" int mote_cuda_gqa_attention_prefill_f16(const void* q, const void* k_
     static std::atomic<std::uint64_t> done{0};
     st = ensure_dynamic_smem(gqa_prefill_kernel, Smem::kBytes, done);
     if (st != kSuccess) return st;
+    // The register split is exact for a launch at kLaunchRegs per thread; a
+    // build that allocated another count could leave setmaxnreg.inc waiting
+    // for registers that do not exist, so it is never launched.
+    static std::atomic<int> regs_checked{0};
+    if (regs_checked.load(std::memory_order_acquire) == 0) {
+        cudaFuncAttributes fa{};
+        const cudaError_t ea = cudaFuncGetAttributes(&fa, gqa_prefill_kernel);
+        if (ea != cudaSuccess) return static_cast<int>(ea);
+        if (fa.numRegs != kLaunchRegs) return static_cast<int>(cudaErrorInvalidConfiguration);
+        regs_checked.store(1, std::memory_order_release);
+    }
     // persistent: one CTA per SM (at most one per item)
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);

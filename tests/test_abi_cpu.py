@@ -131,6 +131,70 @@ def test_new_op_argument_rules(lib):
                                            1, 64, 1, 1, 64, 5, eps, STREAM) == -1
 
 
+def test_attention_argument_rules(lib):
+    scale = ctypes.c_float(0.125)
+    # KV-cache append: null pointers, empty, rows not in 16-byte vectors, alignment
+    assert lib.mote_cuda_kv_cache_append_f16(None, FAKE, FAKE, FAKE, FAKE, 1, 8, 64, 16, None,
+                                             STREAM) == 1
+    assert lib.mote_cuda_kv_cache_append_f16(FAKE, FAKE, FAKE, FAKE, FAKE, 0, 8, 64, 16, None,
+                                             STREAM) == 0
+    assert lib.mote_cuda_kv_cache_append_f16(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 1, 4, 16, None,
+                                             STREAM) == 1
+    assert lib.mote_cuda_kv_cache_append_f16(FAKE + 8, FAKE, FAKE, FAKE, FAKE, 1, 8, 64, 16, None,
+                                             STREAM) == 1
+    # decode: nulls, empty batch, group, head_dim, max_len beyond the capacity, scale
+    dec = lib.mote_cuda_gqa_attention_decode_f16
+    assert dec(None, FAKE, FAKE, FAKE, FAKE, 1, 32, 8, 64, 64, 64, scale, None, 0, STREAM) == 1
+    assert dec(FAKE, FAKE, FAKE, FAKE, FAKE, 0, 32, 8, 64, 64, 64, scale, None, 0, STREAM) == 0
+    assert dec(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 30, 8, 64, 64, 64, scale, None, 0, STREAM) == 1
+    assert dec(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 32, 8, 96, 64, 64, scale, None, 0, STREAM) == 1
+    assert dec(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 32, 8, 64, 64, 65, scale, None, 0, STREAM) == 1
+    assert dec(FAKE, FAKE, FAKE, FAKE, FAKE, 1, 32, 8, 64, 64, 64, ctypes.c_float(float("inf")),
+               None, 0, STREAM) == 1
+    # prefill: nulls, empty, head_dim, a non-positive scale, rows beyond the cache
+    pre = lib.mote_cuda_gqa_attention_prefill_f16
+    assert pre(None, FAKE, FAKE, FAKE, 8, 0, 32, 8, 64, 0, 64, scale, STREAM) == 1
+    assert pre(FAKE, FAKE, FAKE, FAKE, 0, 0, 32, 8, 64, 0, 64, scale, STREAM) == 0
+    assert pre(FAKE, FAKE, FAKE, FAKE, 8, 0, 32, 8, 128, 0, 64, scale, STREAM) == 1
+    assert pre(FAKE, FAKE, FAKE, FAKE, 8, 0, 32, 8, 64, 0, 64, ctypes.c_float(0.0), STREAM) == 1
+    assert pre(FAKE, FAKE, FAKE, FAKE, 8, 0, 32, 8, 64, 0, 64, ctypes.c_float(-0.1), STREAM) == 1
+    assert pre(FAKE, FAKE, FAKE, FAKE, 8, 60, 32, 8, 64, 0, 64, scale, STREAM) == 1
+
+
+def test_decode_attention_chunk_plan(lib):
+    """The decode split's chunk count (host logic): one chunk when the
+    sequences x KV heads already fill the SMs, else chunks of whole tiles
+    (4096 / head_dim positions) dealt four to a CTA; the workspace holds one
+    f32 partial output plus max and sum per (sequence, query head, chunk)."""
+    def ws(batch, qh, kvh, hd, max_len):
+        n = ctypes.c_uint64(123)
+        assert lib.mote_cuda_gqa_attention_decode_workspace_bytes(batch, qh, kvh, hd, max_len,
+                                                                  ctypes.byref(n)) == 0
+        return n.value
+    assert ws(16, 32, 8, 64, 4096) == 0                  # 128 CTAs, one chunk each
+    assert ws(1, 32, 8, 64, 4096) == 32 * 16 * 66 * 4    # 16 chunks of 4 tiles
+    assert ws(1, 32, 8, 64, 32768) == 32 * 16 * 66 * 4   # 16 chunks of 32 tiles
+    assert ws(1, 64, 2, 128, 2000) == 64 * 16 * 130 * 4  # two head groups, 63 tiles of 32
+    assert ws(4, 32, 8, 64, 0) == 0
+    assert ws(1, 32, 8, 96, 64) == 0                     # rejected by the launch itself
+
+
+def test_decoder_stack_argument_rules(lib):
+    n = ctypes.c_uint64(0)
+    assert lib.mote_cuda_q4_0_decoder_stack_workspace_bytes(2048, ctypes.byref(n)) == 0
+    assert n.value == 256 + 16 * 2048
+    eps = ctypes.c_float(1e-5)
+    stack = lib.mote_cuda_q4_0_decoder_stack_f16
+    ws_ok = 0x10000  # 256-byte aligned
+    assert stack(None, 1, FAKE, 2048, 8192, 32, 8, 64, eps, ws_ok, n.value, STREAM) == 1
+    assert stack(FAKE, 0, FAKE, 2048, 8192, 32, 8, 64, eps, ws_ok, n.value, STREAM) == 0
+    assert stack(FAKE, 1, FAKE, 2000, 8192, 32, 8, 64, eps, ws_ok, n.value, STREAM) == 1
+    assert stack(FAKE, 1, FAKE, 2048, 8192, 30, 8, 64, eps, ws_ok, n.value, STREAM) == 1
+    assert stack(FAKE, 1, FAKE, 2048, 8192, 32, 8, 64, eps, ws_ok, n.value - 1, STREAM) == 1
+    assert stack(FAKE, 1, FAKE, 2048, 8192, 32, 8, 64, ctypes.c_float(-1.0), ws_ok, n.value,
+                 STREAM) == 1
+
+
 def test_status_strings(lib):
     assert b"invalid" in lib.mote_cuda_status_string(-1).lower()
     assert lib.mote_cuda_status_string(1)

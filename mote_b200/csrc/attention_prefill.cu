@@ -172,6 +172,31 @@ __device__ __forceinline__ float2 half2_bits_to_float2_f(std::uint32_t v) {
     return __half22float2(h);
 }
 
+// Packed f32 pairs (Blackwell f32x2 arithmetic) and the three-input maximum.
+__device__ __forceinline__ std::uint64_t pack_f32x2(float lo, float hi) {
+    std::uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack_f32x2(std::uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ std::uint64_t fma_f32x2(std::uint64_t a, std::uint64_t b, std::uint64_t c) {
+    std::uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ std::uint64_t add_f32x2(std::uint64_t a, std::uint64_t b) {
+    std::uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float m;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+    return m;
+}
+
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -406,7 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) mx8[e % 8] = fmaxf(mx8[e % 8], __uint_as_float(v[cc][e]));
+                    for (int e = 0; e < 32; e += 2)
+                        mx8[(e / 2) % 8] = max3f(mx8[(e / 2) % 8], __uint_as_float(v[cc][e]),
+                                                 __uint_as_float(v[cc][e + 1]));
                 const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                        fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
                 // The reference maximum m (raw units) moves, and O_g and the
@@ -425,20 +452,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m = mnew;
                 }
                 const float neg_m = m == -INFINITY ? 0.f : -m * sc;
-                float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+                // pairs of probabilities with packed f32x2 arithmetic: one
+                // FMA for both exponents, one add for both sums
+                const std::uint64_t sc2 = pack_f32x2(sc, sc), nm2 = pack_f32x2(neg_m, neg_m);
+                std::uint64_t acc2[4] = {0, 0, 0, 0};  // (+0, +0) per pair of lanes
                 std::uint32_t pk[2][32];
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
-                        const float a = ex2f(fmaf(__uint_as_float(v[cc][e]), sc, neg_m));
-                        const float b = ex2f(fmaf(__uint_as_float(v[cc][e + 1]), sc, neg_m));
-                        sum4[(e / 2) % 4] += a + b;
+                        float xa, xb;
+                        unpack_f32x2(fma_f32x2(pack_f32x2(__uint_as_float(v[cc][e]),
+                                                          __uint_as_float(v[cc][e + 1])),
+                                               sc2, nm2),
+                                     xa, xb);
+                        const float a = ex2f(xa);
+                        const float b = ex2f(xb);
+                        acc2[(e / 2) % 4] = add_f32x2(acc2[(e / 2) % 4], pack_f32x2(a, b));
                         std::uint32_t h2;
                         asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(b), "f"(a));
                         pk[cc / 2][(cc % 2) * 16 + e / 2] = h2;
                     }
-                l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+                float sum = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float x0, x1;
+                    unpack_f32x2(acc2[i], x0, x1);
+                    sum += x0 + x1;
+                }
+                l = fmaf(l, alpha, sum);
                 // P over the first 64 columns of this group's S buffer
                 tmem_st32(tmem + lane_off + grp * kBN, pk[0]);
                 tmem_st32(tmem + lane_off + grp * kBN + 32, pk[1]);

@@ -348,10 +348,12 @@ __global__ void __launch_bounds__(kThreads, 2) q4_k_gemv_kernel(const Params p) 
             const float dmh = half_bits_to_float(hh.x >> 16);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                acc[nt][0] = fmaf(dg, dot[nt][0], fmaf(-dmg, mins[nt][0], acc[nt][0]));
-                acc[nt][1] = fmaf(dg, dot[nt][1], fmaf(-dmg, mins[nt][1], acc[nt][1]));
-                acc[nt][2] = fmaf(dh, dot[nt][2], fmaf(-dmh, mins[nt][2], acc[nt][2]));
-                acc[nt][3] = fmaf(dh, dot[nt][3], fmaf(-dmh, mins[nt][3], acc[nt][3]));
+                // acc += d * dot - dmin * mins, as two packed f32x2 FMAs per row
+                // pair (each lane rounds as fmaf, in the same order)
+                q4::fma_pair(acc[nt][0], acc[nt][1], -dmg, -dmg, mins[nt][0], mins[nt][1]);
+                q4::fma_pair(acc[nt][0], acc[nt][1], dg, dg, dot[nt][0], dot[nt][1]);
+                q4::fma_pair(acc[nt][2], acc[nt][3], -dmh, -dmh, mins[nt][2], mins[nt][3]);
+                q4::fma_pair(acc[nt][2], acc[nt][3], dh, dh, dot[nt][2], dot[nt][3]);
             }
             __syncwarp();  // the slot is refilled by the next iteration's issue
             slot = slot + 1 == STAGES ? 0 : slot + 1;
@@ -600,10 +602,9 @@ __global__ void __launch_bounds__(kThreads, 2) q6_k_gemv_kernel(const Params p) 
                         float tmp[4] = {0.f, 0.f, 0.f, 0.f};
                         mma_16816(tmp, p01[0], p01[1], p23[0], p23[1], xb.x, xb.y, tmp);
                         const int k4 = decltype(ss)::value;
-                        acc[nt][0] = fmaf(dsg[k4], tmp[0], acc[nt][0]);
-                        acc[nt][1] = fmaf(dsg[k4], tmp[1], acc[nt][1]);
-                        acc[nt][2] = fmaf(dsh[k4], tmp[2], acc[nt][2]);
-                        acc[nt][3] = fmaf(dsh[k4], tmp[3], acc[nt][3]);
+                        // packed f32x2 FMAs (each lane rounds as fmaf)
+                        q4::fma_pair(acc[nt][0], acc[nt][1], dsg[k4], dsg[k4], tmp[0], tmp[1]);
+                        q4::fma_pair(acc[nt][2], acc[nt][3], dsh[k4], dsh[k4], tmp[2], tmp[3]);
                     }
                 });
             });

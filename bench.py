@@ -1305,6 +1305,32 @@ def run_single_case(args) -> None:
                 hd, 0, ctypes.c_float(1e-6), b.stream()), "norm_rope")
         nbytes = (2 * t * hidden + 2 * t * qh * hd + 2 * t * kh * hd) * 2 + hidden * 2 + \
             2 * t * (hd // 2) * 4
+    elif args.only == "stack":
+        # the persistent decoder stack: --m layers of Llama-3.2-1B shapes at one
+        # token (distinct random weights; 4 layers = 137 MB > L2)
+        import numpy as np
+
+        from mote_b200 import decoder
+        from mote_b200.context import CudaContext
+        from mote_b200.types import DType, plain
+
+        ctx = CudaContext(b.local_rank)
+        shape = decoder.LayerShape()
+        count = max(1, args.m)
+        layers = [decoder.random_layer(ctx, shape, seed=70 + i, vocab=1000) for i in range(count)]
+        rng = np.random.default_rng(0)
+        for layer in layers:
+            ctx.upload_numpy(layer.attn, rng.normal(0, 1, (1, shape.hidden)).astype(np.float16))
+            layer.set_position(7)
+        h_in = ctx.from_bytes(plain((1, shape.hidden), DType.F16),
+                              rng.normal(0, 0.5, shape.hidden).astype(np.float16))
+        st = decoder.DecoderStackQ4_0(ctx, layers)
+        ctx.sync()
+        torch.cuda.set_stream(torch.cuda.ExternalStream(ctx.stream))  # the events' stream
+
+        def launch():
+            st.run(h_in)
+        nbytes = count * shape.weight_bytes()
     else:
         raise SystemExit(f"unknown --only {args.only}")
     for _ in range(args.launches):
@@ -1324,7 +1350,8 @@ def main() -> int:
     p = argparse.ArgumentParser()
     p.add_argument("--only", default=None,
                    help="profile one kernel: gemv | q8_0 | q4_k | q6_k | norm_rope | "
-                        "attn_decode (--m batch, --n length) | attn_prefill (--n tokens)")
+                        "attn_decode (--m batch, --n length) | attn_prefill (--n tokens) | "
+                        "stack (--m layers)")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--n", type=int, default=128256)
     p.add_argument("--k", type=int, default=4096)

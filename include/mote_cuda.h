@@ -406,7 +406,8 @@ int mote_cuda_kv_cache_append_f16(const void* k_new, const void* v_new, void* k_
  * len_b = min(seq_lens[b], max_len), max_len <= seq_capacity; a sequence of
  * length 0 gets zeros.  q_heads % kv_heads == 0, head_dim 64 or 128,
  * 16-byte aligned tensors.  Splits the
- * positions over CTAs and merges the parts in a second kernel: workspace of
+ * positions over CTAs, which merge their parts inside a thread-block cluster
+ * (up to 8 parts) or in a second kernel: workspace of
  * mote_cuda_gqa_attention_decode_workspace_bytes bytes (16-byte aligned; 0
  * means none is needed; contents need no initialisation).  Other shapes or a
  * missing workspace -> 1. */

@@ -41,6 +41,12 @@ constexpr int kStageBytes = 16384;   // K and V of one tile
 constexpr int kStagesPerWarp = 3;    // 48 KB ring per warp, 192 KB per CTA
 constexpr int kHeadsPerCta = 16;     // query heads per CTA (the MMA rows)
 constexpr int kSplitSmem = kWarpsPerCta * kStagesPerWarp * kStageBytes;
+// Cluster path: a CTA's merged state (O [16][D] f32, max [16], sum [16]) at
+// 24 KB into warp 0's ring, after that warp's own state (at most 8.1 KB).
+constexpr int kClusterStateOffset = 24 * 1024;
+// At most 8 chunks to a cluster (the portable size): 16-CTA clusters of
+// full-SM CTAs measured slower (fewer of them fit on the GPCs at a time).
+constexpr int kMaxClusterChunks = 8;
 
 // ---------------------------------------------------------------------------
 // KV-cache append
@@ -91,6 +97,24 @@ __device__ __forceinline__ float2 half2_bits_to_float2(std::uint32_t v) {
     __half2 h;
     memcpy(&h, &v, sizeof(h));
     return __half22float2(h);
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ std::uint32_t cluster_rank() {
+    std::uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// A float of cluster CTA `rank`'s shared memory at this CTA's address `addr`.
+__device__ __forceinline__ float ld_dsmem_f32(std::uint32_t addr, std::uint32_t rank) {
+    std::uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -154,7 +178,12 @@ __device__ __forceinline__ void split_pair(float a, float b, std::uint32_t& hi,
 // Warp w takes the chunk's tiles w, w + 4, ... through its own ring of
 // kStagesPerWarp stages and keeps its own online softmax; the four warps'
 // states meet in shared memory at the end.
-template <int D>
+// CLUSTER: the chunks of a (sequence, head group) are one thread-block
+// cluster (grid.x = chunks <= kMaxClusterChunks); each CTA leaves its merged
+// state in its own shared memory and the cluster's CTAs merge the chunks over
+// distributed shared memory, so no partials go to global memory and no merge
+// kernel follows.
+template <int D, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1) gqa_decode_split_kernel(const DecodeParams p) {
     using T = DecodeTile<D>;
     constexpr int TP = T::kPos;
@@ -373,7 +402,15 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_split_kernel(const Dec
                 L = fmaf(cw[kHeadsPerCta * D + kHeadsPerCta + row], wt, L);
             }
         }
-        if (p.chunks == 1) {
+        if constexpr (CLUSTER) {
+            // this chunk's state, in warp 0's ring past its O/max/sum area
+            float* cr = reinterpret_cast<float*>(smem + kClusterStateOffset);
+            cr[row * D + d] = acc;
+            if (d == 0) {
+                cr[kHeadsPerCta * D + row] = M;
+                cr[kHeadsPerCta * D + kHeadsPerCta + row] = L;
+            }
+        } else if (p.chunks == 1) {
             p.out[(qh0 + row) * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
         } else {
             p.part_o[((qh0 + row) * p.chunks + chunk) * D + d] = acc;
@@ -382,6 +419,50 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_split_kernel(const Dec
                 p.part_ml[((qh0 + row) * p.chunks + chunk) * 2 + 1] = L;
             }
         }
+    }
+    if constexpr (CLUSTER) {
+        cluster_sync();  // every chunk's state is in its CTA's shared memory
+        // Each CTA merges a share of the elements: the chunks' weights per
+        // row first (into this CTA's warp-1 ring), then the outputs.
+        const std::uint32_t rank = cluster_rank();
+        const std::uint32_t cr = smem_u32(smem + kClusterStateOffset);
+        float* wts = reinterpret_cast<float*>(smem + kStagesPerWarp * kStageBytes);
+        constexpr int WS = kMaxClusterChunks + 1;  // weights of a row, then its sum
+        if (threadIdx.x < nh) {
+            const std::uint32_t row = threadIdx.x;
+            float mc[kMaxClusterChunks];
+            float Mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kMaxClusterChunks; ++c) {
+                mc[c] = static_cast<std::uint32_t>(c) < p.chunks
+                            ? ld_dsmem_f32(cr + (kHeadsPerCta * D + row) * 4, c)
+                            : -INFINITY;
+                Mx = fmaxf(Mx, mc[c]);
+            }
+            float L = 0.f;
+#pragma unroll
+            for (int c = 0; c < kMaxClusterChunks; ++c) {
+                float w = 0.f;
+                if (Mx != -INFINITY && mc[c] != -INFINITY) {
+                    w = ex2(mc[c] - Mx);
+                    L = fmaf(ld_dsmem_f32(cr + (kHeadsPerCta * D + kHeadsPerCta + row) * 4, c), w, L);
+                }
+                wts[row * WS + c] = w;
+            }
+            wts[row * WS + kMaxClusterChunks] = L;
+        }
+        __syncthreads();
+        for (std::uint32_t i = rank * kThreads + threadIdx.x; i < nh * D; i += p.chunks * kThreads) {
+            const std::uint32_t row = i / D, d = i - row * D;
+            float acc = 0.f;
+#pragma unroll
+            for (int c = 0; c < kMaxClusterChunks; ++c)
+                if (static_cast<std::uint32_t>(c) < p.chunks)
+                    acc = fmaf(ld_dsmem_f32(cr + (row * D + d) * 4, c), wts[row * WS + c], acc);
+            const float L = wts[row * WS + kMaxClusterChunks];
+            p.out[(qh0 + row) * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
+        }
+        cluster_sync();  // a CTA's shared memory stays until the others have read it
     }
     pdl_launch_dependents();
 }
@@ -409,15 +490,20 @@ __global__ void __launch_bounds__(D) gqa_decode_merge_kernel(const DecodeParams 
 
 // Chunks per sequence.  The split kernel holds one CTA per SM (192 KB of
 // rings); a chunk is a whole number of tiles, dealt to the four warps.
-// Cost model: waves of CTAs x (tiles per warp + 2 tiles of fixed latency);
-// the fewest chunks that reach the minimum.
+// Cost model: waves of CTAs x (tiles per warp + 2 tiles of fixed latency),
+// plus kMergePenalty when the chunks need the merge kernel (more chunks
+// than a cluster holds); the fewest chunks that reach the minimum.  cluster:
+// the chunks (2 .. kMaxClusterChunks) merge inside a thread-block cluster.
+constexpr std::uint64_t kMergePenalty = 2;
+
 inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64_t head_groups,
                         std::uint64_t head_dim, std::uint64_t max_len, std::uint32_t& chunks,
-                        std::uint32_t& chunk_len) {
+                        std::uint32_t& chunk_len, bool& cluster) {
     const std::uint64_t tp = 4096 / head_dim;  // positions per tile
     const std::uint64_t tiles = (max_len + tp - 1) / tp;
     chunks = 1;
     chunk_len = static_cast<std::uint32_t>(tp * (tiles > 0 ? tiles : 1));
+    cluster = false;
     if (tiles == 0) return;
     const std::uint64_t units = batch * kv_heads * head_groups;
     std::uint64_t best = ~0ull;
@@ -425,13 +511,67 @@ inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64
         const std::uint64_t tpc = (tiles + c - 1) / c;
         if ((tiles + tpc - 1) / tpc != c) continue;  // same split as a smaller c
         const std::uint64_t waves = (units * c + 147) / 148;
-        const std::uint64_t cost = waves * ((tpc + kWarpsPerCta - 1) / kWarpsPerCta + 2);
+        const std::uint64_t cost = waves * ((tpc + kWarpsPerCta - 1) / kWarpsPerCta + 2) +
+                                   (c > static_cast<std::uint64_t>(kMaxClusterChunks) ? kMergePenalty : 0);
         if (cost < best) {
             best = cost;
             chunks = static_cast<std::uint32_t>(c);
             chunk_len = static_cast<std::uint32_t>(tpc * tp);
         }
     }
+    cluster = chunks > 1 && chunks <= static_cast<std::uint32_t>(kMaxClusterChunks);
+}
+
+inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64_t head_groups,
+                        std::uint64_t head_dim, std::uint64_t max_len, std::uint32_t& chunks,
+                        std::uint32_t& chunk_len) {
+    bool cluster;
+    decode_plan(batch, kv_heads, head_groups, head_dim, max_len, chunks, chunk_len, cluster);
+}
+
+// Launches the split kernel with the chunks of each (sequence, head group)
+// as one cluster, once the device has been seen to fit such a cluster
+// (cudaOccupancyMaxActiveClusters, remembered per device and size).  Returns
+// false, launching nothing, when it does not.
+template <int D>
+inline bool launch_decode_cluster(const DecodeParams& p, dim3 grid, cudaStream_t s, int& st) {
+    auto kernel = gqa_decode_split_kernel<D, true>;
+    static std::atomic<std::uint64_t> smem_done{0};
+    static std::atomic<std::uint64_t> fits[kMaxClusterChunks + 1];  // bit dev: 1 = fits
+    static std::atomic<std::uint64_t> seen[kMaxClusterChunks + 1];  // bit dev: checked
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    const std::uint64_t bit = 1ull << dev;
+    const std::uint32_t n = p.chunks;
+    st = ensure_dynamic_smem(kernel, kSplitSmem, smem_done);
+    if (st != kSuccess) return true;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSplitSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = n;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    if (!(seen[n].load(std::memory_order_acquire) & bit)) {
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            clusters = 0;
+        }
+        if (clusters > 0) fits[n].fetch_or(bit, std::memory_order_acq_rel);
+        seen[n].fetch_or(bit, std::memory_order_acq_rel);
+    }
+    if (!(fits[n].load(std::memory_order_acquire) & bit)) return false;
+    cfg.numAttrs = 2;
+    st = static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, p));
+    return true;
 }
 
 }  // namespace attn
@@ -532,7 +672,9 @@ extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_c
     p.head_groups = static_cast<std::uint32_t>(head_groups);
     p.scale_log2 = scale * 1.4426950408889634f;
     p.max_len = max_len;
-    attn::decode_plan(batch, kv_heads, head_groups, head_dim, max_len, p.chunks, p.chunk_len);
+    bool cluster = false;
+    attn::decode_plan(batch, kv_heads, head_groups, head_dim, max_len, p.chunks, p.chunk_len,
+                      cluster);
     if (p.chunks > 1) {
         const std::uint64_t need = batch * q_heads * p.chunks * (head_dim + 2) * 4;
         if (workspace == nullptr || workspace_bytes < need ||
@@ -544,24 +686,25 @@ extern "C" int mote_cuda_gqa_attention_decode_f16(const void* q, const void* k_c
     const dim3 grid(p.chunks, static_cast<unsigned>(kv_heads * head_groups),
                     static_cast<unsigned>(batch));
     const auto s = static_cast<cudaStream_t>(stream);
-    int st;
+    int st = kSuccess;
+    if (cluster && (head_dim == 64 ? attn::launch_decode_cluster<64>(p, grid, s, st)
+                                   : attn::launch_decode_cluster<128>(p, grid, s, st)))
+        return st;
     if (head_dim == 64) {
-        constexpr int smem = attn::kSplitSmem;
         static std::atomic<std::uint64_t> done{0};
-        st = ensure_dynamic_smem(attn::gqa_decode_split_kernel<64>, smem, done);
+        st = ensure_dynamic_smem(attn::gqa_decode_split_kernel<64, false>, attn::kSplitSmem, done);
         if (st == kSuccess)
-            st = launch_pdl_smem(attn::gqa_decode_split_kernel<64>, grid, dim3(attn::kThreads), smem,
-                                 s, p);
+            st = launch_pdl_smem(attn::gqa_decode_split_kernel<64, false>, grid, dim3(attn::kThreads),
+                                 attn::kSplitSmem, s, p);
         if (st == kSuccess && p.chunks > 1)
             st = launch_pdl(attn::gqa_decode_merge_kernel<64>,
                             dim3(static_cast<unsigned>(batch * q_heads)), dim3(64), s, p);
     } else {
-        constexpr int smem = attn::kSplitSmem;
         static std::atomic<std::uint64_t> done{0};
-        st = ensure_dynamic_smem(attn::gqa_decode_split_kernel<128>, smem, done);
+        st = ensure_dynamic_smem(attn::gqa_decode_split_kernel<128, false>, attn::kSplitSmem, done);
         if (st == kSuccess)
-            st = launch_pdl_smem(attn::gqa_decode_split_kernel<128>, grid, dim3(attn::kThreads),
-                                 smem, s, p);
+            st = launch_pdl_smem(attn::gqa_decode_split_kernel<128, false>, grid, dim3(attn::kThreads),
+                                 attn::kSplitSmem, s, p);
         if (st == kSuccess && p.chunks > 1)
             st = launch_pdl(attn::gqa_decode_merge_kernel<128>,
                             dim3(static_cast<unsigned>(batch * q_heads)), dim3(128), s, p);

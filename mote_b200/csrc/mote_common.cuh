@@ -70,6 +70,19 @@ __device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t 
     return ok != 0;
 }
 
+// Non-blocking: whether the phase with the given parity has completed.
+__device__ __forceinline__ bool mbar_test_wait(std::uint64_t* bar, std::uint32_t parity) {
+    std::uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false (and
 // records kDevWaitTimeout in *status) if it has not completed within
 // kWaitCycles.

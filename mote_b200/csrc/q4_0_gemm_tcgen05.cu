@@ -15,7 +15,8 @@
 // operand (N = 256), so every weight converted to f16 feeds 256 tokens:
 // * warp 16 (producer) streams activation tiles (64 k x 256 tokens, TMA
 //   with 128-byte swizzle) and raw Q4_0 row slices (128 rows x 144 bytes = 8
-//   blocks per row, TMA 2-D tile of bytes) into shared memory;
+//   blocks per row, TMA 2-D tile of bytes) into shared memory, each as soon
+//   as a stage of its own ring is free;
 // * warps 0-15 (converters, two groups of 8 taking alternate 64-k slices)
 //   dequantize each slice of the raw rows into f16 (q - 8) * d -- correctly
 //   rounded, exactly what a dense f16 weight would hold -- written straight
@@ -50,12 +51,9 @@ constexpr int kBK = 64;                  // k per operand stage (one 128-B f16 s
 constexpr int kSuperK = 256;             // k per raw weight stage (8 blocks, 144 B per row)
 // Four operand stages (4 x 48 KB at TT = 256) keep three 64-k slices of
 // MMA work queued behind the one in flight, enough to cover the TMA
-// latency of the activation tiles; one raw stage (256 k) is refilled while
-// the converted stages ahead of it drain.  Three operand stages with two
-// raw stages ran at 931 TFLOP/s, four with one at 1008 (M=2048, K=4096,
-// N=14336, 8 converter warps).
+// latency of the activation tiles.  Three operand stages ran at 931
+// TFLOP/s, four at 1008 (M=2048, K=4096, N=14336, 8 converter warps).
 constexpr int kStages = 4;               // operand stages
-constexpr int kRawStages = 1;            // raw weight stages
 // Raw weight rows of a 256-k stage: 8 Q4_0 blocks (144 bytes) or 8 Q8_0
 // blocks (272 bytes; its TMA box counts 2-byte elements, a box edge being
 // at most 256 elements).
@@ -82,6 +80,18 @@ constexpr int kProducerWarp = kConvWarps;
 constexpr int kMmaWarp = kConvWarps + 1;
 constexpr int kThreads = (kConvWarps + 2) * 32;
 
+// Raw weight stages (256 k each) of a CTA: as many as fit, up to four, in
+// the shared memory that keeps the kernel's CTAs per SM (two for TT <= 128,
+// one at 256 tokens).  The producer refills a raw stage as soon as the
+// converters free it, independently of the activation stages, so the weight
+// stream runs that many stages ahead: at 64 tokens a raw stage is converted
+// faster than its DRAM latency.
+constexpr int raw_stages(int tt, int raw_bytes) {
+    const int budget = tt <= 128 ? 115712 : 232448;  // per-CTA shared memory
+    const int r = (budget - kStages * tt * kBK * 2 - 2048) / raw_bytes;
+    return r < 1 ? 1 : r > 4 ? 4 : r;
+}
+
 // The converted weights (the MMA's A operand) live in tensor memory, next
 // to the accumulator: the converters write them with tcgen05.st (a warp
 // reaches exactly the 32 TMEM lanes = weight rows it converts) and the MMA
@@ -106,12 +116,14 @@ struct Layout {
     static constexpr int kAColBase = TT;
     static constexpr int kTmemCols = pow2_at_least(TT + kStages * 32);
     static_assert(kTmemCols <= 512, "tensor memory");
+    static constexpr int kRawStages = raw_stages(TT, kRawBytes<WF>);
     static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes<WF>;
     // barriers: x_full[S], w_full[S], empty[S], raw_full[R], raw_empty[R], accum
     static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + slack for 1024-B alignment
+    static_assert(kSmemBytes <= (TT <= 128 ? 115712 : 232448), "CTAs per SM");
     // Instruction descriptor, kind::f16: F32 accumulate, A = B = F16, both
     // K-major, N >> 3 at bit 17, M >> 4 at bit 24.
     static constexpr std::uint32_t kIdesc = (1u << 4) | (static_cast<std::uint32_t>(TT >> 3) << 17) |
@@ -543,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     std::uint64_t* w_full = bars + kStages;
     std::uint64_t* empty = bars + 2 * kStages;
     std::uint64_t* raw_full = bars + 3 * kStages;
+    constexpr int kRawStages = L::kRawStages;
     std::uint64_t* raw_empty = raw_full + kRawStages;
     std::uint64_t* accum = raw_empty + kRawStages;
     volatile std::uint32_t* tmem_slot = reinterpret_cast<volatile std::uint32_t*>(smem + kOffTmemSlot);
@@ -582,17 +595,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            for (std::uint32_t kb = 0; kb < num_kb; ++kb) {
-                const int s = kb % kStages;
-                if (kb >= kStages &&
-                    !wait_or_abort(&empty[s], ((kb / kStages) - 1) & 1u, abort_flag))
-                    break;
-                if (kb % (kSuperK / kBK) == 0) {
-                    const std::uint32_t sb = kb / (kSuperK / kBK);
+            // One thread feeds both rings: each pass issues the next raw
+            // stage and the next activation stage whose slots are free
+            // (non-blocking tests); no progress for kWaitCycles aborts.
+            const std::uint32_t nsb = num_kb / (kSuperK / kBK);
+            std::uint32_t kb = 0, sb = 0;
+            long long idle_since = clock64();
+            while (kb < num_kb || sb < nsb) {
+                bool progress = false;
+                if (sb < nsb && (sb < kRawStages ||
+                                 mbar_test_wait(&raw_empty[sb % kRawStages],
+                                                ((sb / kRawStages) - 1) & 1u))) {
                     const int r = sb % kRawStages;
-                    if (sb >= kRawStages &&
-                        !wait_or_abort(&raw_empty[r], ((sb / kRawStages) - 1) & 1u, abort_flag))
-                        break;
                     mbar_arrive_expect_tx(&raw_full[r], kRaw);
                     // x in the map's elements: bytes (Q4_0, Q4_K) or 2-byte
                     // units (Q8_0; Q6_K from the window's aligned start)
@@ -602,11 +616,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                   : static_cast<int>(u * kRawRow);
                     tma_load_2d(base + kOffRaw + r * kRaw, &map_w, rx, static_cast<int>(n0),
                                 smem_u32(&raw_full[r]));
+                    ++sb;
+                    progress = true;
                 }
-                mbar_arrive_expect_tx(&x_full[s], kXBytes);
-                tma_load_2d(base + kOffX + s * kXBytes, &map_x,
-                            static_cast<int>((kb0 + kb) * kBK), static_cast<int>(m0),
-                            smem_u32(&x_full[s]));
+                if (kb < num_kb &&
+                    (kb < kStages ||
+                     mbar_test_wait(&empty[kb % kStages], ((kb / kStages) - 1) & 1u))) {
+                    const int s = kb % kStages;
+                    mbar_arrive_expect_tx(&x_full[s], kXBytes);
+                    tma_load_2d(base + kOffX + s * kXBytes, &map_x,
+                                static_cast<int>((kb0 + kb) * kBK), static_cast<int>(m0),
+                                smem_u32(&x_full[s]));
+                    ++kb;
+                    progress = true;
+                }
+                if (progress) {
+                    idle_since = clock64();
+                } else {
+                    if (*abort_flag) break;
+                    if (clock64() - idle_since > kWaitCycles) {
+                        *abort_flag = 1u;
+                        atomicOr(&g_device_status, kDevWaitTimeout);
+                        break;
+                    }
+                }
             }
         }
         __syncwarp();  // reconverge before the block-wide barrier below

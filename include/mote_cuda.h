@@ -82,6 +82,9 @@ int mote_cuda_event_create(void** event);
 int mote_cuda_event_destroy(void* event);
 int mote_cuda_event_record(void* event, void* stream);
 int mote_cuda_event_elapsed_ms(float* ms, void* start, void* end);
+/* `stream` waits on the device for the work recorded in `event`
+ * (cudaStreamWaitEvent); null handles -> 1. */
+int mote_cuda_stream_wait_event(void* stream, void* event);
 /* Reads (clear != 0: and clears) the current device's status word.  Bit 0:
  * a bounded device-side wait expired; bit 1: an index was out of range. */
 int mote_cuda_device_status(unsigned* status, int clear);

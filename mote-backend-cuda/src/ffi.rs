@@ -57,6 +57,7 @@ unsafe extern "C" {
     pub fn mote_cuda_event_destroy(event: *mut c_void) -> i32;
     pub fn mote_cuda_event_record(event: *mut c_void, stream: *mut c_void) -> i32;
     pub fn mote_cuda_event_elapsed_ms(ms: *mut f32, start: *mut c_void, end: *mut c_void) -> i32;
+    pub fn mote_cuda_stream_wait_event(stream: *mut c_void, event: *mut c_void) -> i32;
     pub fn mote_cuda_device_status(status: *mut u32, clear: i32) -> i32;
     pub fn mote_cuda_status_string(status: i32) -> *const c_char;
     pub fn mote_cuda_abi_version() -> i32;

@@ -43,6 +43,7 @@ SIGNATURES: dict[str, tuple] = {
     "mote_cuda_event_destroy": (I, [P]),
     "mote_cuda_event_record": (I, [P, P]),
     "mote_cuda_event_elapsed_ms": (I, [ctypes.POINTER(F), P, P]),
+    "mote_cuda_stream_wait_event": (I, [P, P]),
     "mote_cuda_device_status": (I, [ctypes.POINTER(ctypes.c_uint), I]),
     "mote_cuda_status_string": (ctypes.c_char_p, [I]),
     "mote_cuda_abi_version": (I, []),

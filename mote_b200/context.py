@@ -46,12 +46,32 @@ class _ContextInner:
         errors.check(lib().mote_cuda_set_device(ordinal), "select device")
         errors.check(lib().mote_cuda_stream_create(ctypes.byref(stream)), "create stream")
         self.stream = stream.value
+        self.copy_stream = None  # created by the first overlapped download
+        self.copy_event = None
         self._lock = threading.Lock()
 
     def select(self) -> None:
         errors.check(lib().mote_cuda_set_device(self.ordinal), "select device")
 
+    def copy_channel(self) -> tuple[int, int]:
+        """The copy stream and the event that orders it after the compute
+        stream, created on first use."""
+        if self.copy_stream is None:
+            self.select()
+            stream, event = ctypes.c_void_p(), ctypes.c_void_p()
+            errors.check(lib().mote_cuda_stream_create(ctypes.byref(stream)),
+                         "create copy stream")
+            errors.check(lib().mote_cuda_event_create(ctypes.byref(event)), "create event")
+            self.copy_stream, self.copy_event = stream.value, event.value
+        return self.copy_stream, self.copy_event
+
     def close(self) -> None:
+        if self.copy_stream:
+            lib().mote_cuda_set_device(self.ordinal)
+            lib().mote_cuda_stream_synchronize(self.copy_stream)
+            lib().mote_cuda_event_destroy(self.copy_event)
+            lib().mote_cuda_stream_destroy(self.copy_stream)
+            self.copy_stream = self.copy_event = None
         if self.stream:
             lib().mote_cuda_set_device(self.ordinal)
             lib().mote_cuda_stream_synchronize(self.stream)
@@ -275,8 +295,13 @@ class CudaContext:
                                                                           np.uint8)
 
     def sync(self) -> None:
+        """Waits for the compute stream and, if overlapped downloads were
+        issued, the copy stream."""
         self.inner.select()
         errors.check(lib().mote_cuda_stream_synchronize(self.stream), "synchronize stream")
+        if self.inner.copy_stream is not None:
+            errors.check(lib().mote_cuda_stream_synchronize(self.inner.copy_stream),
+                         "synchronize copy stream")
 
     def memory_info(self) -> MemoryInfo:
         self.inner.select()
@@ -303,6 +328,19 @@ class CudaContext:
         n = tensor.desc.required_span_bytes if nbytes is None else nbytes
         errors.check(lib().mote_cuda_memcpy_device_to_host_async(
             host.pointer, tensor.pointer, n, self.stream), "download (async)")
+
+    def download_overlapped(self, host: "PinnedBuffer", tensor: Tensor,
+                            nbytes: int | None = None):
+        """Device-to-host copy on the context's copy stream, ordered after
+        everything issued so far on the compute stream, so the kernels issued
+        after it run while it copies.  ``tensor`` must not be written again,
+        nor ``host`` read, before ``sync()`` (which waits for both streams)."""
+        n = tensor.desc.required_span_bytes if nbytes is None else nbytes
+        copy_stream, event = self.inner.copy_channel()
+        errors.check(lib().mote_cuda_event_record(event, self.stream), "record event")
+        errors.check(lib().mote_cuda_stream_wait_event(copy_stream, event), "order copy stream")
+        errors.check(lib().mote_cuda_memcpy_device_to_host_async(
+            host.pointer, tensor.pointer, n, copy_stream), "download (overlapped)")
 
     # -- ownership check used by every op (context.rs:150-176) --------------
     def storage(self, tensor: Tensor) -> CudaStorage:

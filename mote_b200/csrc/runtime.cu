@@ -103,6 +103,14 @@ extern "C" int mote_cuda_event_record(void* event, void* stream) {
         cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)));
 }
 
+// `stream` waits (on the device) for the work recorded in `event`: the
+// ordering between a context's compute stream and its copy stream.
+extern "C" int mote_cuda_stream_wait_event(void* stream, void* event) {
+    if (stream == nullptr || event == nullptr) return mote::kInvalidValue;
+    return static_cast<int>(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream),
+                                                static_cast<cudaEvent_t>(event), 0));
+}
+
 extern "C" int mote_cuda_event_elapsed_ms(float* ms, void* start, void* end) {
     if (ms == nullptr) return mote::kInvalidValue;
     return static_cast<int>(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start),

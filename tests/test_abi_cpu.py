@@ -198,6 +198,11 @@ def test_decoder_stack_argument_rules(lib):
                  STREAM) == 1
 
 
+def test_stream_wait_event_rejects_null_handles(lib):
+    assert lib.mote_cuda_stream_wait_event(None, FAKE) == 1
+    assert lib.mote_cuda_stream_wait_event(STREAM, None) == 1
+
+
 def test_status_strings(lib):
     assert b"invalid" in lib.mote_cuda_status_string(-1).lower()
     assert lib.mote_cuda_status_string(1)

@@ -343,3 +343,34 @@ def test_split_k_workspace_path(ctx, oracle_lib, m, n, k):
         ok, bad = checker.within_reference_tolerance(got, checker.f16_round(want), 0.01, 0.002)
         assert ok, bad
         assert checker.rel_err_elementwise(got, ref64) <= F16_BOUND
+
+
+def test_overlapped_downloads_match_the_outputs(ctx, oracle_lib):
+    """Host-buffer pipeline of the end-to-end bench: activations uploaded
+    from pinned memory, linears on the compute stream, each output copied
+    back on the context's copy stream right after its linear (the later
+    linears run meanwhile); after sync() every host buffer holds exactly the
+    device output, on every one of several back-to-back steps."""
+    from mote_b200.context import PinnedBuffer
+
+    rng = np.random.default_rng(91)
+    k = 4096
+    shapes = [(1, 4096), (4, 11008), (16, 2048)]
+    ws = {n: ctx.from_bytes(quantized((n, k)), fx.q4_0_weights(oracle_lib, n, k, seed=300 + n))
+          for _, n in shapes}
+    xs = {m: ctx.empty(plain((m, k), DType.F16)) for m, _ in shapes}
+    ys = {(m, n): ctx.empty(plain((m, n), DType.F16)) for m, n in shapes}
+    hx = {m: PinnedBuffer(m * k * 2) for m, _ in shapes}
+    hy = {(m, n): PinnedBuffer(m * n * 2) for m, n in shapes}
+    for step in range(3):
+        for m, _ in shapes:
+            hx[m].view(np.float16)[:] = rng.normal(0, 1, m * k).astype(np.float16)
+            ctx.upload_async(xs[m], hx[m])
+        for m, n in shapes:
+            ops.quantized_linear_q4_0_f16(ctx, xs[m], ws[n], ys[(m, n)])
+            ctx.download_overlapped(hy[(m, n)], ys[(m, n)])
+        ctx.sync()
+        for m, n in shapes:
+            want = np.frombuffer(ctx.read_bytes(ys[(m, n)]), np.uint16)
+            got = hy[(m, n)].view(np.uint16)
+            assert np.array_equal(got, want), (step, m, n)

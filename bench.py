@@ -270,17 +270,24 @@ class Bench:
 
     # -- public-API end-to-end leg ------------------------------------------------
     def e2e(self, steps: int) -> dict:
-        """Config-3 sweep through mote_b200.ops with host buffers: every step
-        copies the five activation matrices from pinned host memory, runs the
-        15 linears and copies each of the 15 outputs back (on the context's
-        copy stream, overlapping the later linears), then synchronizes."""
+        """Config-3 sweep with host buffers through the C ABI the reference's
+        Rust crate binds (include/mote_cuda.h, called here through ctypes
+        with the arguments prepared once, as a Rust caller holds them).  The
+        five activation matrices sit in one pinned host buffer and one device
+        arena, the 15 outputs likewise (16-byte aligned offsets, as the ABI
+        requires).  Every step copies the activations up in one copy, runs
+        the 15 linears back to back (the workspace entry, as mote_b200.ops
+        calls it), copies the outputs down in one copy and synchronizes.
+        (Copying each token count's outputs on a second stream while the
+        next linears run measured slower: the event between two linears
+        breaks their programmatic dependent launch.)"""
         import numpy as np
 
-        from mote_b200 import ops
         from mote_b200.context import CudaContext, PinnedBuffer
         from mote_b200.types import DType, plain, quantized
 
         ctx = CudaContext(self.local_rank)
+        lib = self.lib
         k = SWEEP_K
         # each step takes the next of R_N copies of every weight matrix (the
         # copies of one N hold >= 2.5x L2), so every step streams from HBM
@@ -291,30 +298,45 @@ class Bench:
                 wt = ctx.empty(quantized((n, k)))
                 self.encode_into(wt.pointer, n, k, seed=1000 + n)
                 weights[n].append(wt)
-        xs = {m: ctx.empty(plain((m, k), DType.F16)) for m in SWEEP_M}
-        ys = {(m, n): ctx.empty(plain((m, n), DType.F16)) for m in SWEEP_M for n in SWEEP_N}
-        hx = {m: PinnedBuffer(m * k * 2) for m in SWEEP_M}
-        hy = {(m, n): PinnedBuffer(m * n * 2) for m in SWEEP_M for n in SWEEP_N}
-        rng = np.random.default_rng(5)
+        x_off, off = {}, 0
         for m in SWEEP_M:
-            hx[m].view(np.float16)[:] = rng.normal(0, 1, m * k).astype(np.float16)
-        h2d = sum(m * k * 2 for m in SWEEP_M)
-        d2h = sum(m * n * 2 for m in SWEEP_M for n in SWEEP_N)
+            x_off[m] = off
+            off += m * k * 2
+        h2d = off
+        y_off, off = {}, 0
+        for m in SWEEP_M:
+            for n in SWEEP_N:
+                y_off[(m, n)] = off
+                off += m * n * 2
+        d2h = off
+        assert all(v % 16 == 0 for v in list(x_off.values()) + list(y_off.values()))
+        x_dev = ctx.empty(plain((h2d // 2,), DType.F16))
+        y_dev = ctx.empty(plain((d2h // 2,), DType.F16))
+        hx, hy = PinnedBuffer(h2d), PinnedBuffer(d2h)
+        hx.view(np.float16)[:] = np.random.default_rng(5).normal(0, 1, h2d // 2).astype(np.float16)
         alg = sum(linear_bytes(m, n, k) for m in SWEEP_M for n in SWEEP_N)
+        need = max(ctx.linear_workspace_bytes(m, n, k) for m in SWEEP_M for n in SWEEP_N)
+        ws_ptr, ws_bytes = ctx.linear_workspace(need)
+        stream = ctx.stream
+        groups = [(m, [(x_dev.pointer + x_off[m], [w.pointer for w in weights[n]],
+                        y_dev.pointer + y_off[(m, n)], n) for n in SWEEP_N])
+                  for m in SWEEP_M]
+        upload = lib.mote_cuda_memcpy_host_to_device_async
+        linear = lib.mote_cuda_quantized_linear_q4_0_f16_ws
+        download = lib.mote_cuda_memcpy_device_to_host_async
+        sync = lib.mote_cuda_stream_synchronize
 
         def step(i):
-            # a step's inputs up, its 15 linears, each output down on the
-            # copy stream as soon as it is computed (the later linears run
-            # meanwhile), one sync of both streams
-            for m in SWEEP_M:
-                ctx.upload_async(xs[m], hx[m])
-            for m in SWEEP_M:
-                for n in SWEEP_N:
-                    ops.quantized_linear_q4_0_f16(ctx, xs[m], weights[n][i % len(weights[n])],
-                                                  ys[(m, n)])
-                    ctx.download_overlapped(hy[(m, n)], ys[(m, n)])
-            ctx.sync()
+            st = upload(x_dev.pointer, hx.pointer, h2d, stream)
+            for m, lins in groups:
+                for xp, wps, yp, n in lins:
+                    st |= linear(xp, wps[i % len(wps)], yp, m, n, k, ws_ptr, ws_bytes, stream)
+            st |= download(hy.pointer, y_dev.pointer, d2h, stream)
+            st |= sync(stream)
+            if st:
+                raise RuntimeError(f"e2e step: CUDA status {st}")
 
+        ctx.inner.select()
         for i in range(3):
             step(i)
         t0 = time.perf_counter()
@@ -326,10 +348,11 @@ class Bench:
         return {"value": round(alg * steps * self.world / dt / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(dt * 1e3 / steps, 4),
-                "path": "mote_b200.ops.quantized_linear_q4_0_f16 (C ABI); per step: the "
-                        "activations H2D from pinned host memory, the 15 linears, each output "
-                        "D2H on the context's copy stream after its linear, one sync of both "
-                        "streams; weights rotated over copies holding >= 2.5x L2 per N"}
+                "path": "C ABI (include/mote_cuda.h: mote_cuda_quantized_linear_q4_0_f16_ws, "
+                        "the async copies) through ctypes; per step: the activations H2D from "
+                        "pinned host memory in one copy, the 15 linears back to back, the "
+                        "outputs D2H in one copy, one stream sync; weights rotated over copies "
+                        "holding >= 2.5x L2 per N"}
 
     # -- extra configs ----------------------------------------------------------
     def config1(self) -> dict:

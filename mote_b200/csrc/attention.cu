@@ -20,30 +20,36 @@
 //   V byte of the sequence is read once.  Flash-decoding on the tensor
 //   cores: a CTA takes one (sequence, KV head, group of up to 16 query
 //   heads, chunk of positions); its query heads are the 16 rows of
-//   mma.sync.m16n8k16 (f16 in, f32 accumulate).  Each of its four warps
-//   streams tiles of 4096 / head_dim positions through a private
+//   mma.sync.m16n8k16 (f16 in, f32 accumulate).  Each of its eight warps
+//   streams tiles of 2048 / head_dim positions through a private
 //   three-stage cp.async ring (K and V rows swizzled for conflict-free
 //   ldmatrix) and computes S = Q K^T, an online softmax on the S
 //   accumulators (exp2 with the scale folded in), and O += P V with the S
 //   accumulators reused as the A operand.  P is split into f16 hi + lo
 //   parts (two MMAs), so the probabilities keep ~22 bits.  The warps'
-//   states meet in shared memory; the CTA writes its output, or with
-//   several chunks per sequence its unnormalised partial output with its
-//   max and sum, and a second kernel merges the chunks.
+//   states meet in shared memory; the CTA writes its output, or the chunks
+//   of a sequence merge inside a thread-block cluster (up to 8), or write
+//   unnormalised partials with their max and sum for a merge kernel.
 #include "mote_common.cuh"
 
 namespace mote {
 namespace attn {
 
-constexpr int kThreads = 128;        // decode split kernel: four warps
-constexpr int kWarpsPerCta = 4;
-constexpr int kStageBytes = 16384;   // K and V of one tile
-constexpr int kStagesPerWarp = 3;    // 48 KB ring per warp, 192 KB per CTA
+// Decode split kernel: eight warps, each with a three-stage ring of 8 KB
+// tiles (K and V of 2048 / head_dim positions), 192 KB per CTA.  Four warps
+// with 16 KB tiles measured 7-10 % slower (one warp per scheduler left the
+// MMA and ldmatrix latencies exposed).
+constexpr int kWarpsPerCta = 8;
+constexpr int kThreads = 32 * kWarpsPerCta;
+constexpr int kStageBytes = 8192;    // K and V of one tile
+constexpr int kStagesPerWarp = 3;
 constexpr int kHeadsPerCta = 16;     // query heads per CTA (the MMA rows)
 constexpr int kSplitSmem = kWarpsPerCta * kStagesPerWarp * kStageBytes;
 // Cluster path: a CTA's merged state (O [16][D] f32, max [16], sum [16]) at
-// 24 KB into warp 0's ring, after that warp's own state (at most 8.1 KB).
-constexpr int kClusterStateOffset = 24 * 1024;
+// 12 KB into warp 0's ring, after that warp's own state (at most 8.2 KB).
+constexpr int kClusterStateOffset = 12 * 1024;
+static_assert(kClusterStateOffset + (16 * 128 + 32) * 4 <= kStagesPerWarp * kStageBytes,
+              "the cluster state fits in warp 0's ring");
 // At most 8 chunks to a cluster (the portable size): 16-CTA clusters of
 // full-SM CTAs measured slower (fewer of them fit on the GPCs at a time).
 constexpr int kMaxClusterChunks = 8;
@@ -130,10 +136,10 @@ __device__ __forceinline__ float ex2(float x) {
 // in eight different 16-byte bank groups.
 template <int D>
 struct DecodeTile {
-    static constexpr int kPos = 4096 / D;              // 64 (D = 64) or 32 (D = 128)
+    static constexpr int kPos = kStageBytes / (4 * D);  // D = 64: 32, D = 128: 16
     static constexpr int kCpr = D / 8;                 // 16-byte chunks per row
-    static constexpr int kHalfBytes = kPos * D * 2;    // 8 KB: the K (or V) rows
-    static constexpr int kChunksPerLane = kHalfBytes / 16 / 32;  // 16
+    static constexpr int kHalfBytes = kPos * D * 2;    // the K (or V) rows
+    static constexpr int kChunksPerLane = kHalfBytes / 16 / 32;
     static constexpr int kRowStep = 32 / kCpr;         // rows between a lane's chunks
     static_assert(2 * kHalfBytes == kStageBytes, "a stage holds K and V of one tile");
     static_assert(kPos % 16 == 0, "whole k16 steps of positions");
@@ -175,8 +181,8 @@ __device__ __forceinline__ void split_pair(float a, float b, std::uint32_t& hi,
 
 // One CTA: sequence b = blockIdx.z, (KV head, head group) = blockIdx.y,
 // chunk = blockIdx.x.  The CTA's up to 16 query heads are the MMA rows.
-// Warp w takes the chunk's tiles w, w + 4, ... through its own ring of
-// kStagesPerWarp stages and keeps its own online softmax; the four warps'
+// Warp w takes the chunk's tiles w, w + 8, ... through its own ring of
+// kStagesPerWarp stages and keeps its own online softmax; the eight warps'
 // states meet in shared memory at the end.
 // CLUSTER: the chunks of a (sequence, head group) are one thread-block
 // cluster (grid.x = chunks <= kMaxClusterChunks); each CTA leaves its merged
@@ -489,17 +495,20 @@ __global__ void __launch_bounds__(D) gqa_decode_merge_kernel(const DecodeParams 
 }
 
 // Chunks per sequence.  The split kernel holds one CTA per SM (192 KB of
-// rings); a chunk is a whole number of tiles, dealt to the four warps.
-// Cost model: waves of CTAs x (tiles per warp + 2 tiles of fixed latency),
-// plus kMergePenalty when the chunks need the merge kernel (more chunks
-// than a cluster holds); the fewest chunks that reach the minimum.  cluster:
+// rings); a chunk is a whole number of tiles, dealt to the eight warps.
+// Cost model: waves of CTAs x (tiles per warp + kFixedTiles), plus
+// kMergePenalty when the chunks need the merge kernel (more chunks than a
+// cluster holds); the fewest chunks that reach the minimum.  cluster:
 // the chunks (2 .. kMaxClusterChunks) merge inside a thread-block cluster.
-constexpr std::uint64_t kMergePenalty = 2;
+// Fixed latency of a CTA and the merge kernel's cost, in tiles of the
+// warps' work: each about 32 KB of K and V per warp.
+constexpr std::uint64_t kFixedTiles = 32768 / kStageBytes;
+constexpr std::uint64_t kMergePenalty = 32768 / kStageBytes;
 
 inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64_t head_groups,
                         std::uint64_t head_dim, std::uint64_t max_len, std::uint32_t& chunks,
                         std::uint32_t& chunk_len, bool& cluster) {
-    const std::uint64_t tp = 4096 / head_dim;  // positions per tile
+    const std::uint64_t tp = kStageBytes / (4 * head_dim);  // positions per tile
     const std::uint64_t tiles = (max_len + tp - 1) / tp;
     chunks = 1;
     chunk_len = static_cast<std::uint32_t>(tp * (tiles > 0 ? tiles : 1));
@@ -511,8 +520,9 @@ inline void decode_plan(std::uint64_t batch, std::uint64_t kv_heads, std::uint64
         const std::uint64_t tpc = (tiles + c - 1) / c;
         if ((tiles + tpc - 1) / tpc != c) continue;  // same split as a smaller c
         const std::uint64_t waves = (units * c + 147) / 148;
-        const std::uint64_t cost = waves * ((tpc + kWarpsPerCta - 1) / kWarpsPerCta + 2) +
-                                   (c > static_cast<std::uint64_t>(kMaxClusterChunks) ? kMergePenalty : 0);
+        const std::uint64_t cost =
+            waves * ((tpc + kWarpsPerCta - 1) / kWarpsPerCta + kFixedTiles) +
+            (c > static_cast<std::uint64_t>(kMaxClusterChunks) ? kMergePenalty : 0);
         if (cost < best) {
             best = cost;
             chunks = static_cast<std::uint32_t>(c);

@@ -164,9 +164,9 @@ def test_attention_argument_rules(lib):
 def test_decode_attention_chunk_plan(lib):
     """The decode split's chunk count (host logic): one chunk when the
     sequences x KV heads already fill the SMs, else chunks of whole tiles
-    (4096 / head_dim positions) dealt four to a CTA, where more than 8 chunks
-    (a cluster's worth, merged in the split kernel) cost two tiles more for
-    the merge kernel; the workspace holds one f32 partial output plus max
+    (2048 / head_dim positions) dealt eight to a CTA, where more than 8
+    chunks (a cluster's worth, merged in the split kernel) cost four tiles
+    more for the merge kernel; the workspace holds one f32 partial output plus max
     and sum per (sequence, query head, chunk)."""
     def ws(batch, qh, kvh, hd, max_len):
         n = ctypes.c_uint64(123)
@@ -174,10 +174,10 @@ def test_decode_attention_chunk_plan(lib):
                                                                   ctypes.byref(n)) == 0
         return n.value
     assert ws(16, 32, 8, 64, 4096) == 0                  # 128 CTAs, one chunk each
-    assert ws(1, 32, 8, 64, 4096) == 32 * 8 * 66 * 4     # 8 chunks of 8 tiles (a cluster)
-    assert ws(1, 32, 8, 64, 1000) == 32 * 4 * 66 * 4     # 4 chunks of 4 tiles (a cluster)
-    assert ws(1, 32, 8, 64, 32768) == 32 * 16 * 66 * 4   # 16 chunks of 32 tiles, merged
-    assert ws(1, 64, 2, 128, 2000) == 64 * 8 * 130 * 4   # two head groups, 63 tiles of 32
+    assert ws(1, 32, 8, 64, 4096) == 32 * 8 * 66 * 4     # 8 chunks of 16 tiles (a cluster)
+    assert ws(1, 32, 8, 64, 1000) == 32 * 4 * 66 * 4     # 4 chunks of 8 tiles (a cluster)
+    assert ws(1, 32, 8, 64, 32768) == 32 * 16 * 66 * 4   # 16 chunks of 64 tiles, merged
+    assert ws(1, 64, 2, 128, 2000) == 64 * 8 * 130 * 4   # two head groups, 125 tiles of 16
     assert ws(4, 32, 8, 64, 0) == 0
     assert ws(1, 32, 8, 96, 64) == 0                     # rejected by the launch itself
 
